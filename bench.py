@@ -1,0 +1,479 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 layer-kernel hot path (one JSON line on rank 0).
+
+A step is one pass of the hot path of ``TransformerModel::forward`` over one
+batch (see glassboxai-transformer_b200/chain.py): embed, then per layer
+residual+LayerNorm, row softmax over every head of every sequence,
+residual+LayerNorm and bias+GELU, then the final LayerNorm of each
+sequence's last row.  Default workload: GPT-2 XL prefill, 32 sequences x 1024
+tokens per GPU, d 1600, ff 6400, 25 heads, 48 layers, bf16 GGUF tables.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+N > 1 runs one process per GPU under torch.distributed.run; each rank owns
+whole sequences (weak scaling: the per-GPU batch is fixed), no collective
+touches the data; the step time is the max over ranks.
+
+``--impl reference`` times the reference's loops on the host cores (the
+oracle's restatement, all cores) on a bounded sample of the same workload,
+and, when the reference build is present, also the reference's own CUDA
+kernels on one GPU; only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "layer-kernel HBM GB/s (% of B200 peak); tokens/s at GPT-2 XL shape, 1-8 GPU"
+
+# name -> (ChainShape kwargs, description, Chain kwargs)
+WORKLOADS = {
+    "gpt2-xl-prefill": (dict(batch=32, seq=1024, d=1600, ff=6400, heads=25, layers=48, vocab=50257, n_ctx=1024,
+                             table_dtype=30),
+                        "GPT-2 XL prefill B32xS1024 per GPU, d1600, ff6400, 25 heads, 48 layers, bf16 GGUF tables",
+                        dict(score_std=1.0)),
+    "gpt2-medium-prefill": (dict(batch=8, seq=1024, d=1024, ff=4096, heads=16, layers=24, vocab=50257, n_ctx=1024,
+                                 table_dtype=1),
+                            "GPT-2 medium prefill B8xS1024, d1024, ff4096, 16 heads, 24 layers, f16 GGUF tables",
+                            dict(score_std=1.0)),
+    "gpt2-xl-decode": (dict(batch=256, seq=1, d=1600, ff=6400, heads=25, layers=48, vocab=50257, n_ctx=2048,
+                            table_dtype=30, kv_len=2048, pos_off=2047),
+                       "GPT-2 XL decode step B256xS1 at position 2047, 2048-long softmax rows, d1600, ff6400, "
+                       "25 heads, 48 layers, bf16 tables", dict(score_std=math.sqrt(2.0))),
+    "gpt2-small-chain": (dict(batch=1, seq=64, d=768, ff=3072, heads=12, layers=12, vocab=50257, n_ctx=1024,
+                              table_dtype=0),
+                         "GPT-2 small chain B1xS64, d768, ff3072, 12 heads, 12 layers, f32 tables",
+                         dict(score_std=1.0)),
+}
+DEFAULT_WORKLOAD = "gpt2-xl-prefill"
+
+
+def load_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_from_profiles(kernel, workload):
+    """DRAM bytes per launch from a committed ncu summary, if one exists:
+    a line 'dram_bytes_per_launch: <int>' in profiles/<kernel>_<workload>.md."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+
+NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+                0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+                0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, index, period=0.1):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:   # no NVML: report nothing rather than guess
+            self._nv = None
+            self.error = str(e)
+            return self
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def _run(self):
+        nv = self._nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                bits = get_reasons(self._h)
+                for b, name in NVML_REASONS.items():
+                    if bits & b and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (timing only: no collective on the data path)
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def relaunch_distributed(n):
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr", "127.0.0.1", "--master-port", os.environ.get("MASTER_PORT", "29531"), *sys.argv]
+    sys.exit(subprocess.call(cmd))
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference loops (oracle restatement) on the host cores
+
+def cpu_chain_sample(shape, n_tok, layers, nthreads, seed=0):
+    """Times `layers` layers of the chain for `n_tok` tokens of `shape` on the
+    host (embed for those tokens, then per layer residual+LN, the softmax
+    rows of those tokens for every head, residual+LN, bias+GELU).  Returns
+    seconds per token for the full chain (embed + shape.layers layers)."""
+    import numpy as np
+    import oracle
+    rng = np.random.default_rng(seed)
+    d, F, H, L = shape.d, shape.ff, shape.heads, shape.L
+    es_dtype = {0: np.float32, 1: np.float16}.get(shape.table_dtype, np.uint16)
+    wte = (0.02 * rng.standard_normal((shape.vocab, d))).astype(np.float32)
+    if shape.table_dtype == 1:
+        wte = wte.astype(np.float16).view(np.uint16)
+    elif shape.table_dtype == 30:
+        wte = (wte.view(np.uint32) >> 16).astype(np.uint16)
+    wpe = wte[:shape.n_ctx].copy()
+    del es_dtype
+    ids = rng.integers(0, shape.vocab, n_tok).astype(np.int32)
+    x = rng.standard_normal((n_tok, d)).astype(np.float32)
+    r = rng.standard_normal((n_tok, d)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(d)).astype(np.float32)
+    pre = rng.standard_normal((n_tok, F)).astype(np.float32)
+    bias = (0.02 * rng.standard_normal(F)).astype(np.float32)
+    scores = rng.standard_normal((n_tok * H, L)).astype(np.float32)
+    t0 = time.perf_counter()
+    oracle.embed(ids, wte, shape.table_dtype, wpe, shape.table_dtype, d, shape.vocab, shape.n_ctx,
+                 seq=shape.seq, pos_off=shape.pos_off, nthreads=nthreads)
+    t_embed = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    for _ in range(layers):
+        oracle.residual_layernorm(x, r, g, b, nthreads=nthreads)
+        oracle.softmax_rows(scores, nthreads=nthreads)
+        oracle.residual_layernorm(x, r, g, b, nthreads=nthreads)
+        oracle.bias_gelu(pre, bias, nthreads=nthreads)
+    t_layer = (time.perf_counter() - t0) / layers
+    return (t_embed + shape.layers * t_layer) / n_tok, t_embed + layers * t_layer
+
+
+def cpu_baseline(shape, budget_s=12.0):
+    import oracle
+    cores = oracle.max_threads()
+    # size the sample from a quick probe so the whole measurement is ~budget_s
+    per_tok, _ = cpu_chain_sample(shape, n_tok=max(4, cores), layers=1, nthreads=cores)
+    layer_tok = per_tok / max(1, shape.layers)
+    n_tok = int(max(cores, min(shape.tokens, budget_s / 2 / max(layer_tok, 1e-9))))
+    n_tok = max(1, min(n_tok, 8192))
+    per_tok, spent = cpu_chain_sample(shape, n_tok=n_tok, layers=2, nthreads=cores, seed=1)
+    return {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n_tok} tokens x 2 layers of the chain (embed + residual+LN, their {shape.heads} "
+                      f"softmax rows of length {shape.L} each, residual+LN, bias+GELU), extrapolated to "
+                      f"{shape.layers} layers; oracle C restatement of the reference loops, gcc -O3, "
+                      f"{cores} threads", "seconds": round(spent, 2)}
+
+
+# ---------------------------------------------------------------------------
+
+def run_ours(args, shape, desc, chain_kw):
+    import torch
+    rank, world, local = dist_setup(args.gpus)
+    assert torch.cuda.is_available(), "bench.py needs a CUDA device"
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from importlib import import_module
+    chain_mod = import_module("glassboxai-transformer_b200.chain")
+    chain = chain_mod.Chain(shape, device, seed=1000 + rank, **chain_kw)
+    stream = torch.cuda.current_stream(device)
+    torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        chain.step(stream)
+    torch.cuda.synchronize(device)
+    assert int(chain.err.item()) == 0, "embed reported out-of-range ids"
+
+    # --- device-resident timing -------------------------------------------------
+    timers = {}
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            chain.step(stream, timers=timers)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms_local = start.elapsed_time(end)
+    ms = max_over_ranks(ms_local, world, device)
+    ms_per_step = ms / args.steps
+
+    kernels = {}
+    for name, pairs in timers.items():
+        durs = [a.elapsed_time(b) for a, b in pairs]
+        kernels[name] = {"launches": len(durs), "avg_us": 1000.0 * sum(durs) / len(durs)}
+    byte_of = {"embed": shape.bytes_embed(), "layernorm": shape.bytes_ln(),
+               "residual_layernorm": shape.bytes_residual_ln(), "softmax_rows": shape.bytes_softmax(),
+               "bias_gelu": shape.bytes_gelu(), "final_layernorm": 16 * shape.batch * shape.d + 8 * shape.d}
+    peak, peak_kind = load_peak()
+    for name, k in kernels.items():
+        k["bytes_per_launch"] = byte_of[name]
+        k["gbs"] = byte_of[name] / (k["avg_us"] * 1e-6) / 1e9
+        k["frac_of_" + peak_kind] = k["gbs"] / peak
+
+    # --- end to end through the API with host buffers -----------------------------
+    ids_host = chain.ids.cpu().pin_memory()
+    out_host = torch.empty(chain.out.shape, dtype=torch.float32).pin_memory()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        chain.ids.copy_(ids_host, non_blocking=True)
+        chain.step(stream)
+        out_host.copy_(chain.out, non_blocking=True)
+        stream.synchronize()
+    barrier(world)
+    torch.cuda.synchronize(device)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        chain.ids.copy_(ids_host, non_blocking=True)      # H2D of the step's token ids
+        chain.step(stream)
+        out_host.copy_(chain.out, non_blocking=True)      # D2H of the step's result
+        stream.synchronize()                              # the caller reads the result
+    e_end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e_ms = max_over_ranks(e_start.elapsed_time(e_end), world, device) / args.steps
+
+    tokens_total = shape.tokens * world
+    sm = kernels["softmax_rows"]
+    result = {
+        "metric": METRIC,
+        "value": tokens_total / (ms_per_step * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (activations; tables " + {0: "f32", 1: "f16", 30: "bf16"}[shape.table_dtype] + ")",
+        "data": "synthetic (seeded torch.randn / randint on device; random-init tables)",
+        "config": {"workload": args.workload, "description": desc, "tokens_per_gpu": shape.tokens,
+                   "global_batch": shape.batch * world, "seq_len": shape.seq, "layers": shape.layers,
+                   "parallelism": f"row shards of whole sequences over {world} GPU(s), no collective",
+                   "l2": "no flush; every streamed buffer is larger than the 126 MB L2 "
+                         f"(smallest: {shape.tokens * shape.d * 4 / 1e6:.0f} MB)"},
+        "hbm": {"bytes_per_step": shape.bytes_per_step(),
+                "gbs": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
+                "frac": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9 / peak,
+                "peak": peak, "peak_kind": peak_kind},
+        "roofline": {"kernel": "softmax_rows", "bound": "hbm", "achieved": sm["gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": sm["gbs"] / peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": shape.bytes_softmax(),
+                     "traffic": traffic_from_profiles("softmax_rows", args.workload)},
+        "kernels": kernels,
+        "gpu_launches": shape.launches_per_step() * args.steps,
+        "clocks": clk.summary(),
+        "e2e": {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(chain.ids.numel() * 4), "d2h_bytes_per_step": int(chain.out.numel() * 4),
+                "ms_per_step": e_ms,
+                "path": "C ABI launches (ctypes) with pinned host token ids in, final LayerNorm rows out"},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(shape)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def reference_gpu_kernels(shape):
+    """The reference's own kernels (its transformer.cu compiled unmodified) on
+    one GPU for one layer of the chain, with its launch shapes."""
+    import torch
+    import oracle
+    if not oracle.ref_available():
+        return {"unavailable": "reference build (oracle/_ref) not present"}
+    R = oracle.ref()
+    dev = torch.device("cuda", 0)
+    N, d, F = shape.tokens, shape.d, shape.ff
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    f32 = dict(dtype=torch.float32, device=dev)
+    h = torch.randn((N, d), generator=g, **f32)
+    x = torch.randn((N, d), generator=g, **f32)
+    y = torch.empty((N, d), **f32)
+    gam = torch.randn((d,), generator=g, **f32)
+    bet = torch.randn((d,), generator=g, **f32)
+    ffn = torch.randn((N, F), generator=g, **f32)
+    scores = torch.randn((shape.batch * shape.heads * shape.seq, shape.L), generator=g, **f32)
+    per_launch_rows = shape.seq          # one launch per head of one sequence (transformer.cu:839-842)
+    n_sm_launch = shape.batch * shape.heads
+
+    def timed(fn, reps=3):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps * 1e-3
+
+    def ln():
+        assert R.ref_launch_layernorm(h.data_ptr(), y.data_ptr(), gam.data_ptr(), bet.data_ptr(), N, d, None) == 0
+
+    def resid():
+        assert R.ref_launch_add(h.data_ptr(), x.data_ptr(), N * d, None) == 0
+
+    def sm():
+        base = scores.data_ptr()
+        step = per_launch_rows * shape.L * 4
+        for i in range(n_sm_launch):
+            assert R.ref_launch_softmax(base + i * step, per_launch_rows, shape.L, None) == 0
+
+    def gelu():
+        assert R.ref_launch_gelu(ffn.data_ptr(), N * F, None) == 0
+
+    t = {"layerNormKernel": timed(ln), "addResidualKernel": timed(resid), "softmaxKernel (per head)": timed(sm),
+         "geluKernel": timed(gelu)}
+    layer = 2 * t["layerNormKernel"] + 2 * t["addResidualKernel"] + t["softmaxKernel (per head)"] + t["geluKernel"]
+    algo = {"layerNormKernel": shape.bytes_ln(), "addResidualKernel": 12 * N * d,
+            "softmaxKernel (per head)": shape.bytes_softmax(), "geluKernel": 8 * N * F}
+    del h, x, y, ffn, scores
+    torch.cuda.empty_cache()
+    emb = ("launch failure as shipped: embedTokensKernel uses blockDim = d = %d > 1024" % d) if d > 1024 else None
+    return {"tokens_per_s_chain_without_embed": shape.tokens / (shape.layers * layer),
+            "per_kernel": {k: {"ms": v * 1e3, "algorithmic_gbs": algo[k] / v / 1e9} for k, v in t.items()},
+            "embed": emb or "not timed",
+            "note": "one layer timed (LN x2, residual add x2, softmax per head of each sequence, GELU in place), "
+                    "chain = layers x that"}
+
+
+def run_reference(args, shape, desc):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import oracle
+    cores = oracle.max_threads()
+    # bounded sample per step: n_s tokens through the whole chain on all host cores
+    n_s = max(cores, 16)
+    for _ in range(args.warmup):
+        cpu_chain_sample(shape, n_tok=n_s, layers=1, nthreads=cores)
+    per_step = []
+    for k in range(args.steps):
+        per_tok, _ = cpu_chain_sample(shape, n_tok=n_s, layers=1, nthreads=cores, seed=k)
+        per_step.append(per_tok * n_s)
+    sec = statistics.mean(per_step)
+    value = n_s / sec
+    out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
+           "config": {"workload": args.workload, "description": desc, "sample_tokens_per_step": n_s},
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": f"{n_s} tokens per step through embed + 1 layer of the chain (all "
+                                      f"{shape.heads} softmax rows of length {shape.L} per token), extrapolated "
+                                      f"to {shape.layers} layers; the reference's loops restated in C "
+                                      f"(oracle/gbx_oracle.c) on {cores} host threads"},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    try:
+        import torch
+        if torch.cuda.is_available() and not args.no_ref_gpu:
+            out["reference_gpu_kernels"] = reference_gpu_kernels(shape)
+    except Exception as e:   # report, never fail the reference line
+        out["reference_gpu_kernels"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
+        relaunch_distributed(args.gpus)
+    shape_kw, desc, chain_kw = WORKLOADS[args.workload]
+    chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
+    shape = chain_mod.ChainShape(**shape_kw)
+    if args.impl == "reference":
+        run_reference(args, shape, desc)
+    else:
+        run_ours(args, shape, desc, chain_kw)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,132 @@
+"""Python binding of the B200 hot-path C ABI (``include/gbx.h``, ``libgbx.so``).
+
+The product is the C ABI; this module is a thin ctypes layer over it for the
+test suite, the benchmark and Python callers.  Pointers are passed straight
+through: arguments may be torch tensors (``data_ptr()``), raw integer device
+addresses, or ``None`` for nullable pointers.  Every call raises ``GbxError``
+on a non-zero status with the library's own message.
+
+There is no fallback: importing this module fails loudly if ``libgbx.so``
+has not been built (``make -C glassboxai-transformer_b200``).
+
+Import it by path, e.g. ``importlib.import_module("glassboxai-transformer_b200")``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgbx.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "gbx.h")
+
+DT_F32, DT_F16, DT_BF16 = 0, 1, 30
+EMBED_BAD_ID, EMBED_BAD_POS = 1, 2
+
+STATUS = {0: "GBX_OK", 1: "GBX_EINVAL", 2: "GBX_EDTYPE", 3: "GBX_ERANGE", 4: "GBX_ECUDA",
+          5: "GBX_EIO", 6: "GBX_ENOTFOUND", 7: "GBX_ENOMEM"}
+
+
+class GbxError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_f = ctypes.c_float
+
+# name -> argtypes (restype int unless listed in _RESTYPES)
+SIGNATURES = {
+    "gbx_version": [],
+    "gbx_status_string": [_int],
+    "gbx_last_error": [],
+    "gbx_dequant": [_vp, _int, _vp, _i64, _vp],
+    "gbx_embed": [_vp, _vp, _int, _vp, _int, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, _vp],
+    "gbx_layernorm": [_vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
+    "gbx_residual_layernorm": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
+    "gbx_bias_gelu": [_vp, _vp, _vp, _i64, _int, _vp],
+    "gbx_softmax_rows": [_vp, _vp, _i64, _int, _vp],
+}
+_RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"libgbx.so is not built ({LIB_PATH}); run make -C glassboxai-transformer_b200")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPES.get(name, _int)
+        _lib = L
+    return _lib
+
+
+lib()   # fail at import time when the library is missing
+
+
+def _p(x):
+    """Device address of a tensor / int / None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return torch.cuda.current_stream().cuda_stream
+        except ImportError:
+            pass
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise GbxError(rc, lib().gbx_last_error().decode(errors="replace"))
+
+
+def version() -> int:
+    return lib().gbx_version()
+
+
+def dequant(src, dtype: int, dst, n: int, stream=None):
+    _check(lib().gbx_dequant(_p(src), dtype, _p(dst), n, _stream(stream)))
+
+
+def embed(ids, wte, wte_dtype, wpe, wpe_dtype, out, *, n_tok, d, vocab, n_ctx, seq=None, pos_off=0,
+          pos_ids=None, err_flag=None, stream=None):
+    seq = n_tok if seq is None else seq
+    _check(lib().gbx_embed(_p(ids), _p(wte), wte_dtype, _p(wpe), wpe_dtype, _p(pos_ids), _p(out), n_tok,
+                           seq, pos_off, d, vocab, n_ctx, _p(err_flag), _stream(stream)))
+
+
+def layernorm(x, y, gamma, beta, *, rows, d, eps=1e-5, stream=None):
+    _check(lib().gbx_layernorm(_p(x), _p(y), _p(gamma), _p(beta), rows, d, eps, _stream(stream)))
+
+
+def residual_layernorm(x, r, h_out, y, gamma, beta, *, rows, d, eps=1e-5, xbias=None, stream=None):
+    _check(lib().gbx_residual_layernorm(_p(x), _p(r), _p(xbias), _p(h_out), _p(y), _p(gamma), _p(beta),
+                                        rows, d, eps, _stream(stream)))
+
+
+def bias_gelu(x, out, bias, *, rows, F, stream=None):
+    _check(lib().gbx_bias_gelu(_p(x), _p(out), _p(bias), rows, F, _stream(stream)))
+
+
+def softmax_rows(x, out, *, rows, L, stream=None):
+    _check(lib().gbx_softmax_rows(_p(x), _p(out), rows, L, _stream(stream)))

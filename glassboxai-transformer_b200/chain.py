@@ -1,0 +1,189 @@
+"""The per-layer hot-path chain of ``TransformerModel::forward``
+(transformer.cu:913-927), as launched through the C ABI.
+
+For each forward the reference runs: embedTokens (:805-815); per layer
+LayerNorm (:828) -> [QKV, scores] -> softmax per head (:839-842) ->
+[PV, projection + residual (:850)] -> LayerNorm (:868) -> [ffn-up + bias +
+GELU (:872)] -> [ffn-down + residual (:876)]; finally LayerNorm of the last
+row (:890-896) before the logits.  The bracketed contractions are outside the
+hot path: their outputs are supplied as buffers (``attn_out``: projection
+output, ``ffn_pre``: ffn-up pre-activation, ``ffn_out``: ffn-down output,
+``scores``: scaled and causally masked QK^T in the reference's -1e9
+convention), and the hot path consumes them exactly as the reference's
+kernels would:
+
+  embed                                   -> h
+  layer 0:  LN1(h)                        -> ln        (layernorm)
+  layer l:  h += ffn_out(l-1); LN1(h)     -> ln        (residual_layernorm)
+            softmax(scores)               -> probs     (softmax_rows, all heads, all sequences)
+            h += attn_out; LN2(h)         -> ln        (residual_layernorm)
+            bias + GELU(ffn_pre)          -> ffn_act   (bias_gelu)
+  final:    h_last += ffn_out_last; LN_f  -> out [B, d] (residual_layernorm on each
+                                                        sequence's last row)
+
+Rows are independent, so a batch of B whole sequences is one call per
+kernel (the reference launches per head and has no batch dimension).
+"""
+from __future__ import annotations
+
+import importlib
+from dataclasses import dataclass
+
+_gbx = importlib.import_module(__package__)
+
+
+@dataclass
+class ChainShape:
+    batch: int          # sequences
+    seq: int            # query rows per sequence
+    d: int              # d_model
+    ff: int             # feed-forward width
+    heads: int
+    layers: int
+    vocab: int = 50257
+    n_ctx: int = 1024
+    table_dtype: int = 30     # GGUF dtype of wte / wpe
+    kv_len: int | None = None  # softmax row length (defaults to seq: causal prefill)
+    pos_off: int = 0
+
+    @property
+    def tokens(self):
+        return self.batch * self.seq
+
+    @property
+    def L(self):
+        return self.kv_len if self.kv_len is not None else self.seq
+
+    @property
+    def softmax_rows(self):
+        return self.batch * self.heads * self.seq
+
+    def table_es(self):
+        return 4 if self.table_dtype == 0 else 2
+
+    # Algorithmic bytes per launch (each input read once, each output written once).
+    def bytes_embed(self):
+        # ids + gathered wte rows + distinct wpe rows + output
+        distinct_pos = min(self.seq, self.n_ctx)
+        return 4 * self.tokens + self.tokens * self.d * self.table_es() + distinct_pos * self.d * self.table_es() \
+            + 4 * self.tokens * self.d
+
+    def bytes_ln(self, rows=None):
+        rows = self.tokens if rows is None else rows
+        return 8 * rows * self.d + 8 * self.d
+
+    def bytes_residual_ln(self, rows=None):
+        rows = self.tokens if rows is None else rows
+        return 16 * rows * self.d + 8 * self.d
+
+    def bytes_gelu(self):
+        return 8 * self.tokens * self.ff + 4 * self.ff
+
+    def bytes_softmax(self):
+        return 8 * self.softmax_rows * self.L
+
+    def launches_per_step(self):
+        return 1 + 1 + 4 * self.layers - 1 + 1
+
+    def bytes_per_step(self):
+        final = 16 * self.batch * self.d + 8 * self.d
+        return (self.bytes_embed() + self.bytes_ln() + (2 * self.layers - 1) * self.bytes_residual_ln()
+                + self.layers * (self.bytes_softmax() + self.bytes_gelu()) + final)
+
+
+class Chain:
+    """Device buffers for one shard and the launch sequence of one step.
+
+    ``timers``: optional dict kernel-name -> list, into which (start, end)
+    CUDA event pairs are appended around every launch (events recorded on the
+    launching stream).
+    """
+
+    def __init__(self, shape: ChainShape, device, seed=0, act_std=1.0, table_std=0.02, score_std=1.0,
+                 causal=True):
+        import torch
+        self.s = s = shape
+        self.device = device
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        f32 = dict(dtype=torch.float32, device=device)
+
+        def normal(shape_, std, mean=0.0):
+            return torch.randn(shape_, generator=g, **f32).mul_(std).add_(mean)
+
+        def table(rows):
+            t = normal((rows, s.d), table_std)
+            if s.table_dtype == 0:
+                return t
+            return (t.to(torch.float16) if s.table_dtype == 1 else t.to(torch.bfloat16)).contiguous()
+
+        self.ids = torch.randint(0, s.vocab, (s.tokens,), generator=g, dtype=torch.int32, device=device)
+        self.wte = table(s.vocab)
+        self.wpe = table(s.n_ctx)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        N, d, F = s.tokens, s.d, s.ff
+        self.h = torch.empty((N, d), **f32)
+        self.ln = torch.empty((N, d), **f32)
+        self.attn_out = normal((N, d), act_std)
+        self.ffn_out = normal((N, d), act_std)
+        self.ffn_pre = normal((N, F), act_std)
+        self.ffn_act = torch.empty((N, F), **f32)
+        self.scores = normal((s.softmax_rows, s.L), score_std)
+        if causal and s.kv_len is None:
+            # scores[b, h, p, q] = -1e9 for q > p (transformer.cu:220-221)
+            mask = torch.triu(torch.ones(s.seq, s.seq, dtype=torch.bool, device=device), diagonal=1)
+            self.scores.view(-1, s.seq, s.seq).masked_fill_(mask, -1e9)
+        self.probs = torch.empty_like(self.scores)
+        self.g1 = normal((s.layers, d), 0.1, 1.0)
+        self.b1 = normal((s.layers, d), 0.02)
+        self.g2 = normal((s.layers, d), 0.1, 1.0)
+        self.b2 = normal((s.layers, d), 0.02)
+        self.up_bias = normal((s.layers, F), 0.02)
+        self.gf = normal((d,), 0.1, 1.0)
+        self.bf = normal((d,), 0.02)
+        self.last_h = torch.empty((s.batch, d), **f32)
+        self.last_f = torch.empty((s.batch, d), **f32)
+        self.out = torch.empty((s.batch, d), **f32)
+
+    def step(self, stream=None, timers=None):
+        import torch
+        s, G = self.s, _gbx
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+
+        def run(name, fn):
+            if timers is None:
+                fn()
+                return
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            timers.setdefault(name, []).append((a, b))
+
+        N, d = s.tokens, s.d
+        run("embed", lambda: G.embed(self.ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, self.h, n_tok=N,
+                                     d=d, vocab=s.vocab, n_ctx=s.n_ctx, seq=s.seq, pos_off=s.pos_off,
+                                     err_flag=self.err, stream=st))
+        for l in range(s.layers):
+            if l == 0:
+                run("layernorm", lambda: G.layernorm(self.h, self.ln, self.g1[0], self.b1[0], rows=N, d=d,
+                                                     stream=st))
+            else:
+                run("residual_layernorm",
+                    lambda: G.residual_layernorm(self.ffn_out, self.h, self.h, self.ln, self.g1[l], self.b1[l],
+                                                 rows=N, d=d, stream=st))
+            run("softmax_rows", lambda: G.softmax_rows(self.scores, self.probs, rows=s.softmax_rows, L=s.L,
+                                                       stream=st))
+            run("residual_layernorm",
+                lambda: G.residual_layernorm(self.attn_out, self.h, self.h, self.ln, self.g2[l], self.b2[l],
+                                             rows=N, d=d, stream=st))
+            run("bias_gelu", lambda: G.bias_gelu(self.ffn_pre, self.ffn_act, self.up_bias[l], rows=N, F=s.ff,
+                                                 stream=st))
+        # final residual add + ln_f on each sequence's last row (transformer.cu:890-896)
+        with torch.cuda.stream(st):
+            self.last_h.copy_(self.h.view(s.batch, s.seq, d)[:, -1])
+            self.last_f.copy_(self.ffn_out.view(s.batch, s.seq, d)[:, -1])
+        run("final_layernorm", lambda: G.residual_layernorm(self.last_f, self.last_h, None, self.out, self.gf,
+                                                            self.bf, rows=s.batch, d=d, stream=st))
+        return self.out

@@ -1,0 +1,114 @@
+// bias_gelu.cu -- bias + GELU(tanh) (replaces the ffnUpKernel epilogue,
+// transformer.cu:272, 276-277, and geluKernel, :68-75).
+//
+// Layout: a CTA owns one band of T float4 columns and walks the rows of its
+// slab; each thread keeps its column's 4 bias values in registers for the
+// whole kernel (the bias row never goes back to memory) and streams kU rows
+// per pass with all loads issued before any arithmetic.  The formula is the
+// reference's, with the cubic term fused as the reference's nvcc build fuses
+// it, and CUDA's tanhf (no fast-math):
+//   u = in + bias; out = u * (0.5f * (1.0f + tanhf(0.7978845608f * (u + 0.044715f*u*u*u))))
+#include "gbx_common.cuh"
+
+namespace gbx {
+
+constexpr int kGeluU = 4;
+
+__device__ __forceinline__ float gelu_tanh(float u)
+{
+    const float inner = fmaf((0.044715f * u) * u, u, u);
+    return u * (0.5f * (1.0f + tanhf(0.7978845608f * inner)));
+}
+
+__device__ __forceinline__ float4 gelu4(float4 u)
+{
+    return make_float4(gelu_tanh(u.x), gelu_tanh(u.y), gelu_tanh(u.z), gelu_tanh(u.w));
+}
+
+template <bool BIAS>
+__global__ void __launch_bounds__(512)
+bias_gelu_vec_kernel(const float* in, float* out, const float* __restrict__ bias, int64_t rows, int n4)
+{
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= n4) return;   // no barriers below
+    const int64_t F = 4LL * n4;
+    const float4 b = BIAS ? ld_param4(bias + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t r0 = (int64_t)blockIdx.y * kGeluU; r0 < rows; r0 += (int64_t)gridDim.y * kGeluU) {
+        float4 v[kGeluU];
+#pragma unroll
+        for (int u = 0; u < kGeluU; ++u)
+            v[u] = (r0 + u < rows) ? ld_stream(in + (r0 + u) * F + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < kGeluU; ++u) {
+            if (r0 + u < rows) {
+                float4 x = v[u];
+                if (BIAS) x = make_float4(x.x + b.x, x.y + b.y, x.z + b.z, x.w + b.w);
+                st_stream(out + (r0 + u) * F + 4 * c, gelu4(x));
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+bias_gelu_general_kernel(const float* in, float* out, const float* __restrict__ bias, int64_t rows, int F)
+{
+    const int64_t total = rows * F;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float u = in[i];
+        if (bias) u = u + bias[i % F];
+        out[i] = gelu_tanh(u);
+    }
+}
+
+// Column band width: the largest multiple of 32 in [128, 512] that divides
+// n4 (no idle lanes), else 256 (short rows: n4 rounded up to a warp).
+static int gelu_band(int n4)
+{
+    if (n4 < 128) return (n4 + 31) / 32 * 32;
+    for (int t = 512; t >= 128; t -= 32)
+        if (n4 % t == 0) return t;
+    return 256;
+}
+
+template <bool BIAS>
+static int launch_gelu_vec(const float* in, float* out, const float* bias, int64_t rows, int n4,
+                           cudaStream_t stream)
+{
+    auto k = bias_gelu_vec_kernel<BIAS>;
+    const int T = gelu_band(n4);
+    const int gx = (n4 + T - 1) / T;
+    DeviceInfo di;
+    if (device_info(&di) != GBX_OK) return GBX_ECUDA;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, T, 0) != cudaSuccess || occ < 1) occ = 1;
+    const int64_t target = (int64_t)di.sm_count * occ;
+    int64_t gy = (target + gx - 1) / gx;
+    const int64_t slabs = (rows + kGeluU - 1) / kGeluU;
+    if (gy > slabs) gy = slabs;
+    if (gy > 65535) gy = 65535;
+    if (gy < 1) gy = 1;
+    k<<<dim3(gx, (unsigned)gy), T, 0, stream>>>(in, out, bias, rows, n4);
+    return check_launch("gbx_bias_gelu");
+}
+
+}  // namespace gbx
+
+using namespace gbx;
+
+extern "C" int gbx_bias_gelu(const float* in, float* out, const float* bias, int64_t rows, int F,
+                             gbx_stream_t stream)
+{
+    if (rows < 0 || F <= 0) return set_error(GBX_EINVAL, "gbx_bias_gelu: rows=%lld F=%d", (long long)rows, F);
+    if (rows == 0) return GBX_OK;
+    if (!in || !out) return set_error(GBX_EINVAL, "gbx_bias_gelu: null pointer");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (F % 4 == 0 && aligned16(in) && aligned16(out) && (!bias || aligned16(bias))) {
+        return bias ? launch_gelu_vec<true>(in, out, bias, rows, F / 4, s)
+                    : launch_gelu_vec<false>(in, out, bias, rows, F / 4, s);
+    }
+    const int grid = persistent_grid(bias_gelu_general_kernel, 256, 0, (rows * F + 255) / 256, 4);
+    if (grid < 1) return GBX_ECUDA;
+    bias_gelu_general_kernel<<<grid, 256, 0, s>>>(in, out, bias, rows, F);
+    return check_launch("gbx_bias_gelu");
+}

@@ -1,0 +1,295 @@
+// embed.cu -- GGUF f32/f16/bf16 decode and the token+position embedding
+// gather/add (replaces GGUFLoader's host dequant, transformer.cu:508-534 and
+// :635-650, and embedTokensKernel, transformer.cu:175-185).
+//
+// The tables stay in their GGUF encoding in HBM; each 16-byte load brings 8
+// f16/bf16 elements (or 4 f32), which are decoded in registers with the
+// reference's exact rules and added in fp32.  Output rows are written with
+// streaming 16-byte stores.
+#include "gbx_common.cuh"
+
+namespace gbx {
+
+// GGUF dtype code -> template index.
+enum { TF32 = 0, TF16 = 1, TBF16 = 2 };
+
+// Reference float16ToFloat32 (transformer.cu:508-527), as fp32 bits:
+// normal halves re-biased exactly; +-0 -> +0 (sign dropped, :514);
+// subnormals mantissa * 2^-24 (exact); +-inf kept; any NaN -> 0x7fc00000 (:521).
+__device__ __forceinline__ uint32_t f16_to_f32_bits(uint32_t h)
+{
+    const uint32_t sign = (h & 0x8000u) << 16;
+    const uint32_t ex = (h >> 10) & 0x1fu;
+    const uint32_t man = h & 0x3ffu;
+    const uint32_t normal = sign | ((ex + 112u) << 23) | (man << 13);
+    const uint32_t sub = sign | __float_as_uint(__uint2float_rn(man) * 5.9604644775390625e-8f);
+    const uint32_t infnan = man ? 0x7fc00000u : (sign | 0x7f800000u);
+    return ex == 0 ? (man ? sub : 0u) : (ex == 31 ? infnan : normal);
+}
+
+__device__ __forceinline__ float f16_to_f32(uint32_t h) { return __uint_as_float(f16_to_f32_bits(h)); }
+
+// Decode the 8 consecutive elements starting at element `e` (a multiple of 8)
+// of a table of type T.  16-byte aligned by construction.
+template <int T>
+__device__ __forceinline__ void load8(const void* base, int64_t e, float (&v)[8])
+{
+    if (T == TF32) {
+        const float* p = static_cast<const float*>(base) + e;
+        float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint16_t* p = static_cast<const uint16_t*>(base) + e;
+        uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
+        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (T == TF16) {
+                v[2 * k] = f16_to_f32(ws[k] & 0xffffu);
+                v[2 * k + 1] = f16_to_f32(ws[k] >> 16);
+            } else {
+                v[2 * k] = __uint_as_float(ws[k] << 16);
+                v[2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
+            }
+        }
+    }
+}
+
+template <int T>
+__device__ __forceinline__ float load1(const void* base, int64_t e)
+{
+    if (T == TF32) return __ldg(static_cast<const float*>(base) + e);
+    uint32_t h = __ldg(static_cast<const unsigned short*>(base) + e);
+    return T == TF16 ? f16_to_f32(h) : __uint_as_float(h << 16);
+}
+
+// ---------------------------------------------------------------------------
+// Embedding, vector path.  Work item = (token t, 8-element chunk c); items are
+// numbered t*n8 + c so consecutive threads cover consecutive 32-byte pieces of
+// one output row.  Each thread takes kU items per pass and issues all their
+// loads before any arithmetic.
+constexpr int kEmbedThreads = 256;
+constexpr int kEmbedU = 4;
+
+template <int WT, int PT>
+__global__ void __launch_bounds__(kEmbedThreads)
+embed_vec8_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
+                  const void* __restrict__ wpe, const int32_t* __restrict__ pos_ids,
+                  float* __restrict__ out, uint32_t total, FastDiv div_n8, FastDiv div_seq,
+                  int pos_off, int d, int vocab, int n_ctx, int32_t* __restrict__ err)
+{
+    const uint32_t n8 = div_n8.d;
+    const uint32_t seq = div_seq.d;
+    const uint32_t stride = gridDim.x * (uint32_t)kEmbedThreads * kEmbedU;
+    for (uint32_t base = blockIdx.x * (uint32_t)kEmbedThreads * kEmbedU + threadIdx.x; base < total;
+         base += stride) {
+        int32_t tok[kEmbedU], col[kEmbedU], id[kEmbedU], pos[kEmbedU];
+#pragma unroll
+        for (int u = 0; u < kEmbedU; ++u) {
+            uint32_t i = base + u * kEmbedThreads;
+            uint32_t t = fast_div(i < total ? i : 0, div_n8);
+            tok[u] = (int32_t)t;
+            col[u] = (int32_t)((i < total ? i : 0) - t * n8);
+            id[u] = i < total ? __ldg(ids + t) : 0;
+            pos[u] = pos_ids ? (i < total ? __ldg(pos_ids + t) : 0)
+                             : pos_off + (int32_t)(t - fast_div(t, div_seq) * seq);
+        }
+        float a[kEmbedU][8], b[kEmbedU][8];
+#pragma unroll
+        for (int u = 0; u < kEmbedU; ++u) {
+            const bool ok = (uint32_t)id[u] < (uint32_t)vocab && (uint32_t)pos[u] < (uint32_t)n_ctx;
+            if (base + u * kEmbedThreads < total && ok) {
+                load8<WT>(wte, (int64_t)id[u] * d + col[u] * 8, a[u]);
+                load8<PT>(wpe, (int64_t)pos[u] * d + col[u] * 8, b[u]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) { a[u][k] = 0.0f; b[u][k] = 0.0f; }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kEmbedU; ++u) {
+            uint32_t i = base + u * kEmbedThreads;
+            if (i >= total) continue;
+            const bool bad_id = (uint32_t)id[u] >= (uint32_t)vocab;
+            const bool bad_pos = (uint32_t)pos[u] >= (uint32_t)n_ctx;
+            if ((bad_id || bad_pos) && col[u] == 0 && err)
+                atomicOr(err, (bad_id ? GBX_EMBED_BAD_ID : 0) | (bad_pos ? GBX_EMBED_BAD_POS : 0));
+            float* o = out + (int64_t)tok[u] * d + col[u] * 8;
+            // one fp32 add per element, as embedTokensKernel (transformer.cu:183);
+            // a rejected token's row is zeros (0 + 0).
+            st_stream(o, make_float4(a[u][0] + b[u][0], a[u][1] + b[u][1], a[u][2] + b[u][2], a[u][3] + b[u][3]));
+            st_stream(o + 4, make_float4(a[u][4] + b[u][4], a[u][5] + b[u][5], a[u][6] + b[u][6], a[u][7] + b[u][7]));
+        }
+    }
+}
+
+// General path: any d, any alignment, 64-bit indexing; one element per item.
+template <int WT, int PT>
+__global__ void __launch_bounds__(256)
+embed_scalar_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
+                    const void* __restrict__ wpe, const int32_t* __restrict__ pos_ids,
+                    float* __restrict__ out, int64_t n_tok, int seq, int pos_off, int d, int vocab,
+                    int n_ctx, int32_t* __restrict__ err)
+{
+    const int64_t total = n_tok * d;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / d;
+        const int c = (int)(i - t * d);
+        const int32_t id = __ldg(ids + t);
+        const int64_t pos = pos_ids ? (int64_t)__ldg(pos_ids + t) : (int64_t)pos_off + t % seq;
+        const bool bad_id = (uint32_t)id >= (uint32_t)vocab;
+        const bool bad_pos = pos < 0 || pos >= n_ctx;
+        float v = 0.0f;
+        if (!bad_id && !bad_pos) v = load1<WT>(wte, (int64_t)id * d + c) + load1<PT>(wpe, pos * d + c);
+        else if (c == 0 && err)
+            atomicOr(err, (bad_id ? GBX_EMBED_BAD_ID : 0) | (bad_pos ? GBX_EMBED_BAD_POS : 0));
+        out[i] = v;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Dequant: 8 elements per item on the vector path, scalar tail.
+template <int T>
+__global__ void __launch_bounds__(256)
+dequant_vec8_kernel(const void* __restrict__ src, float* __restrict__ dst, int64_t n8)
+{
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float v[8];
+        load8<T>(src, i * 8, v);
+        st_stream(dst + i * 8, make_float4(v[0], v[1], v[2], v[3]));
+        st_stream(dst + i * 8 + 4, make_float4(v[4], v[5], v[6], v[7]));
+    }
+}
+
+template <int T>
+__global__ void __launch_bounds__(256)
+dequant_scalar_kernel(const void* __restrict__ src, float* __restrict__ dst, int64_t begin, int64_t n)
+{
+    for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = load1<T>(src, i);
+}
+
+static int dtype_index(int dt)
+{
+    switch (dt) {
+    case GBX_DT_F32: return TF32;
+    case GBX_DT_F16: return TF16;
+    case GBX_DT_BF16: return TBF16;
+    default: return -1;
+    }
+}
+
+template <int WT, int PT>
+static int launch_embed(const int32_t* ids, const void* wte, const void* wpe, const int32_t* pos_ids,
+                        float* out, int64_t n_tok, int seq, int pos_off, int d, int vocab, int n_ctx,
+                        int32_t* err, cudaStream_t stream)
+{
+    const int n8 = d / 8;
+    const int64_t total = n_tok * (int64_t)n8;
+    // total < 2^31 keeps base + stride (stride < 2^31 as well) from wrapping
+    // the 32-bit item counter of the grid-stride loop.
+    const bool vec = (d % 8 == 0) && total < 0x7fffffffLL && aligned16(wte) && aligned16(wpe) &&
+                     aligned16(out);
+    if (vec) {
+        auto k = embed_vec8_kernel<WT, PT>;
+        const int64_t blocks = (total + (int64_t)kEmbedThreads * kEmbedU - 1) / ((int64_t)kEmbedThreads * kEmbedU);
+        const int grid = persistent_grid(k, kEmbedThreads, 0, blocks, 2);
+        if (grid < 1) return GBX_ECUDA;
+        k<<<grid, kEmbedThreads, 0, stream>>>(ids, wte, wpe, pos_ids, out, (uint32_t)total,
+                                               make_fastdiv((uint32_t)n8), make_fastdiv((uint32_t)seq),
+                                               pos_off, d, vocab, n_ctx, err);
+    } else {
+        auto k = embed_scalar_kernel<WT, PT>;
+        const int64_t total_e = n_tok * (int64_t)d;
+        const int grid = persistent_grid(k, 256, 0, (total_e + 255) / 256, 4);
+        if (grid < 1) return GBX_ECUDA;
+        k<<<grid, 256, 0, stream>>>(ids, wte, wpe, pos_ids, out, n_tok, seq, pos_off, d, vocab, n_ctx, err);
+    }
+    return check_launch("gbx_embed");
+}
+
+template <int WT>
+static int launch_embed_p(int pt, const int32_t* ids, const void* wte, const void* wpe,
+                          const int32_t* pos_ids, float* out, int64_t n_tok, int seq, int pos_off,
+                          int d, int vocab, int n_ctx, int32_t* err, cudaStream_t s)
+{
+    switch (pt) {
+    case TF32: return launch_embed<WT, TF32>(ids, wte, wpe, pos_ids, out, n_tok, seq, pos_off, d, vocab, n_ctx, err, s);
+    case TF16: return launch_embed<WT, TF16>(ids, wte, wpe, pos_ids, out, n_tok, seq, pos_off, d, vocab, n_ctx, err, s);
+    default: return launch_embed<WT, TBF16>(ids, wte, wpe, pos_ids, out, n_tok, seq, pos_off, d, vocab, n_ctx, err, s);
+    }
+}
+
+template <int T>
+static int launch_dequant(const void* src, float* dst, int64_t n, cudaStream_t stream)
+{
+    int64_t done = 0;
+    if (aligned16(src) && aligned16(dst) && n >= 8) {
+        auto k = dequant_vec8_kernel<T>;
+        const int64_t n8 = n / 8;
+        const int grid = persistent_grid(k, 256, 0, (n8 + 255) / 256, 4);
+        if (grid < 1) return GBX_ECUDA;
+        k<<<grid, 256, 0, stream>>>(src, dst, n8);
+        done = n8 * 8;
+    }
+    if (done < n) {
+        auto k = dequant_scalar_kernel<T>;
+        const int grid = persistent_grid(k, 256, 0, (n - done + 255) / 256, 4);
+        if (grid < 1) return GBX_ECUDA;
+        k<<<grid, 256, 0, stream>>>(src, dst, done, n);
+    }
+    return check_launch("gbx_dequant");
+}
+
+}  // namespace gbx
+
+using namespace gbx;
+
+extern "C" int gbx_dequant(const void* src, int dtype, float* dst, int64_t n, gbx_stream_t stream)
+{
+    const int t = dtype_index(dtype);
+    if (t < 0) return set_error(GBX_EDTYPE, "gbx_dequant: unsupported GGUF dtype %d", dtype);
+    if (n < 0) return set_error(GBX_EINVAL, "gbx_dequant: n=%lld", (long long)n);
+    if (n == 0) return GBX_OK;
+    if (!src || !dst) return set_error(GBX_EINVAL, "gbx_dequant: null pointer");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (t) {
+    case TF32: return launch_dequant<TF32>(src, dst, n, s);
+    case TF16: return launch_dequant<TF16>(src, dst, n, s);
+    default: return launch_dequant<TBF16>(src, dst, n, s);
+    }
+}
+
+extern "C" int gbx_embed(const int32_t* ids, const void* wte, int wte_dtype, const void* wpe,
+                         int wpe_dtype, const int32_t* pos_ids, float* out, int64_t n_tok, int seq,
+                         int pos_off, int d, int vocab, int n_ctx, int32_t* err_flag,
+                         gbx_stream_t stream)
+{
+    const int wt = dtype_index(wte_dtype), pt = dtype_index(wpe_dtype);
+    if (wt < 0 || pt < 0)
+        return set_error(GBX_EDTYPE, "gbx_embed: unsupported GGUF dtype (wte %d, wpe %d)", wte_dtype, wpe_dtype);
+    if (n_tok < 0 || d <= 0 || vocab <= 0 || n_ctx <= 0)
+        return set_error(GBX_EINVAL, "gbx_embed: n_tok=%lld d=%d vocab=%d n_ctx=%d", (long long)n_tok, d, vocab, n_ctx);
+    if (n_tok == 0) return GBX_OK;
+    if (!ids || !wte || !wpe || !out) return set_error(GBX_EINVAL, "gbx_embed: null pointer");
+    if (!pos_ids) {
+        if (seq <= 0) return set_error(GBX_EINVAL, "gbx_embed: seq=%d", seq);
+        const int64_t span = n_tok < seq ? n_tok : seq;
+        if (pos_off < 0 || (int64_t)pos_off + span > n_ctx)
+            return set_error(GBX_ERANGE, "gbx_embed: positions [%d, %lld) exceed n_ctx=%d", pos_off,
+                             (long long)pos_off + span, n_ctx);
+    } else if (seq <= 0) {
+        seq = 1;
+    }
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (wt) {
+    case TF32: return launch_embed_p<TF32>(pt, ids, wte, wpe, pos_ids, out, n_tok, seq, pos_off, d, vocab, n_ctx, err_flag, s);
+    case TF16: return launch_embed_p<TF16>(pt, ids, wte, wpe, pos_ids, out, n_tok, seq, pos_off, d, vocab, n_ctx, err_flag, s);
+    default: return launch_embed_p<TBF16>(pt, ids, wte, wpe, pos_ids, out, n_tok, seq, pos_off, d, vocab, n_ctx, err_flag, s);
+    }
+}

@@ -1,0 +1,113 @@
+// gbx_common.cuh -- shared device helpers and launcher plumbing for the
+// sm_100a hot-path kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gbx.h"
+
+namespace gbx {
+
+// ---------------------------------------------------------------------------
+// Status reporting (status.cu).  set_error records a one-line reason for the
+// calling host thread and returns `code`, so launchers can `return set_error(...)`.
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);   // cudaGetLastError -> GBX_ECUDA + message
+void clear_error();
+
+// Per-device properties cached once per process (thread-safe).
+struct DeviceInfo {
+    int sm_count;
+    int max_smem_optin;   // bytes of dynamic+static smem one CTA may opt into
+};
+int device_info(DeviceInfo* out);   // for the current device; returns GBX_OK / GBX_ECUDA
+
+// Grid size for a grid-stride kernel: `waves` full waves of resident CTAs,
+// never more CTAs than there are work blocks.
+template <class K>
+inline int persistent_grid(K kernel, int block, size_t smem, int64_t work_blocks, int waves = 1)
+{
+    DeviceInfo di;
+    if (device_info(&di) != GBX_OK) return -1;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, block, smem) != cudaSuccess || occ < 1)
+        occ = 1;
+    int64_t g = (int64_t)di.sm_count * occ * waves;
+    if (g > work_blocks) g = work_blocks;
+    if (g < 1) g = 1;
+    if (g > 0x7fffffff) g = 0x7fffffff;
+    return (int)g;
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Memory access.  Activations are streamed exactly once per kernel, so loads
+// do not allocate in L1 and stores are marked evict-first.  The coherent
+// (not .nc) load is used because in-place calls write the buffer they read.
+// In-place calls are safe: every value a thread stores depends on the values
+// it loaded from the same addresses, so no store can be ordered before the
+// load it overwrites, and no element is read after it is written.
+__device__ __forceinline__ float4 ld_stream(const float* p)
+{
+    float4 v;
+    asm("ld.global.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+        : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+        : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream(float* p, float4 v)
+{
+    asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};"
+                 :: "l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w));
+}
+
+// Read-only parameters (gamma, beta, bias rows, small tables): cached path.
+__device__ __forceinline__ float4 ld_param4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// ---------------------------------------------------------------------------
+// Division by a run-time constant without a hardware divide (Granlund-
+// Montgomery round-up method): for 0 <= n < 2^32 and 1 <= d < 2^31,
+// q = (umulhi(n, m) + n) >> s with s = ceil(log2 d), m = floor(2^32 (2^s - d) / d) + 1.
+struct FastDiv {
+    uint32_t d, m, s;
+};
+
+inline FastDiv make_fastdiv(uint32_t d)
+{
+    FastDiv f;
+    f.d = d;
+    uint32_t s = 0;
+    while ((1ull << s) < d) ++s;
+    f.s = s;
+    f.m = (uint32_t)((((1ull << s) - d) << 32) / d + 1);
+    return f;
+}
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, FastDiv f)
+{
+    uint64_t t = (uint64_t)__umulhi(n, f.m) + n;
+    return (uint32_t)(t >> f.s);
+}
+
+// ---------------------------------------------------------------------------
+// Reductions across `TPR` consecutive lanes (TPR a power of two <= 32).
+template <int TPR>
+__device__ __forceinline__ float group_sum(float v)
+{
+#pragma unroll
+    for (int o = TPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <int TPR>
+__device__ __forceinline__ float group_max(float v)
+{
+#pragma unroll
+    for (int o = TPR / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+}  // namespace gbx

@@ -1,0 +1,137 @@
+/*
+ * gbx.h -- C ABI of the B200 (sm_100a) layer-kernel hot path for
+ * GlassBoxAI-Transformer: token+position embedding gather/add from GGUF
+ * f32/f16/bf16 tables, residual-add + LayerNorm, bias + GELU(tanh), and the
+ * row softmax.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer argument is a DEVICE pointer unless its name ends in
+ *     `_host`.  Callers own every buffer; nothing here allocates per call.
+ *   - Work is enqueued asynchronously on `stream` (NULL = the legacy default
+ *     stream, which is what the reference uses).  Entry points are stateless
+ *     and safe to call from several host threads at once.
+ *   - Return GBX_OK (0) or a GBX_E* code; they never exit the process
+ *     (the reference's CUDA_CHECK prints and calls exit(1),
+ *     transformer.cu:24-32).  gbx_last_error() gives a one-line reason,
+ *     per host thread.
+ *   - dtype codes are GGUF's: 0 = f32, 1 = f16, 30 = bf16
+ *     (transformer.cu:635-650 accepts exactly these three).
+ *   - Rows are contiguous (row stride = row length).  Outputs may alias the
+ *     matching input where stated; rows are processed whole, so aliasing is
+ *     safe exactly as stated.
+ *   - Fast paths need 16-byte aligned pointers and a row length that is a
+ *     multiple of 4 floats (8 elements for the embed tables); other shapes
+ *     run a slower general kernel on the GPU with the same results.
+ */
+#ifndef GBX_H
+#define GBX_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st* gbx_stream_t; /* identical to cudaStream_t */
+
+enum {
+    GBX_OK = 0,
+    GBX_EINVAL = 1,    /* bad argument: null pointer, negative size, forbidden alias */
+    GBX_EDTYPE = 2,    /* dtype code other than 0 / 1 / 30 */
+    GBX_ERANGE = 3,    /* a size or position beyond what the call supports */
+    GBX_ECUDA = 4,     /* the CUDA runtime reported an error (launch or copy) */
+    GBX_EIO = 5,       /* file could not be opened / read / parsed */
+    GBX_ENOTFOUND = 6, /* no tensor under any of the given names */
+    GBX_ENOMEM = 7     /* device or host allocation failed (model set-up only) */
+};
+
+enum { GBX_DT_F32 = 0, GBX_DT_F16 = 1, GBX_DT_BF16 = 30 };
+
+/* Bits set in *err_flag by gbx_embed (device int32, OR-ed in). */
+enum { GBX_EMBED_BAD_ID = 1, GBX_EMBED_BAD_POS = 2 };
+
+/* Library version, major*10000 + minor*100 + patch. */
+int gbx_version(void);
+/* Static name of a status code. */
+const char* gbx_status_string(int status);
+/* Detail of the last failing call made by this host thread ("" if none). */
+const char* gbx_last_error(void);
+
+/*
+ * GGUF tensor decode to fp32 on the device, bit-identical to the reference's
+ * host dequant GGUFLoader::loadTensorByIndex (transformer.cu:635-650) with
+ * float16ToFloat32 (:508-527: -0 -> +0, every NaN -> 0x7fc00000, subnormals
+ * exact) and bfloat16ToFloat32 (:529-534: bits << 16).  n elements.
+ * Replaces the host loop behind GGUFLoader::getTensorGPU (:676-695).
+ */
+int gbx_dequant(const void* src, int dtype, float* dst, int64_t n, gbx_stream_t stream);
+
+/*
+ * Token + position embedding, replacing embedTokensKernel / embedTokens
+ * (transformer.cu:175-185, 805-815):
+ *   out[t*d + i] = dec(wte[ids[t]*d + i]) + dec(wpe[pos(t)*d + i])
+ * with dec() the reference decode above and one fp32 add (bit-exact with the
+ * reference).  The tables stay in their GGUF dtype on the device (no fp32
+ * copy).  pos(t) = pos_ids ? pos_ids[t] : pos_off + (t % seq); `seq` is the
+ * sequence length of a batch of n_tok/seq sequences (the reference has one
+ * sequence, pos = t).  Tokens whose id is outside [0, vocab) or whose
+ * position is outside [0, n_ctx) get an all-zero row, and the matching
+ * GBX_EMBED_* bit is OR-ed into *err_flag (a device int32; may be NULL).
+ * The reference reads out of bounds in that case.  Without pos_ids the
+ * position range is checked on the host (GBX_ERANGE).
+ * out: [n_tok, d] fp32; wte: [vocab, d]; wpe: [n_ctx, d].
+ */
+int gbx_embed(const int32_t* ids, const void* wte, int wte_dtype, const void* wpe, int wpe_dtype,
+              const int32_t* pos_ids, float* out, int64_t n_tok, int seq, int pos_off, int d,
+              int vocab, int n_ctx, int32_t* err_flag, gbx_stream_t stream);
+
+/*
+ * LayerNorm over rows of length d, replacing layerNormKernel
+ * (transformer.cu:77-124, launched at :828, :868, :896):
+ *   mean = sum(x)/d; var = sum((x-mean)^2)/d; inv = rsqrtf(var + eps);
+ *   y = ((x - mean) * inv) * gamma + beta
+ * gamma / beta may be NULL (treated as 1 / 0, as at :120-121).  y may alias x.
+ */
+int gbx_layernorm(const float* x, float* y, const float* gamma, const float* beta, int64_t rows,
+                  int d, float eps, gbx_stream_t stream);
+
+/*
+ * Fused residual add + LayerNorm.  Replaces the residual epilogue of
+ * projectionKernel / ffnDownKernel (transformer.cu:262, :292:
+ * out = residual + (bias + sum)) followed by the next layerNormKernel:
+ *   h = r + (x + xbias)      (xbias: optional per-column bias of the
+ *                             sublayer output, may be NULL)
+ *   y = LayerNorm(h) as in gbx_layernorm
+ * h_out may be NULL (h not stored) and may alias r or x; y may alias x or r;
+ * h_out and y must differ.  Each row is read once and written once.
+ */
+int gbx_residual_layernorm(const float* x, const float* r, const float* xbias, float* h_out,
+                           float* y, const float* gamma, const float* beta, int64_t rows, int d,
+                           float eps, gbx_stream_t stream);
+
+/*
+ * Bias + GELU(tanh), replacing the ffnUpKernel epilogue
+ * (transformer.cu:272, 276-277) and geluKernel (:68-75):
+ *   u = in + bias[col]        (bias may be NULL: u = in)
+ *   out = u * (0.5f * (1.0f + tanhf(0.7978845608f * (u + 0.044715f*u*u*u))))
+ * in/out: [rows, F]; out may alias in.
+ */
+int gbx_bias_gelu(const float* in, float* out, const float* bias, int64_t rows, int F,
+                  gbx_stream_t stream);
+
+/*
+ * Row softmax over rows of length L, replacing softmaxKernel
+ * (transformer.cu:126-166; the reference launches it once per head,
+ * :839-842; here all rows of all heads and sequences go in one call):
+ *   m = max(-1e30f, row); e = expf(x - m); out = e / sum(e)
+ * Entries masked with -1e9f (the reference's causal-mask value,
+ * transformer.cu:221) come out as exactly 0.  out may alias in.
+ */
+int gbx_softmax_rows(const float* in, float* out, int64_t rows, int L, gbx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GBX_H */

@@ -1,0 +1,365 @@
+"""Parity of the sm_100a kernels (called through the C ABI) with the oracle.
+
+Bar: embed and dequant bit-exact; LayerNorm / residual+LayerNorm / GELU /
+softmax within |a-b| <= 1e-6 + 1e-5*|b| in fp32 (assert_close).
+Every output is written into the middle of a larger buffer whose guard rows
+hold a NaN canary, and the guards are checked afterwards.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_bits_equal, assert_close
+
+pytestmark = pytest.mark.gpu
+
+CANARY = np.uint32(0x7FBADBAD)   # a NaN no kernel produces
+
+
+def _guarded(shape, torch):
+    """Device buffer with one guard row before and after; returns (full, view)."""
+    rows, cols = shape
+    full = torch.empty((rows + 2, cols), dtype=torch.float32, device="cuda")
+    full.view(torch.int32).fill_(int(CANARY.view(np.int32)))
+    return full, full[1:rows + 1]
+
+
+def _check_guards(full):
+    h = full.cpu().numpy().view(np.uint32)
+    assert np.all(h[0] == CANARY) and np.all(h[-1] == CANARY), "write outside the output rows"
+
+
+def _t(a, torch):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    elif a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return torch.from_numpy(a).cuda()
+
+
+# ---------------------------------------------------------------------------
+# dequant
+
+@pytest.mark.parametrize("dtype", [1, 30])
+def test_dequant_every_pattern_bit_exact(gbx, orc, cuda, dtype):
+    import torch
+    pat = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    out = torch.empty(65536, dtype=torch.float32, device="cuda")
+    gbx.dequant(_t(pat, torch), dtype, out, 65536)
+    assert_bits_equal(out.cpu().numpy(), orc.dequant(pat, dtype), f"dequant dtype {dtype}")
+
+
+@pytest.mark.parametrize("dtype", [0, 1, 30])
+def test_dequant_unaligned_and_ragged(gbx, orc, cuda, dtype):
+    import torch
+    rng = np.random.default_rng(5)
+    n = 1003
+    raw = rng.integers(0, 2**16, n + 8, dtype=np.uint32).astype(np.uint16)
+    if dtype == 0:
+        raw = rng.integers(0, 2**32, n + 8, dtype=np.uint64).astype(np.uint32)
+    src = _t(raw, torch)
+    out = torch.empty(n + 3, dtype=torch.float32, device="cuda")
+    # 1-element offsets on both sides force the general (scalar) path
+    es = 4 if dtype == 0 else 2
+    gbx.dequant(src.data_ptr() + es, dtype, out.data_ptr() + 4, n)
+    ref = orc.dequant(raw[1:n + 1], dtype)
+    assert_bits_equal(out.cpu().numpy()[1:n + 1], ref, "unaligned dequant")
+
+
+def test_dequant_rejects_bad_dtype(gbx, cuda):
+    import torch
+    x = torch.zeros(16, device="cuda")
+    with pytest.raises(gbx.GbxError) as e:
+        gbx.dequant(x, 2, x, 4)
+    assert e.value.status == 2
+
+
+# ---------------------------------------------------------------------------
+# embed
+
+def _table(rng, rows, d, dtype, scale):
+    vals = (scale * rng.standard_normal((rows, d))).astype(np.float32)
+    if dtype == 0:
+        return vals
+    if dtype == 1:
+        return vals.astype(np.float16).view(np.uint16)
+    u = vals.view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("wdt,pdt", [(0, 0), (1, 1), (30, 30), (1, 0), (30, 1), (0, 30)])
+@pytest.mark.parametrize("d", [768, 1600, 64, 12, 1028])
+def test_embed_bit_exact(gbx, orc, cuda, wdt, pdt, d):
+    import torch
+    rng = np.random.default_rng(d * 100 + wdt + pdt)
+    V, C, B, S = 301, 40, 3, 17
+    wte = _table(rng, V, d, wdt, 0.02)
+    wpe = _table(rng, C, d, pdt, 0.01)
+    ids = rng.integers(0, V, B * S).astype(np.int32)
+    if wdt != 0:   # plant decode specials in rows that are gathered
+        for j, p in enumerate([0x8000, 0x7C01, 0xFC00, 0x0001, 0x83FF, 0xFFC1]):
+            wte[ids[j], j % d] = p
+    full, out = _guarded((B * S, d), torch)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.embed(_t(ids, torch), _t(wte, torch), wdt, _t(wpe, torch), pdt, out, n_tok=B * S, d=d, vocab=V,
+              n_ctx=C, seq=S, pos_off=5, err_flag=err)
+    ref, bad = orc.embed(ids, wte, wdt, wpe, pdt, d, V, C, seq=S, pos_off=5)
+    assert bad == 0 and int(err.item()) == 0
+    assert_bits_equal(out.cpu().numpy(), ref, f"embed {wdt}/{pdt} d={d}")
+    _check_guards(full)
+
+
+def test_embed_f32_specials_canonical_nan(gbx, orc, cuda):
+    import torch
+    rng = np.random.default_rng(9)
+    V, C, d, n = 8, 4, 16, 4
+    wte = rng.standard_normal((V, d)).astype(np.float32)
+    wpe = rng.standard_normal((C, d)).astype(np.float32)
+    wte[1, 0] = np.array([0x7FA00001], np.uint32).view(np.float32)[0]
+    wte[2, 1] = -0.0; wpe[1, 1] = -0.0
+    wte[3, 2] = np.inf; wpe[2, 2] = -np.inf
+    ids = np.array([1, 2, 3, 0], np.int32)
+    out = torch.empty((n, d), device="cuda")
+    gbx.embed(_t(ids, torch), _t(wte, torch), 0, _t(wpe, torch), 0, out, n_tok=n, d=d, vocab=V, n_ctx=C)
+    ref, _ = orc.embed(ids, wte, 0, wpe, 0, d, V, C)
+    got = out.cpu().numpy()
+    assert_bits_equal(got, ref)
+    assert got.view(np.uint32)[0, 0] == 0x7FFFFFFF and got.view(np.uint32)[1, 1] == 0x80000000
+
+
+def test_embed_out_of_range_ids_and_positions(gbx, orc, cuda):
+    import torch
+    rng = np.random.default_rng(11)
+    V, C, d = 50, 10, 32
+    wte = rng.standard_normal((V, d)).astype(np.float32)
+    wpe = rng.standard_normal((C, d)).astype(np.float32)
+    ids = np.array([0, 49, 50, -1, 7, 3], np.int32)
+    pos = np.array([0, 9, 1, 2, 10, -3], np.int32)
+    for dd, wt, pt in ((d, wte, wpe), (d - 3, wte[:, :d - 3].copy(), wpe[:, :d - 3].copy())):
+        out = torch.full((6, dd), 7.0, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        gbx.embed(_t(ids, torch), _t(wt, torch), 0, _t(pt, torch), 0, out, n_tok=6, d=dd, vocab=V, n_ctx=C,
+                  pos_ids=_t(pos, torch), err_flag=err)
+        ref, bad = orc.embed(ids, wt, 0, pt, 0, dd, V, C, pos_ids=pos)
+        assert bad == 4
+        assert int(err.item()) == (gbx.EMBED_BAD_ID | gbx.EMBED_BAD_POS)
+        assert_bits_equal(out.cpu().numpy(), ref)
+
+
+def test_embed_host_position_check(gbx, cuda):
+    import torch
+    x = torch.zeros((4, 8), device="cuda")
+    ids = torch.zeros(4, dtype=torch.int32, device="cuda")
+    with pytest.raises(gbx.GbxError) as e:
+        gbx.embed(ids, x, 0, x, 0, x, n_tok=4, d=8, vocab=4, n_ctx=4, seq=4, pos_off=1)
+    assert e.value.status == 3
+
+
+def test_embed_decode_position_2047(gbx, orc, cuda):
+    """Decode-step shape: B sequences of one token each at position 2047."""
+    import torch
+    rng = np.random.default_rng(12)
+    V, C, d, B = 1000, 2048, 1600, 64
+    wte = _table(rng, V, d, 30, 0.02)
+    wpe = _table(rng, C, d, 30, 0.02)
+    ids = rng.integers(0, V, B).astype(np.int32)
+    out = torch.empty((B, d), device="cuda")
+    gbx.embed(_t(ids, torch), _t(wte, torch), 30, _t(wpe, torch), 30, out, n_tok=B, d=d, vocab=V, n_ctx=C,
+              seq=1, pos_off=2047)
+    ref, _ = orc.embed(ids, wte, 30, wpe, 30, d, V, C, seq=1, pos_off=2047)
+    assert_bits_equal(out.cpu().numpy(), ref)
+
+
+# ---------------------------------------------------------------------------
+# LayerNorm and residual + LayerNorm
+
+LN_DIMS = [1, 3, 4, 5, 8, 64, 100, 132, 768, 772, 1024, 1600, 2048, 4096, 8192, 8196, 12000]
+
+
+def _ln_params(rng, d, with_params):
+    if not with_params:
+        return None, None
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(d)).astype(np.float32)
+    return g, b
+
+
+@pytest.mark.parametrize("d", LN_DIMS)
+@pytest.mark.parametrize("rows", [1, 37])
+def test_layernorm(gbx, orc, cuda, d, rows):
+    import torch
+    rng = np.random.default_rng(d + rows)
+    x = (3.0 * rng.standard_normal((rows, d)) + 0.5).astype(np.float32)
+    g, b = _ln_params(rng, d, True)
+    full, y = _guarded((rows, d), torch)
+    gbx.layernorm(_t(x, torch), y, _t(g, torch), _t(b, torch), rows=rows, d=d)
+    assert_close(y.cpu().numpy(), orc.layernorm(x, g, b), what=f"layernorm d={d}")
+    _check_guards(full)
+
+
+@pytest.mark.parametrize("d", [768, 1600, 5])
+def test_layernorm_null_params_and_in_place(gbx, orc, cuda, d):
+    import torch
+    rng = np.random.default_rng(d)
+    x = rng.standard_normal((9, d)).astype(np.float32)
+    xd = _t(x, torch)
+    gbx.layernorm(xd, xd, None, None, rows=9, d=d, eps=1e-5)
+    assert_close(xd.cpu().numpy(), orc.layernorm(x, None, None), what="in-place, no gamma/beta")
+    g, b = _ln_params(rng, d, True)
+    xd = _t(x, torch)
+    gbx.layernorm(xd, xd, _t(g, torch), None, rows=9, d=d, eps=1e-3)
+    assert_close(xd.cpu().numpy(), orc.layernorm(x, g, None, eps=1e-3), what="gamma only, eps 1e-3")
+
+
+@pytest.mark.parametrize("d", LN_DIMS)
+def test_residual_layernorm(gbx, orc, cuda, d):
+    import torch
+    rng = np.random.default_rng(7 * d)
+    rows = 19
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    r = (2 * rng.standard_normal((rows, d))).astype(np.float32)
+    g, b = _ln_params(rng, d, True)
+    fh, h = _guarded((rows, d), torch)
+    fy, y = _guarded((rows, d), torch)
+    gbx.residual_layernorm(_t(x, torch), _t(r, torch), h, y, _t(g, torch), _t(b, torch), rows=rows, d=d)
+    h_ref, y_ref = orc.residual_layernorm(x, r, g, b)
+    assert_bits_equal(h.cpu().numpy(), h_ref, "residual sum")
+    assert_close(y.cpu().numpy(), y_ref, what=f"residual layernorm d={d}")
+    _check_guards(fh)
+    _check_guards(fy)
+
+
+@pytest.mark.parametrize("d", [1024, 1600, 772, 6])
+def test_residual_layernorm_aliasing_and_xbias(gbx, orc, cuda, d):
+    import torch
+    rng = np.random.default_rng(3 * d)
+    rows = 11
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    r = rng.standard_normal((rows, d)).astype(np.float32)
+    xb = (0.05 * rng.standard_normal(d)).astype(np.float32)
+    g, b = _ln_params(rng, d, True)
+    xpb = (x + xb[None, :]).astype(np.float32)
+    h_ref, y_ref = orc.residual_layernorm(xpb, r, g, b)
+    # h written over r (the residual stream updated in place), y over x
+    xd, rd = _t(x, torch), _t(r, torch)
+    gbx.residual_layernorm(xd, rd, rd, xd, _t(g, torch), _t(b, torch), rows=rows, d=d, xbias=_t(xb, torch))
+    assert_bits_equal(rd.cpu().numpy(), h_ref, "h over r")
+    assert_close(xd.cpu().numpy(), y_ref, what="y over x")
+    # h not stored
+    xd, rd = _t(x, torch), _t(r, torch)
+    y = torch.empty((rows, d), device="cuda")
+    gbx.residual_layernorm(xd, rd, None, y, _t(g, torch), _t(b, torch), rows=rows, d=d, xbias=_t(xb, torch))
+    assert_close(y.cpu().numpy(), y_ref, what="no h_out")
+    assert_bits_equal(rd.cpu().numpy(), r, "r untouched")
+
+
+def test_residual_layernorm_rejects_h_equal_y(gbx, cuda):
+    import torch
+    a = torch.zeros((2, 8), device="cuda")
+    with pytest.raises(gbx.GbxError) as e:
+        gbx.residual_layernorm(a, a, a, a, None, None, rows=2, d=8)
+    assert e.value.status == 1
+
+
+# ---------------------------------------------------------------------------
+# bias + GELU
+
+@pytest.mark.parametrize("F", [1, 3, 4, 64, 100, 3072, 4096, 6400, 16384])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_bias_gelu(gbx, orc, cuda, F, with_bias):
+    import torch
+    rng = np.random.default_rng(F + with_bias)
+    rows = 13
+    x = (2 * rng.standard_normal((rows, F))).astype(np.float32)
+    bias = (0.02 * rng.standard_normal(F)).astype(np.float32) if with_bias else None
+    full, out = _guarded((rows, F), torch)
+    gbx.bias_gelu(_t(x, torch), out, _t(bias, torch) if with_bias else None, rows=rows, F=F)
+    assert_close(out.cpu().numpy(), orc.bias_gelu(x, bias), what=f"gelu F={F}")
+    _check_guards(full)
+
+
+def test_gelu_sweep_specials_in_place(gbx, orc, cuda):
+    import torch
+    x = np.concatenate([np.linspace(-12, 12, 8185, dtype=np.float32),
+                        np.array([0.0, -0.0, np.inf, -np.inf, 1e-40, -1e-40, np.nan], np.float32)]).reshape(1, -1)
+    xd = _t(x, torch)
+    gbx.bias_gelu(xd, xd, None, rows=1, F=x.shape[1])
+    assert_close(xd.cpu().numpy(), orc.bias_gelu(x, None), what="gelu sweep")
+
+
+# ---------------------------------------------------------------------------
+# softmax
+
+@pytest.mark.parametrize("L", [1, 2, 3, 4, 33, 64, 100, 1024, 1028, 2048, 4096, 8192, 8196, 40000])
+def test_softmax(gbx, orc, cuda, L):
+    import torch
+    rng = np.random.default_rng(L)
+    rows = 21
+    x = (1.5 * rng.standard_normal((rows, L))).astype(np.float32)
+    full, out = _guarded((rows, L), torch)
+    gbx.softmax_rows(_t(x, torch), out, rows=rows, L=L)
+    assert_close(out.cpu().numpy(), orc.softmax_rows(x), what=f"softmax L={L}")
+    _check_guards(full)
+
+
+@pytest.mark.parametrize("S", [64, 1024])
+def test_softmax_causal_in_place(gbx, orc, cuda, S):
+    import torch
+    rng = np.random.default_rng(S)
+    H = 2 if S == 1024 else 12
+    s = rng.standard_normal((H, S, S)).astype(np.float32)
+    iu = np.triu_indices(S, 1)
+    s[:, iu[0], iu[1]] = -1e9
+    sd = _t(s, torch)
+    gbx.softmax_rows(sd, sd, rows=H * S, L=S)
+    got = sd.cpu().numpy()
+    assert np.all(got[:, iu[0], iu[1]] == 0.0), "masked entries must be exactly 0"
+    assert_close(got, orc.softmax_rows(s), what=f"causal softmax S={S}")
+
+
+def test_softmax_specials(gbx, orc, cuda):
+    import torch
+    rng = np.random.default_rng(77)
+    for L in (64, 1024, 37):
+        sp = rng.standard_normal((6, L)).astype(np.float32)
+        sp[0, :] = -1e9; sp[0, 5] = 0.25
+        sp[1, 3] = -np.inf
+        sp[2, :] = -np.inf
+        sp[3, 7] = np.inf
+        sp[4, 9] = np.nan
+        sp[5, :] = 3.0
+        out = torch.empty((6, L), device="cuda")
+        gbx.softmax_rows(_t(sp, torch), out, rows=6, L=L)
+        assert_close(out.cpu().numpy(), orc.softmax_rows(sp), what=f"softmax specials L={L}")
+
+
+# ---------------------------------------------------------------------------
+# argument errors, streams
+
+def test_invalid_arguments(gbx, cuda):
+    import torch
+    a = torch.zeros((4, 8), device="cuda")
+    for call, code in ((lambda: gbx.layernorm(None, a, None, None, rows=4, d=8), 1),
+                       (lambda: gbx.layernorm(a, a, None, None, rows=-1, d=8), 1),
+                       (lambda: gbx.softmax_rows(a, a, rows=4, L=0), 1),
+                       (lambda: gbx.bias_gelu(a, None, None, rows=4, F=8), 1),
+                       (lambda: gbx.embed(a, a, 7, a, 0, a, n_tok=4, d=8, vocab=4, n_ctx=4), 2)):
+        with pytest.raises(gbx.GbxError) as e:
+            call()
+        assert e.value.status == code
+    # zero rows is a no-op, not an error
+    gbx.softmax_rows(a, a, rows=0, L=8)
+
+
+def test_runs_on_a_side_stream(gbx, orc, cuda):
+    import torch
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((300, 1024)).astype(np.float32)
+    s = torch.cuda.Stream()
+    xd = _t(x, torch)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        out = torch.empty_like(xd)
+        gbx.softmax_rows(xd, out, rows=300, L=1024, stream=s)
+    s.synchronize()
+    assert_close(out.cpu().numpy(), orc.softmax_rows(x), what="side stream")

@@ -452,6 +452,75 @@ def run_reference(args, shape, desc):
     print(json.dumps(out), flush=True)
 
 
+def run_kernel(args, shape):
+    """One hot-path kernel alone on `--rows` rows of the workload's shape
+    (token rows; softmax rows for softmax_rows), timed per launch with CUDA
+    events after the warm-up launches.  Used for sweeps and for small ncu
+    captures; prints one JSON line."""
+    import torch
+    G = importlib.import_module("glassboxai-transformer_b200")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    f32 = dict(dtype=torch.float32, device=dev)
+    R, d, F, L = args.rows, shape.d, shape.ff, shape.L
+    name = args.kernel
+    if name == "softmax_rows":
+        x = torch.randn((R, L), generator=g, **f32)
+        out = torch.empty_like(x)
+        fn = lambda: G.softmax_rows(x, out, rows=R, L=L)
+        nbytes = 8 * R * L
+    elif name in ("layernorm", "residual_layernorm"):
+        x = torch.randn((R, d), generator=g, **f32)
+        r = torch.randn((R, d), generator=g, **f32)
+        h = torch.empty_like(x)
+        y = torch.empty_like(x)
+        gam = 1 + 0.1 * torch.randn((d,), generator=g, **f32)
+        bet = 0.02 * torch.randn((d,), generator=g, **f32)
+        if name == "layernorm":
+            fn = lambda: G.layernorm(x, y, gam, bet, rows=R, d=d)
+            nbytes = 8 * R * d + 8 * d
+        else:
+            fn = lambda: G.residual_layernorm(x, r, h, y, gam, bet, rows=R, d=d)
+            nbytes = 16 * R * d + 8 * d
+    elif name == "bias_gelu":
+        x = torch.randn((R, F), generator=g, **f32)
+        out = torch.empty_like(x)
+        bias = 0.02 * torch.randn((F,), generator=g, **f32)
+        fn = lambda: G.bias_gelu(x, out, bias, rows=R, F=F)
+        nbytes = 8 * R * F + 4 * F
+    elif name == "embed":
+        es = shape.table_es()
+        tdt = {0: torch.float32, 1: torch.float16, 30: torch.bfloat16}[shape.table_dtype]
+        wte = (0.02 * torch.randn((shape.vocab, d), generator=g, **f32)).to(tdt)
+        wpe = (0.02 * torch.randn((shape.n_ctx, d), generator=g, **f32)).to(tdt)
+        seq = min(shape.seq, R)
+        ids = torch.randint(0, shape.vocab, (R,), generator=g, dtype=torch.int32, device=dev)
+        out = torch.empty((R, d), **f32)
+        fn = lambda: G.embed(ids, wte, shape.table_dtype, wpe, shape.table_dtype, out, n_tok=R, d=d,
+                             vocab=shape.vocab, n_ctx=shape.n_ctx, seq=seq, pos_off=shape.pos_off)
+        nbytes = 4 * R + R * d * es + min(seq, shape.n_ctx) * d * es + 4 * R * d
+    else:
+        raise SystemExit(f"unknown kernel {name}")
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in evs:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    us = [1000.0 * a.elapsed_time(b) for a, b in evs]
+    peak, kind = load_peak()
+    med = statistics.median(us)
+    print(json.dumps({"kernel": name, "workload": args.workload, "rows": R, "launches": len(us),
+                      "median_us": med, "min_us": min(us), "bytes_per_launch": nbytes,
+                      "gbs": nbytes / (med * 1e-6) / 1e9, "frac": nbytes / (med * 1e-6) / 1e9 / peak,
+                      "peak": peak, "peak_kind": kind}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -461,6 +530,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--kernel", choices=["embed", "layernorm", "residual_layernorm", "softmax_rows", "bias_gelu"],
+                    help="time one kernel alone on --rows rows of the workload's shape")
+    ap.add_argument("--rows", type=int, default=65536)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -469,7 +541,9 @@ def main():
     shape_kw, desc, chain_kw = WORKLOADS[args.workload]
     chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
     shape = chain_mod.ChainShape(**shape_kw)
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel(args, shape)
+    elif args.impl == "reference":
         run_reference(args, shape, desc)
     else:
         run_ours(args, shape, desc, chain_kw)

@@ -49,6 +49,7 @@ SIGNATURES = {
     "gbx_residual_layernorm": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
     "gbx_bias_gelu": [_vp, _vp, _vp, _i64, _int, _vp],
     "gbx_softmax_rows": [_vp, _vp, _i64, _int, _vp],
+    "gbx_attn_softmax_rows": [_vp, _vp, _i64, _int, _int, _int, _f, _int, _vp],
 }
 _RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
 
@@ -130,3 +131,8 @@ def bias_gelu(x, out, bias, *, rows, F, stream=None):
 
 def softmax_rows(x, out, *, rows, L, stream=None):
     _check(lib().gbx_softmax_rows(_p(x), _p(out), rows, L, _stream(stream)))
+
+
+def attn_softmax_rows(scores, probs, *, rows, L, S, scale, q_off=0, causal=True, stream=None):
+    _check(lib().gbx_attn_softmax_rows(_p(scores), _p(probs), rows, L, S, q_off, scale, 1 if causal else 0,
+                                       _stream(stream)))

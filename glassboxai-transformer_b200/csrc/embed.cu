@@ -2,10 +2,10 @@
 // gather/add (replaces GGUFLoader's host dequant, transformer.cu:508-534 and
 // :635-650, and embedTokensKernel, transformer.cu:175-185).
 //
-// The tables stay in their GGUF encoding in HBM; each 16-byte load brings 8
-// f16/bf16 elements (or 4 f32), which are decoded in registers with the
-// reference's exact rules and added in fp32.  Output rows are written with
-// streaming 16-byte stores.
+// The tables stay in their GGUF encoding in HBM; each load brings 4 elements
+// (8 bytes of f16/bf16, 16 bytes of f32), which are decoded in registers with
+// the reference's exact rules and added in fp32.  Output rows are written
+// with streaming 16-byte stores.
 #include "gbx_common.cuh"
 
 namespace gbx {
@@ -29,32 +29,19 @@ __device__ __forceinline__ uint32_t f16_to_f32_bits(uint32_t h)
 
 __device__ __forceinline__ float f16_to_f32(uint32_t h) { return __uint_as_float(f16_to_f32_bits(h)); }
 
-// Decode the 8 consecutive elements starting at element `e` (a multiple of 8)
-// of a table of type T.  16-byte aligned by construction.
+// Decode the 4 consecutive elements starting at element `e` (a multiple of 4)
+// of a table of type T: one 16-byte load for f32, one 8-byte load for
+// f16/bf16 (aligned by construction: rows are a multiple of 4 elements).
 template <int T>
-__device__ __forceinline__ void load8(const void* base, int64_t e, float (&v)[8])
+__device__ __forceinline__ float4 load4(const void* base, int64_t e)
 {
-    if (T == TF32) {
-        const float* p = static_cast<const float*>(base) + e;
-        float4 a = __ldg(reinterpret_cast<const float4*>(p));
-        float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    } else {
-        const uint16_t* p = static_cast<const uint16_t*>(base) + e;
-        uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
-        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            if (T == TF16) {
-                v[2 * k] = f16_to_f32(ws[k] & 0xffffu);
-                v[2 * k + 1] = f16_to_f32(ws[k] >> 16);
-            } else {
-                v[2 * k] = __uint_as_float(ws[k] << 16);
-                v[2 * k + 1] = __uint_as_float(ws[k] & 0xffff0000u);
-            }
-        }
-    }
+    if (T == TF32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(base) + e));
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + e));
+    if (T == TF16)
+        return make_float4(f16_to_f32(w.x & 0xffffu), f16_to_f32(w.x >> 16), f16_to_f32(w.y & 0xffffu),
+                           f16_to_f32(w.y >> 16));
+    return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
+                       __uint_as_float(w.y & 0xffff0000u));
 }
 
 template <int T>
@@ -66,62 +53,61 @@ __device__ __forceinline__ float load1(const void* base, int64_t e)
 }
 
 // ---------------------------------------------------------------------------
-// Embedding, vector path.  Work item = (token t, 8-element chunk c); items are
-// numbered t*n8 + c so consecutive threads cover consecutive 32-byte pieces of
-// one output row.  Each thread takes kU items per pass and issues all their
-// loads before any arithmetic.
+// Embedding, vector path.  Work item = (token t, 4-element chunk c), numbered
+// t*n4 + c, so the 32 lanes of a warp read 32 consecutive 8- or 16-byte pieces
+// of table rows and write 512 consecutive bytes of output.  A full grid of
+// CTAs, each thread taking kEmbedU items spaced one CTA width apart and
+// issuing all their loads before any arithmetic.  (On B200, 8-element items
+// written as two half-coalesced stores per lane, in a persistent grid,
+// reached 68% of the copy bandwidth on a bf16 gather; this layout 92%.)
 constexpr int kEmbedThreads = 256;
 constexpr int kEmbedU = 4;
 
 template <int WT, int PT>
 __global__ void __launch_bounds__(kEmbedThreads)
-embed_vec8_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
+embed_vec4_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
                   const void* __restrict__ wpe, const int32_t* __restrict__ pos_ids,
-                  float* __restrict__ out, uint32_t total, FastDiv div_n8, FastDiv div_seq,
+                  float* __restrict__ out, uint32_t total, FastDiv div_n4, FastDiv div_seq,
                   int pos_off, int d, int vocab, int n_ctx, int32_t* __restrict__ err)
 {
-    const uint32_t n8 = div_n8.d;
+    const uint32_t n4 = div_n4.d;
     const uint32_t seq = div_seq.d;
-    const uint32_t stride = gridDim.x * (uint32_t)kEmbedThreads * kEmbedU;
-    for (uint32_t base = blockIdx.x * (uint32_t)kEmbedThreads * kEmbedU + threadIdx.x; base < total;
-         base += stride) {
-        int32_t tok[kEmbedU], col[kEmbedU], id[kEmbedU], pos[kEmbedU];
+    const uint32_t base = blockIdx.x * (uint32_t)(kEmbedThreads * kEmbedU) + threadIdx.x;
+    uint32_t tok[kEmbedU], col[kEmbedU];
+    int32_t id[kEmbedU], pos[kEmbedU];
 #pragma unroll
-        for (int u = 0; u < kEmbedU; ++u) {
-            uint32_t i = base + u * kEmbedThreads;
-            uint32_t t = fast_div(i < total ? i : 0, div_n8);
-            tok[u] = (int32_t)t;
-            col[u] = (int32_t)((i < total ? i : 0) - t * n8);
-            id[u] = i < total ? __ldg(ids + t) : 0;
-            pos[u] = pos_ids ? (i < total ? __ldg(pos_ids + t) : 0)
-                             : pos_off + (int32_t)(t - fast_div(t, div_seq) * seq);
+    for (int u = 0; u < kEmbedU; ++u) {
+        const uint32_t i = base + u * kEmbedThreads;
+        const uint32_t ii = i < total ? i : 0;
+        const uint32_t t = fast_div(ii, div_n4);
+        tok[u] = t;
+        col[u] = ii - t * n4;
+        id[u] = __ldg(ids + t);
+        pos[u] = pos_ids ? __ldg(pos_ids + t) : pos_off + (int32_t)(t - fast_div(t, div_seq) * seq);
+    }
+    float4 a[kEmbedU], b[kEmbedU];
+#pragma unroll
+    for (int u = 0; u < kEmbedU; ++u) {
+        const bool ok = (uint32_t)id[u] < (uint32_t)vocab && (uint32_t)pos[u] < (uint32_t)n_ctx;
+        if (base + u * kEmbedThreads < total && ok) {
+            a[u] = load4<WT>(wte, (int64_t)id[u] * d + 4 * col[u]);
+            b[u] = load4<PT>(wpe, (int64_t)pos[u] * d + 4 * col[u]);
+        } else {
+            a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            b[u] = a[u];
         }
-        float a[kEmbedU][8], b[kEmbedU][8];
+    }
 #pragma unroll
-        for (int u = 0; u < kEmbedU; ++u) {
-            const bool ok = (uint32_t)id[u] < (uint32_t)vocab && (uint32_t)pos[u] < (uint32_t)n_ctx;
-            if (base + u * kEmbedThreads < total && ok) {
-                load8<WT>(wte, (int64_t)id[u] * d + col[u] * 8, a[u]);
-                load8<PT>(wpe, (int64_t)pos[u] * d + col[u] * 8, b[u]);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) { a[u][k] = 0.0f; b[u][k] = 0.0f; }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kEmbedU; ++u) {
-            uint32_t i = base + u * kEmbedThreads;
-            if (i >= total) continue;
-            const bool bad_id = (uint32_t)id[u] >= (uint32_t)vocab;
-            const bool bad_pos = (uint32_t)pos[u] >= (uint32_t)n_ctx;
-            if ((bad_id || bad_pos) && col[u] == 0 && err)
-                atomicOr(err, (bad_id ? GBX_EMBED_BAD_ID : 0) | (bad_pos ? GBX_EMBED_BAD_POS : 0));
-            float* o = out + (int64_t)tok[u] * d + col[u] * 8;
-            // one fp32 add per element, as embedTokensKernel (transformer.cu:183);
-            // a rejected token's row is zeros (0 + 0).
-            st_stream(o, make_float4(a[u][0] + b[u][0], a[u][1] + b[u][1], a[u][2] + b[u][2], a[u][3] + b[u][3]));
-            st_stream(o + 4, make_float4(a[u][4] + b[u][4], a[u][5] + b[u][5], a[u][6] + b[u][6], a[u][7] + b[u][7]));
-        }
+    for (int u = 0; u < kEmbedU; ++u) {
+        if (base + u * kEmbedThreads >= total) continue;
+        const bool bad_id = (uint32_t)id[u] >= (uint32_t)vocab;
+        const bool bad_pos = (uint32_t)pos[u] >= (uint32_t)n_ctx;
+        if ((bad_id || bad_pos) && col[u] == 0 && err)
+            atomicOr(err, (bad_id ? GBX_EMBED_BAD_ID : 0) | (bad_pos ? GBX_EMBED_BAD_POS : 0));
+        // one fp32 add per element, as embedTokensKernel (transformer.cu:183);
+        // a rejected token's row is zeros (0 + 0).
+        st_stream(out + (int64_t)tok[u] * d + 4 * col[u],
+                  make_float4(a[u].x + b[u].x, a[u].y + b[u].y, a[u].z + b[u].z, a[u].w + b[u].w));
     }
 }
 
@@ -151,18 +137,13 @@ embed_scalar_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wt
 }
 
 // ---------------------------------------------------------------------------
-// Dequant: 8 elements per item on the vector path, scalar tail.
+// Dequant: full grid of 4-element items on the vector path, scalar tail.
 template <int T>
 __global__ void __launch_bounds__(256)
-dequant_vec8_kernel(const void* __restrict__ src, float* __restrict__ dst, int64_t n8)
+dequant_vec4_kernel(const void* __restrict__ src, float* __restrict__ dst, int64_t n4)
 {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        float v[8];
-        load8<T>(src, i * 8, v);
-        st_stream(dst + i * 8, make_float4(v[0], v[1], v[2], v[3]));
-        st_stream(dst + i * 8 + 4, make_float4(v[4], v[5], v[6], v[7]));
-    }
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n4) st_stream(dst + i * 4, load4<T>(src, i * 4));
 }
 
 template <int T>
@@ -189,20 +170,19 @@ static int launch_embed(const int32_t* ids, const void* wte, const void* wpe, co
                         float* out, int64_t n_tok, int seq, int pos_off, int d, int vocab, int n_ctx,
                         int32_t* err, cudaStream_t stream)
 {
-    const int n8 = d / 8;
-    const int64_t total = n_tok * (int64_t)n8;
-    // total < 2^31 keeps base + stride (stride < 2^31 as well) from wrapping
-    // the 32-bit item counter of the grid-stride loop.
-    const bool vec = (d % 8 == 0) && total < 0x7fffffffLL && aligned16(wte) && aligned16(wpe) &&
-                     aligned16(out);
+    const int n4 = d / 4;
+    const int64_t total = n_tok * (int64_t)n4;
+    const int es_w = WT == TF32 ? 4 : 2, es_p = PT == TF32 ? 4 : 2;
+    // 32-bit item numbers (total < 2^31) and table rows aligned for the
+    // 16-byte (f32) or 8-byte (f16/bf16) loads
+    const bool vec = (d % 4 == 0) && total < 0x7fffffffLL && aligned16(out) &&
+                     ((uintptr_t)wte % (4 * es_w)) == 0 && ((uintptr_t)wpe % (4 * es_p)) == 0;
     if (vec) {
-        auto k = embed_vec8_kernel<WT, PT>;
-        const int64_t blocks = (total + (int64_t)kEmbedThreads * kEmbedU - 1) / ((int64_t)kEmbedThreads * kEmbedU);
-        const int grid = persistent_grid(k, kEmbedThreads, 0, blocks, 2);
-        if (grid < 1) return GBX_ECUDA;
-        k<<<grid, kEmbedThreads, 0, stream>>>(ids, wte, wpe, pos_ids, out, (uint32_t)total,
-                                               make_fastdiv((uint32_t)n8), make_fastdiv((uint32_t)seq),
-                                               pos_off, d, vocab, n_ctx, err);
+        const int64_t per_cta = (int64_t)kEmbedThreads * kEmbedU;
+        const int64_t grid = (total + per_cta - 1) / per_cta;
+        embed_vec4_kernel<WT, PT><<<(unsigned)grid, kEmbedThreads, 0, stream>>>(
+            ids, wte, wpe, pos_ids, out, (uint32_t)total, make_fastdiv((uint32_t)n4), make_fastdiv((uint32_t)seq),
+            pos_off, d, vocab, n_ctx, err);
     } else {
         auto k = embed_scalar_kernel<WT, PT>;
         const int64_t total_e = n_tok * (int64_t)d;
@@ -229,13 +209,14 @@ template <int T>
 static int launch_dequant(const void* src, float* dst, int64_t n, cudaStream_t stream)
 {
     int64_t done = 0;
-    if (aligned16(src) && aligned16(dst) && n >= 8) {
-        auto k = dequant_vec8_kernel<T>;
-        const int64_t n8 = n / 8;
-        const int grid = persistent_grid(k, 256, 0, (n8 + 255) / 256, 4);
-        if (grid < 1) return GBX_ECUDA;
-        k<<<grid, 256, 0, stream>>>(src, dst, n8);
-        done = n8 * 8;
+    const int es = T == TF32 ? 4 : 2;
+    if (((uintptr_t)src % (4 * es)) == 0 && aligned16(dst) && n >= 4) {
+        const int64_t n4 = n / 4;
+        const int64_t grid = (n4 + 255) / 256;
+        if (grid <= 0x7fffffffLL) {
+            dequant_vec4_kernel<T><<<(unsigned)grid, 256, 0, stream>>>(src, dst, n4);
+            done = n4 * 4;
+        }
     }
     if (done < n) {
         auto k = dequant_scalar_kernel<T>;

@@ -4,8 +4,9 @@
 //
 // Per row: one HBM read of x (and r), h = r + x kept in registers, mean and
 // the exact two-pass population variance from registers via warp shuffles,
-// one HBM write of y (and h).  gamma/beta are staged once per CTA in shared
-// memory (the CTA then serves many rows).  The arithmetic is the reference's:
+// one HBM write of y (and h).  gamma/beta/bias rows are read through the
+// read-only path: every CTA of the full-grid launch touches the same few KB,
+// which stay in L2 and L1.  The arithmetic is the reference's:
 //   mean = sum/d; var = sum((x-mean)^2)/d (variance terms fused as the
 //   reference's nvcc build fuses them); inv = rsqrtf(var + eps);
 //   y = fmaf((x - mean) * inv, gamma, beta)
@@ -15,94 +16,79 @@
 
 namespace gbx {
 
-constexpr int kLnMaxStagedFloats = 8192;   // gamma+beta staging up to 64 KB
-
 __device__ __forceinline__ float4 f4add(float4 a, float4 b)
 {
     return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
 
 template <int TPR, int V4, bool RESID>
-__global__ void __launch_bounds__(kRowCTA)
-ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out,
-              float* y, const float* __restrict__ gamma, const float* __restrict__ beta,
-              int64_t rows, int d, float eps)
+__global__ void __launch_bounds__(RowCTA<TPR>::threads)
+ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out, float* y,
+              const float* __restrict__ gamma, const float* __restrict__ beta, int64_t rows, int d, float eps)
 {
-    constexpr int RPC = kRowCTA / TPR;
-    extern __shared__ float4 s_gb[];   // [n4] gamma, then [n4] beta
-    __shared__ float red[2][kRowCTA / 32];
-
+    __shared__ float red[2][RowCTA<TPR>::warps];
     const int n4 = d >> 2;
-    for (int i = threadIdx.x; i < n4; i += kRowCTA) {
-        s_gb[i] = gamma ? ld_param4(gamma + 4 * i) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-        s_gb[n4 + i] = beta ? ld_param4(beta + 4 * i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    }
-    __syncthreads();
-
     const int lane = threadIdx.x & (TPR - 1);
-    const int grp = threadIdx.x / TPR;
+    const int64_t row = (int64_t)blockIdx.x * RowCTA<TPR>::rows + threadIdx.x / TPR;
+    const bool valid = row < rows;
+    const int64_t off = row * d;
     const float fd = (float)d;
 
-    for (int64_t row0 = (int64_t)blockIdx.x * RPC; row0 < rows; row0 += (int64_t)gridDim.x * RPC) {
-        const int64_t row = row0 + grp;
-        const bool valid = row < rows;
-        const int64_t off = row * d;
-
-        float4 v[V4];
+    float4 v[V4];
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        const int c = k * TPR + lane;
+        v[k] = (valid && c < n4) ? ld_stream(x + off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if constexpr (RESID) {
+        float4 rv[V4];
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
             const int c = k * TPR + lane;
-            v[k] = (valid && c < n4) ? ld_stream(x + off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            rv[k] = (valid && c < n4) ? ld_stream(r + off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if constexpr (RESID) {
-            float4 rv[V4];
-#pragma unroll
-            for (int k = 0; k < V4; ++k) {
-                const int c = k * TPR + lane;
-                rv[k] = (valid && c < n4) ? ld_stream(r + off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int k = 0; k < V4; ++k) {
-                const int c = k * TPR + lane;
-                if (xbias && c < n4) v[k] = f4add(v[k], ld_param4(xbias + 4 * c));
-                v[k] = f4add(rv[k], v[k]);
-                if (h_out && valid && c < n4) st_stream(h_out + off + 4 * c, v[k]);
-            }
-        }
-
-        float s = 0.0f;
-#pragma unroll
-        for (int k = 0; k < V4; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-        s = row_sum<TPR>(s, red[0]);
-        const float mean = s / fd;
-
-        float q = 0.0f;
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
-            if (k * TPR + lane < n4) {
-                const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, e = v[k].w - mean;
-                q = fmaf(a, a, q);
-                q = fmaf(b, b, q);
-                q = fmaf(c, c, q);
-                q = fmaf(e, e, q);
-            }
+            const int c = k * TPR + lane;
+            if (xbias && c < n4) v[k] = f4add(v[k], ld_param4(xbias + 4 * c));
+            v[k] = f4add(rv[k], v[k]);
+            if (h_out && valid && c < n4) st_stream(h_out + off + 4 * c, v[k]);
         }
-        q = row_sum<TPR>(q, red[1]);
-        const float inv = rsqrtf(q / fd + eps);
+    }
 
-        if (valid) {
+    float s = 0.0f;
 #pragma unroll
-            for (int k = 0; k < V4; ++k) {
-                const int c = k * TPR + lane;
-                if (c < n4) {
-                    const float4 g = s_gb[c], b = s_gb[n4 + c];
-                    float4 o;
-                    o.x = fmaf((v[k].x - mean) * inv, g.x, b.x);
-                    o.y = fmaf((v[k].y - mean) * inv, g.y, b.y);
-                    o.z = fmaf((v[k].z - mean) * inv, g.z, b.z);
-                    o.w = fmaf((v[k].w - mean) * inv, g.w, b.w);
-                    st_stream(y + off + 4 * c, o);
-                }
+    for (int k = 0; k < V4; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    s = row_sum<TPR>(s, red[0]);
+    const float mean = s / fd;
+
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        if (k * TPR + lane < n4) {
+            const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, e = v[k].w - mean;
+            q = fmaf(a, a, q);
+            q = fmaf(b, b, q);
+            q = fmaf(c, c, q);
+            q = fmaf(e, e, q);
+        }
+    }
+    q = row_sum<TPR>(q, red[1]);
+    const float inv = rsqrtf(q / fd + eps);
+
+    if (valid) {
+#pragma unroll
+        for (int k = 0; k < V4; ++k) {
+            const int c = k * TPR + lane;
+            if (c < n4) {
+                const float4 g = gamma ? ld_param4(gamma + 4 * c) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+                const float4 b = beta ? ld_param4(beta + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                float4 o;
+                o.x = fmaf((v[k].x - mean) * inv, g.x, b.x);
+                o.y = fmaf((v[k].y - mean) * inv, g.y, b.y);
+                o.z = fmaf((v[k].z - mean) * inv, g.z, b.z);
+                o.w = fmaf((v[k].w - mean) * inv, g.w, b.w);
+                st_stream(y + off + 4 * c, o);
             }
         }
     }
@@ -113,12 +99,12 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
 // RESID and h_out is given, pass 0 materialises h there and later passes read
 // it back; without h_out, h = r + (x + xbias) is recomputed in each pass.
 template <bool RESID>
-__global__ void __launch_bounds__(kRowCTA)
+__global__ void __launch_bounds__(kGeneralCTA)
 ln_general_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out,
                   float* y, const float* __restrict__ gamma, const float* __restrict__ beta,
                   int64_t rows, int d, float eps)
 {
-    __shared__ float red[2][kRowCTA / 32];
+    __shared__ float red[2][kGeneralCTA / 32];
     const float fd = (float)d;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const int64_t off = row * d;
@@ -129,22 +115,22 @@ ln_general_kernel(const float* x, const float* r, const float* __restrict__ xbia
             return r[off + i] + xv;
         };
         if (RESID && h_out) {
-            for (int i = threadIdx.x; i < d; i += kRowCTA) {
+            for (int i = threadIdx.x; i < d; i += kGeneralCTA) {
                 const float xv = xbias ? x[off + i] + xbias[i] : x[off + i];
                 h_out[off + i] = r[off + i] + xv;
             }
             __syncthreads();
         }
         float s = 0.0f;
-        for (int i = threadIdx.x; i < d; i += kRowCTA) s += hval(i);
+        for (int i = threadIdx.x; i < d; i += kGeneralCTA) s += hval(i);
         const float mean = block_sum(s, red[0]) / fd;
         float q = 0.0f;
-        for (int i = threadIdx.x; i < d; i += kRowCTA) {
+        for (int i = threadIdx.x; i < d; i += kGeneralCTA) {
             const float diff = hval(i) - mean;
             q = fmaf(diff, diff, q);
         }
         const float inv = rsqrtf(block_sum(q, red[1]) / fd + eps);
-        for (int i = threadIdx.x; i < d; i += kRowCTA) {
+        for (int i = threadIdx.x; i < d; i += kGeneralCTA) {
             const float g = gamma ? gamma[i] : 1.0f;
             const float b = beta ? beta[i] : 0.0f;
             y[off + i] = fmaf((hval(i) - mean) * inv, g, b);
@@ -155,42 +141,35 @@ ln_general_kernel(const float* x, const float* r, const float* __restrict__ xbia
 
 template <int TPR, int V4, bool RESID>
 static int launch_ln_vec(const float* x, const float* r, const float* xbias, float* h_out, float* y,
-                         const float* g, const float* b, int64_t rows, int d, float eps,
-                         cudaStream_t stream)
+                         const float* g, const float* b, int64_t rows, int d, float eps, cudaStream_t stream)
 {
-    auto k = ln_vec_kernel<TPR, V4, RESID>;
-    const size_t smem = (size_t)2 * d * sizeof(float);
-    if (smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return check_launch("gbx_layernorm: smem attribute");
-    }
-    constexpr int RPC = kRowCTA / TPR;
-    const int grid = persistent_grid(k, kRowCTA, smem, (rows + RPC - 1) / RPC, 1);
-    if (grid < 1) return GBX_ECUDA;
-    k<<<grid, kRowCTA, smem, stream>>>(x, r, xbias, h_out, y, g, b, rows, d, eps);
-    return check_launch(RESID ? "gbx_residual_layernorm" : "gbx_layernorm");
+    const int64_t grid = row_grid<TPR>(rows);
+    if (grid < 0) return GBX_ERANGE;
+    ln_vec_kernel<TPR, V4, RESID><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(x, r, xbias, h_out, y, g, b,
+                                                                                     rows, d, eps);
+    return GBX_OK;
 }
 
 template <bool RESID>
-static int launch_ln(const float* x, const float* r, const float* xbias, float* h_out, float* y,
-                     const float* g, const float* b, int64_t rows, int d, float eps,
-                     cudaStream_t stream)
+static int launch_ln(const char* what, const float* x, const float* r, const float* xbias, float* h_out, float* y,
+                     const float* g, const float* b, int64_t rows, int d, float eps, cudaStream_t stream)
 {
     RowShape shape;
-    const bool vec = d % 4 == 0 && d <= kLnMaxStagedFloats && row_shape(d / 4, &shape) &&
-                     aligned16(x) && aligned16(y) && (!RESID || aligned16(r)) &&
-                     (!h_out || aligned16(h_out)) && (!xbias || aligned16(xbias)) &&
+    const bool vec = d % 4 == 0 && row_shape(d / 4, &shape) && aligned16(x) && aligned16(y) &&
+                     (!RESID || aligned16(r)) && (!h_out || aligned16(h_out)) && (!xbias || aligned16(xbias)) &&
                      (!g || aligned16(g)) && (!b || aligned16(b));
     if (vec) {
 #define GBX_LN_CALL(T, V) launch_ln_vec<T, V, RESID>(x, r, xbias, h_out, y, g, b, rows, d, eps, stream)
-        return GBX_ROW_DISPATCH(shape, GBX_LN_CALL, set_error(GBX_ERANGE, "layernorm: no shape for d=%d", d));
+        const int rc = GBX_ROW_DISPATCH(shape, GBX_LN_CALL, GBX_ERANGE);
 #undef GBX_LN_CALL
+        if (rc != GBX_OK) return set_error(rc, "%s: rows=%lld d=%d out of range", what, (long long)rows, d);
+    } else {
+        auto k = ln_general_kernel<RESID>;
+        const int grid = persistent_grid(k, kGeneralCTA, 0, rows, 4);
+        if (grid < 1) return GBX_ECUDA;
+        k<<<grid, kGeneralCTA, 0, stream>>>(x, r, xbias, h_out, y, g, b, rows, d, eps);
     }
-    auto k = ln_general_kernel<RESID>;
-    const int grid = persistent_grid(k, kRowCTA, 0, rows, 4);
-    if (grid < 1) return GBX_ECUDA;
-    k<<<grid, kRowCTA, 0, stream>>>(x, r, xbias, h_out, y, g, b, rows, d, eps);
-    return check_launch(RESID ? "gbx_residual_layernorm" : "gbx_layernorm");
+    return check_launch(what);
 }
 
 }  // namespace gbx
@@ -203,7 +182,7 @@ extern "C" int gbx_layernorm(const float* x, float* y, const float* gamma, const
     if (rows < 0 || d <= 0) return set_error(GBX_EINVAL, "gbx_layernorm: rows=%lld d=%d", (long long)rows, d);
     if (rows == 0) return GBX_OK;
     if (!x || !y) return set_error(GBX_EINVAL, "gbx_layernorm: null pointer");
-    return launch_ln<false>(x, nullptr, nullptr, nullptr, y, gamma, beta, rows, d, eps,
+    return launch_ln<false>("gbx_layernorm", x, nullptr, nullptr, nullptr, y, gamma, beta, rows, d, eps,
                             reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -216,6 +195,6 @@ extern "C" int gbx_residual_layernorm(const float* x, const float* r, const floa
     if (rows == 0) return GBX_OK;
     if (!x || !r || !y) return set_error(GBX_EINVAL, "gbx_residual_layernorm: null pointer");
     if (h_out && h_out == y) return set_error(GBX_EINVAL, "gbx_residual_layernorm: h_out and y must differ");
-    return launch_ln<true>(x, r, xbias, h_out, y, gamma, beta, rows, d, eps,
+    return launch_ln<true>("gbx_residual_layernorm", x, r, xbias, h_out, y, gamma, beta, rows, d, eps,
                            reinterpret_cast<cudaStream_t>(stream));
 }

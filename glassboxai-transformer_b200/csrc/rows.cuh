@@ -4,23 +4,36 @@
 // (TPR a power of two); thread `lane` of the group holds float4s
 // lane, lane+TPR, ..., lane+(V4-1)*TPR in registers, so a warp's loads of one
 // k are 32 consecutive 16-byte pieces (coalesced) and the row is read from
-// HBM exactly once.  A CTA of kRowCTA threads holds kRowCTA/TPR rows and walks
-// the row space grid-stride, so the loop bound is uniform across the CTA and
-// __syncthreads is legal inside it.
+// HBM exactly once.
+//
+// Launch shape: one full grid, each CTA owning RPC = CTA/TPR consecutive rows
+// (no grid-stride loop).  Measured on B200, a full grid of short-lived CTAs
+// streams these rows at 95-106% of the measured copy bandwidth, where a
+// persistent grid of the same kernels reached 87-97%: resident CTAs then
+// work on neighbouring rows, and each SM keeps starting fresh loads while
+// older CTAs finish their arithmetic.
 //
 // Shape selection (row_shape): rows of up to 32 float4s use one group of
-// pow2ceil(n4) threads with one float4 each; longer rows use 32..256 threads
-// with V4 <= 8 float4s each, which keeps the row (plus the residual operand
-// while it is being added) in registers for rows of up to 8192 floats.
+// pow2ceil(n4) threads with one float4 each; longer rows use the smallest
+// power-of-two TPR in [32, 1024] that leaves each thread at most 4 float4s
+// (rows of up to 16384 floats).  Few float4s per thread keep the register
+// count low enough for 5-8 resident CTAs per SM.
 #pragma once
 
 #include "gbx_common.cuh"
 
 namespace gbx {
 
-constexpr int kRowCTA = 256;
-constexpr int kRowMaxV4 = 8;
-constexpr int kRowMaxTPR = 256;
+constexpr int kRowMaxV4 = 4;
+constexpr int kRowMaxTPR = 1024;
+
+// Threads per CTA for a group width: 256, or the group itself when wider.
+template <int TPR>
+struct RowCTA {
+    static constexpr int threads = TPR > 256 ? TPR : 256;
+    static constexpr int rows = threads / TPR;
+    static constexpr int warps = threads / 32;
+};
 
 struct RowShape {
     int tpr, v4;
@@ -38,19 +51,21 @@ inline bool row_shape(int n4, RowShape* s)
         return true;
     }
     int t = 32;
-    while ((n4 + t - 1) / t > kRowMaxV4) t <<= 1;
-    if (t > kRowMaxTPR) return false;
+    while ((n4 + t - 1) / t > kRowMaxV4 && t < kRowMaxTPR) t <<= 1;
+    const int v4 = (n4 + t - 1) / t;
+    if (v4 > kRowMaxV4) return false;
     s->tpr = t;
-    s->v4 = (n4 + t - 1) / t;
+    s->v4 = v4;
     return true;
 }
 
 // Sum / max over the TPR threads of this thread's row group.  For TPR > 32
-// the warps of a group combine through `red` (kRowCTA/32 floats); every
-// thread of the group adds the partials in the same order, so all of them
-// get the same value.  Callers alternate two `red` buffers between
+// the warps of a group combine through `red` (RowCTA<TPR>::warps floats);
+// every thread of the group adds the partials in the same order, so all of
+// them get the same value.  Callers alternate two `red` buffers between
 // consecutive reductions: the barrier inside each reduction then separates
-// the reads of one buffer from its next writes.
+// the reads of one buffer from its next writes.  Every thread of the CTA
+// must call these (they contain __syncthreads for TPR > 32).
 template <int TPR>
 __device__ __forceinline__ float row_sum(float v, float* red)
 {
@@ -85,8 +100,11 @@ __device__ __forceinline__ float row_max(float v, float* red)
     }
 }
 
-// Block-wide sum for the general (any length) kernels: every thread gets the
-// total.  `red` holds kRowCTA/32 floats; same alternation rule as above.
+// Block-wide sum / max for the general (any length) kernels, which run
+// kGeneralCTA threads: every thread gets the total.  `red` holds
+// kGeneralCTA/32 floats; same alternation rule as above.
+constexpr int kGeneralCTA = 256;
+
 __device__ __forceinline__ float block_sum(float v, float* red)
 {
     v = group_sum<32>(v);
@@ -94,7 +112,7 @@ __device__ __forceinline__ float block_sum(float v, float* red)
     __syncthreads();
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kRowCTA / 32; ++w) s += red[w];
+    for (int w = 0; w < kGeneralCTA / 32; ++w) s += red[w];
     return s;
 }
 
@@ -105,12 +123,29 @@ __device__ __forceinline__ float block_max(float v, float* red)
     __syncthreads();
     float m = red[0];
 #pragma unroll
-    for (int w = 1; w < kRowCTA / 32; ++w) m = fmaxf(m, red[w]);
+    for (int w = 1; w < kGeneralCTA / 32; ++w) m = fmaxf(m, red[w]);
     return m;
+}
+
+// Number of CTAs of the full-grid launch for `rows` rows at group width TPR,
+// or -1 when it exceeds the grid limit.
+template <int TPR>
+inline int64_t row_grid(int64_t rows)
+{
+    const int64_t g = (rows + RowCTA<TPR>::rows - 1) / RowCTA<TPR>::rows;
+    return g > 0x7fffffffLL ? -1 : g;
 }
 
 // Expands F(TPR, V4) for every shape row_shape can return; evaluates to the
 // call's result, or `fallback` for an impossible shape.
+#define GBX_ROW_CASE34(shape, F, T)                                                            \
+    case T:                                                                                    \
+        switch ((shape).v4) {                                                                  \
+        case 3: return F(T, 3);                                                                \
+        case 4: return F(T, 4);                                                                \
+        }                                                                                      \
+        break;
+
 #define GBX_ROW_DISPATCH(shape, F, fallback)                                                   \
     [&]() {                                                                                    \
         switch ((shape).tpr) {                                                                 \
@@ -125,38 +160,15 @@ __device__ __forceinline__ float block_max(float v, float* red)
             case 2: return F(32, 2);                                                           \
             case 3: return F(32, 3);                                                           \
             case 4: return F(32, 4);                                                           \
-            case 5: return F(32, 5);                                                           \
-            case 6: return F(32, 6);                                                           \
-            case 7: return F(32, 7);                                                           \
-            case 8: return F(32, 8);                                                           \
             }                                                                                  \
             break;                                                                             \
-        case 64:                                                                               \
-            switch ((shape).v4) {                                                              \
-            case 5: return F(64, 5);                                                           \
-            case 6: return F(64, 6);                                                           \
-            case 7: return F(64, 7);                                                           \
-            case 8: return F(64, 8);                                                           \
-            }                                                                                  \
-            break;                                                                             \
-        case 128:                                                                              \
-            switch ((shape).v4) {                                                              \
-            case 5: return F(128, 5);                                                          \
-            case 6: return F(128, 6);                                                          \
-            case 7: return F(128, 7);                                                          \
-            case 8: return F(128, 8);                                                          \
-            }                                                                                  \
-            break;                                                                             \
-        case 256:                                                                              \
-            switch ((shape).v4) {                                                              \
-            case 5: return F(256, 5);                                                          \
-            case 6: return F(256, 6);                                                          \
-            case 7: return F(256, 7);                                                          \
-            case 8: return F(256, 8);                                                          \
-            }                                                                                  \
-            break;                                                                             \
+        GBX_ROW_CASE34(shape, F, 64)                                                         \
+        GBX_ROW_CASE34(shape, F, 128)                                                         \
+        GBX_ROW_CASE34(shape, F, 256)                                                         \
+        GBX_ROW_CASE34(shape, F, 512)                                                         \
+        GBX_ROW_CASE34(shape, F, 1024)                                                         \
         }                                                                                      \
-        return (fallback);                                                                     \
+        return static_cast<int>(fallback);                                                     \
     }()
 
 }  // namespace gbx

@@ -1,101 +1,167 @@
 // softmax.cu -- row softmax (replaces softmaxKernel, transformer.cu:126-166,
-// which the reference launches once per head, :839-842).
+// which the reference launches once per head, :839-842), and the same softmax
+// fused with the score epilogue of attentionScoresKernel
+// (transformer.cu:213-232: divide by sqrt(headDim), -1e9f above the diagonal).
 //
 // Per row: one HBM read into registers, max by warp shuffles (seeded with
 // -1e30f like the reference), e = expf(x - max) kept in registers, sum by
-// shuffles, out = e / sum with IEEE division, one HBM write.  The reference
-// makes three reads and two writes of every element.  Because max is exact
-// and expf / division are the same CUDA functions, every e is bit-identical
-// to the reference's; only the order of the sum differs.
+// shuffles, out = e / sum, one HBM write.  The reference makes three reads
+// and two writes of every element.
+//
+// Division.  out = e / sum is evaluated as q = e * r, q += (e - q*sum) * r
+// with r = 1/sum (IEEE, once per row) and both steps as FMAs: the residual
+// e - q*sum is exact, and one correction step from a faithful quotient and
+// the correctly rounded reciprocal gives the correctly rounded quotient
+// (Markstein's theorem) whenever no intermediate is subnormal.  Outputs are
+// therefore the IEEE quotients the reference computes, except possibly for
+// subnormal outputs (absolute error below 1e-38).  The per-element IEEE
+// divide has a slow path that every masked entry (e = 0) takes; on B200 it
+// cut the kernel's throughput from 6.5 to 4.3 TB/s on causal score rows.
+// The same identity gives the score scaling x / scale.
+//
+// Because max is exact and expf is the same CUDA function, every e is
+// bit-identical to the reference's; only the order of the sum differs.
 #include "rows.cuh"
 
 namespace gbx {
 
-template <int TPR, int V4>
-__global__ void __launch_bounds__(kRowCTA)
-softmax_vec_kernel(const float* in, float* out, int64_t rows, int L)
+__device__ __forceinline__ float div_by(float a, float b, float rb)
 {
-    constexpr int RPC = kRowCTA / TPR;
-    __shared__ float red[2][kRowCTA / 32];
+    const float q = a * rb;
+    return fmaf(fmaf(-q, b, a), rb, q);
+}
+
+// Score epilogue of the attention variant: the query of row p (p = row % S)
+// sees key columns 0 .. p + q_off; later columns hold -1e9f
+// (transformer.cu:220-221), earlier ones raw / scale (:228).
+struct ScoreEpilogue {
+    int S;
+    int q_off;
+    float scale;
+    bool causal;
+};
+
+template <int TPR, int V4, bool ATTN>
+__global__ void __launch_bounds__(RowCTA<TPR>::threads)
+softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep)
+{
+    __shared__ float red[2][RowCTA<TPR>::warps];
     const int n4 = L >> 2;
     const int lane = threadIdx.x & (TPR - 1);
-    const int grp = threadIdx.x / TPR;
+    const int64_t row = (int64_t)blockIdx.x * RowCTA<TPR>::rows + threadIdx.x / TPR;
+    const bool valid = row < rows;
+    const int64_t off = row * L;
 
-    for (int64_t row0 = (int64_t)blockIdx.x * RPC; row0 < rows; row0 += (int64_t)gridDim.x * RPC) {
-        const int64_t row = row0 + grp;
-        const bool valid = row < rows;
-        const int64_t off = row * L;
+    // last visible column of this row (attention variant)
+    int last = L - 1;
+    float rscale = 1.0f;
+    if (ATTN) {
+        if (ep.causal) last = (int)min((int64_t)L - 1, (valid ? row % ep.S : 0) + (int64_t)ep.q_off);
+        rscale = 1.0f / ep.scale;
+    }
 
-        float4 v[V4];
+    float4 v[V4];
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        const int c = k * TPR + lane;
+        // chunks entirely past `last` are never read
+        const bool need = valid && c < n4 && (!ATTN || 4 * c <= last);
+        v[k] = need ? ld_stream(in + off + 4 * c) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        if (ATTN && c < n4) {
+            float* e = &v[k].x;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) e[j] = (4 * c + j > last) ? -1e9f : div_by(e[j], ep.scale, rscale);
+        }
+    }
+    float m = -1e30f;
+#pragma unroll
+    for (int k = 0; k < V4; ++k) m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
+    m = row_max<TPR>(m, red[0]);
+
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        if (k * TPR + lane < n4) {
+            v[k].x = expf(v[k].x - m);
+            v[k].y = expf(v[k].y - m);
+            v[k].z = expf(v[k].z - m);
+            v[k].w = expf(v[k].w - m);
+            s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        }
+    }
+    s = row_sum<TPR>(s, red[1]);
+
+    if (valid) {
+        const float r = 1.0f / s;
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
             const int c = k * TPR + lane;
-            v[k] = (valid && c < n4) ? ld_stream(in + off + 4 * c)
-                                     : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        }
-        float m = -1e30f;
-#pragma unroll
-        for (int k = 0; k < V4; ++k) m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
-        m = row_max<TPR>(m, red[0]);
-
-        float s = 0.0f;
-#pragma unroll
-        for (int k = 0; k < V4; ++k) {
-            if (k * TPR + lane < n4) {
-                v[k].x = expf(v[k].x - m);
-                v[k].y = expf(v[k].y - m);
-                v[k].z = expf(v[k].z - m);
-                v[k].w = expf(v[k].w - m);
-                s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-            }
-        }
-        s = row_sum<TPR>(s, red[1]);
-
-        if (valid) {
-#pragma unroll
-            for (int k = 0; k < V4; ++k) {
-                const int c = k * TPR + lane;
-                if (c < n4)
-                    st_stream(out + off + 4 * c,
-                              make_float4(v[k].x / s, v[k].y / s, v[k].z / s, v[k].w / s));
-            }
+            if (c < n4)
+                st_stream(out + off + 4 * c, make_float4(div_by(v[k].x, s, r), div_by(v[k].y, s, r),
+                                                         div_by(v[k].z, s, r), div_by(v[k].w, s, r)));
         }
     }
 }
 
 // General path (any L, any alignment, rows longer than the register path):
 // one CTA per row, the reference's three passes with shuffle reductions.
-__global__ void __launch_bounds__(kRowCTA)
-softmax_general_kernel(const float* in, float* out, int64_t rows, int L)
+template <bool ATTN>
+__global__ void __launch_bounds__(kGeneralCTA)
+softmax_general_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep)
 {
-    __shared__ float red[2][kRowCTA / 32];
+    __shared__ float red[2][kGeneralCTA / 32];
+    const float rscale = ATTN ? 1.0f / ep.scale : 1.0f;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const float* ir = in + row * L;
         float* orow = out + row * L;
+        const int last = (ATTN && ep.causal) ? (int)min((int64_t)L - 1, row % ep.S + ep.q_off) : L - 1;
+        auto val = [&](int i) -> float {
+            if (!ATTN) return ir[i];
+            return i > last ? -1e9f : div_by(ir[i], ep.scale, rscale);
+        };
         float m = -1e30f;
-        for (int i = threadIdx.x; i < L; i += kRowCTA) m = fmaxf(m, ir[i]);
+        for (int i = threadIdx.x; i < L; i += kGeneralCTA) m = fmaxf(m, val(i));
         m = block_max(m, red[0]);
         float s = 0.0f;
-        for (int i = threadIdx.x; i < L; i += kRowCTA) {
-            const float e = expf(ir[i] - m);
+        for (int i = threadIdx.x; i < L; i += kGeneralCTA) {
+            const float e = expf(val(i) - m);
             orow[i] = e;
             s += e;
         }
         s = block_sum(s, red[1]);
-        for (int i = threadIdx.x; i < L; i += kRowCTA) orow[i] = orow[i] / s;
+        const float r = 1.0f / s;
+        for (int i = threadIdx.x; i < L; i += kGeneralCTA) orow[i] = div_by(orow[i], s, r);
         __syncthreads();
     }
 }
 
-template <int TPR, int V4>
-static int launch_softmax_vec(const float* in, float* out, int64_t rows, int L, cudaStream_t stream)
+template <int TPR, int V4, bool ATTN>
+static int launch_softmax_vec(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep,
+                              cudaStream_t stream)
 {
-    auto k = softmax_vec_kernel<TPR, V4>;
-    constexpr int RPC = kRowCTA / TPR;
-    const int grid = persistent_grid(k, kRowCTA, 0, (rows + RPC - 1) / RPC, 1);
-    if (grid < 1) return GBX_ECUDA;
-    k<<<grid, kRowCTA, 0, stream>>>(in, out, rows, L);
-    return check_launch("gbx_softmax_rows");
+    const int64_t grid = row_grid<TPR>(rows);
+    if (grid < 0) return GBX_ERANGE;
+    softmax_vec_kernel<TPR, V4, ATTN><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(in, out, rows, L, ep);
+    return GBX_OK;
+}
+
+template <bool ATTN>
+static int launch_softmax(const char* what, const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep,
+                          cudaStream_t s)
+{
+    RowShape shape;
+    int rc;
+    if (L % 4 == 0 && aligned16(in) && aligned16(out) && row_shape(L / 4, &shape)) {
+#define GBX_SM_CALL(T, V) launch_softmax_vec<T, V, ATTN>(in, out, rows, L, ep, s)
+        rc = GBX_ROW_DISPATCH(shape, GBX_SM_CALL, GBX_ERANGE);
+#undef GBX_SM_CALL
+        if (rc != GBX_OK) return set_error(rc, "%s: rows=%lld L=%d out of range", what, (long long)rows, L);
+    } else {
+        const int grid = persistent_grid(softmax_general_kernel<ATTN>, kGeneralCTA, 0, rows, 4);
+        if (grid < 1) return GBX_ECUDA;
+        softmax_general_kernel<ATTN><<<grid, kGeneralCTA, 0, s>>>(in, out, rows, L, ep);
+    }
+    return check_launch(what);
 }
 
 }  // namespace gbx
@@ -107,15 +173,21 @@ extern "C" int gbx_softmax_rows(const float* in, float* out, int64_t rows, int L
     if (rows < 0 || L <= 0) return set_error(GBX_EINVAL, "gbx_softmax_rows: rows=%lld L=%d", (long long)rows, L);
     if (rows == 0) return GBX_OK;
     if (!in || !out) return set_error(GBX_EINVAL, "gbx_softmax_rows: null pointer");
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    RowShape shape;
-    if (L % 4 == 0 && aligned16(in) && aligned16(out) && row_shape(L / 4, &shape)) {
-#define GBX_SM_CALL(T, V) launch_softmax_vec<T, V>(in, out, rows, L, s)
-        return GBX_ROW_DISPATCH(shape, GBX_SM_CALL, set_error(GBX_ERANGE, "softmax: no shape for L=%d", L));
-#undef GBX_SM_CALL
-    }
-    const int grid = persistent_grid(softmax_general_kernel, kRowCTA, 0, rows, 4);
-    if (grid < 1) return GBX_ECUDA;
-    softmax_general_kernel<<<grid, kRowCTA, 0, s>>>(in, out, rows, L);
-    return check_launch("gbx_softmax_rows");
+    ScoreEpilogue ep{1, 0, 1.0f, false};
+    return launch_softmax<false>("gbx_softmax_rows", in, out, rows, L, ep, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t rows, int L, int S, int q_off,
+                                     float scale, int causal, gbx_stream_t stream)
+{
+    if (rows < 0 || L <= 0 || S <= 0 || q_off < 0)
+        return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: rows=%lld L=%d S=%d q_off=%d", (long long)rows, L, S,
+                         q_off);
+    if (!(scale > 0.0f) || scale == INFINITY)
+        return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: scale=%g must be finite and > 0", (double)scale);
+    if (rows == 0) return GBX_OK;
+    if (!scores || !probs) return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: null pointer");
+    ScoreEpilogue ep{S, q_off, scale, causal != 0};
+    return launch_softmax<true>("gbx_attn_softmax_rows", scores, probs, rows, L, ep,
+                                reinterpret_cast<cudaStream_t>(stream));
 }

@@ -130,6 +130,22 @@ int gbx_bias_gelu(const float* in, float* out, const float* bias, int64_t rows, 
  */
 int gbx_softmax_rows(const float* in, float* out, int64_t rows, int L, gbx_stream_t stream);
 
+/*
+ * Attention-score epilogue fused with the row softmax.  Replaces the
+ * epilogue of attentionScoresKernel (transformer.cu:213-232: scores =
+ * dot / scale with scale = sqrtf(headDim) (:836), -1e9f where the key comes
+ * after the query (:220-221)) followed by softmaxKernel (:126-166):
+ *   row r is query position p = r % S of one [S, L] score matrix;
+ *   x[c] = c > p + q_off (and causal) ? -1e9f : dot[r, c] / scale
+ *   out  = softmax(x) exactly as gbx_softmax_rows
+ * `scores` holds the raw dot products q.k; entries past the causal limit
+ * are never read (they may hold anything).  q_off shifts the diagonal:
+ * 0 for prefill (L == S), L - S when S new queries follow L - S cached keys.
+ * rows = matrices * S; probs may alias scores.
+ */
+int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t rows, int L, int S, int q_off,
+                          float scale, int causal, gbx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

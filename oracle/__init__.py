@@ -60,6 +60,8 @@ def lib():
         L.gbxo_residual_ln_mt.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, ctypes.c_float, _c_int]
         L.gbxo_bias_gelu_mt.argtypes = [_vp, _vp, _vp, _c_i64, _c_int, _c_int]
         L.gbxo_softmax_rows_mt.argtypes = [_vp, _vp, _c_i64, _c_int, _c_int]
+        L.gbxo_attn_softmax_mt.argtypes = [_vp, _vp, _c_i64, _c_int, _c_int, _c_int, ctypes.c_float, _c_int,
+                                           _c_int]
         L.gbxo_max_threads.restype = _c_int
         _lib = L
     return _lib
@@ -128,6 +130,16 @@ def softmax_rows(x, nthreads=1):
     rows = x.size // L if L else 0
     out = np.empty_like(x)
     lib().gbxo_softmax_rows_mt(_ptr(x), _ptr(out), rows, L, nthreads)
+    return out
+
+
+def attn_softmax_rows(raw, S, scale, q_off=0, causal=True, nthreads=1):
+    """Score epilogue (raw / scale, -1e9 past the causal limit) + softmax."""
+    raw = np.ascontiguousarray(raw, dtype=np.float32)
+    L = raw.shape[-1]
+    rows = raw.size // L if L else 0
+    out = np.empty_like(raw)
+    lib().gbxo_attn_softmax_mt(_ptr(raw), _ptr(out), rows, L, S, q_off, scale, 1 if causal else 0, nthreads)
     return out
 
 

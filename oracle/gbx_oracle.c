@@ -19,6 +19,9 @@
  *   gbxo_bias_gelu       transformer.cu:272,276-277  ffnUpKernel epilogue
  *                        (same formula as geluKernel transformer.cu:68-75)
  *   gbxo_softmax_rows    transformer.cu:126-166   softmaxKernel
+ *   gbxo_attn_softmax    transformer.cu:213-232   attentionScoresKernel's
+ *                        epilogue (dot / scale, -1e9f above the diagonal),
+ *                        then transformer.cu:126-166 softmaxKernel
  *
  * Pinning: the f16/bf16 decode is checked bit for bit against the reference's
  * own GGUFLoader::getTensor over all 65 536 bit patterns (fixture made by
@@ -31,9 +34,14 @@
  *   - products that nvcc contracts into an FMA under its default -fmad=true
  *     are written as explicit fmaf() here (variance accumulation, the
  *     `normalized * g + b` epilogue, the GELU cubic term);
- *   - reductions are sequential (the reference uses a 256-wide shared-memory
- *     tree), so sums differ in rounding order only; parity for LayerNorm,
- *     GELU and softmax is therefore stated as |a-b| <= 1e-6 + 1e-5*|b|;
+ *   - sums follow the reference's block reduction order exactly
+ *     (transformer.cu:93-104, 140-160 with BLOCK_SIZE = 256, :36): partial t
+ *     accumulates elements t, t+256, t+512, ... in order, then partials are
+ *     folded pairwise, sdata[t] += sdata[t+s] for s = 128, 64, ..., 1;
+ *   - expf / tanhf / rsqrtf are the host's (glibc's expf and tanhf, a
+ *     correctly rounded 1/sqrt), which may differ from CUDA's by an ulp or
+ *     two, so parity for LayerNorm, GELU and softmax is stated as
+ *     |a-b| <= 1e-6 + 1e-5*|b|;
  *   - a GPU fp32 add whose result is NaN yields the canonical NaN 0x7fffffff,
  *     whereas x86 propagates the operand's payload; the embed restatement
  *     canonicalises NaN sums so that embed parity stays bit-exact.
@@ -179,18 +187,38 @@ int64_t gbxo_embed_mt(const int32_t* ids, const void* wte, int wte_dtype,
     return c.bad;
 }
 
+/* The reference's block reduction (transformer.cu:93-104, 112-119, 140-160):
+ * BLOCK_SIZE = 256 threads (:36); thread t folds v(t), v(t+256), ... into
+ * its partial in index order, then sdata[t] += sdata[t + s] for s = 128,
+ * 64, ..., 1.  ACC(acc, i) gives the partial's update for element i. */
+#define REF_BLOCK 256
+#define REF_BLOCK_REDUCE(result, n, ACC)                                         \
+    do {                                                                         \
+        float part_[REF_BLOCK];                                                  \
+        for (int t_ = 0; t_ < REF_BLOCK; t_++) {                                 \
+            float acc = 0.0f;                                                    \
+            for (int i = t_; i < (n); i += REF_BLOCK) ACC(acc, i);               \
+            part_[t_] = acc;                                                     \
+        }                                                                        \
+        for (int s_ = REF_BLOCK / 2; s_ > 0; s_ >>= 1)                           \
+            for (int t_ = 0; t_ < s_; t_++) part_[t_] += part_[t_ + s_];         \
+        (result) = part_[0];                                                     \
+    } while (0)
+
 /* One LayerNorm row, transformer.cu:89-123: mean = sum/dim; variance =
- * sum((x-mean)^2)/dim (population, two-pass); invStd = rsqrtf(var+eps);
+ * sum((x-mean)^2)/dim (population, two-pass; nvcc contracts the square
+ * into the accumulation, fmaf(diff, diff, sum)); invStd = rsqrtf(var+eps);
  * y = ((x-mean)*invStd)*g + b with g=1, b=0 where gamma/beta are NULL
  * (:120-121).  rsqrtf is evaluated as 1/sqrt in double, rounded to fp32
  * (correctly rounded; the GPU's rsqrtf is within 2 ulp of it). */
 static void ln_row(const float* x, float* y, const float* g, const float* b, int d, float eps)
 {
-    float sum = 0.0f;
-    for (int i = 0; i < d; i++) sum += x[i];
+    float sum, sq;
+#define ACC_X(acc, i) (acc) += x[i]
+    REF_BLOCK_REDUCE(sum, d, ACC_X);
     float mean = sum / (float)d;
-    float sq = 0.0f;
-    for (int i = 0; i < d; i++) { float diff = x[i] - mean; sq = fmaf(diff, diff, sq); }
+#define ACC_SQ(acc, i) do { float diff_ = x[i] - mean; (acc) = fmaf(diff_, diff_, (acc)); } while (0)
+    REF_BLOCK_REDUCE(sq, d, ACC_SQ);
     float variance = sq / (float)d;
     float inv = (float)(1.0 / sqrt((double)(variance + eps)));
     for (int i = 0; i < d; i++) {
@@ -278,7 +306,8 @@ void gbxo_bias_gelu_mt(const float* in, float* out, const float* bias,
 }
 
 /* transformer.cu:126-166: maxVal starts at -1e30f and folds fmaxf over the
- * row; e = expf(x - maxVal) (stored in place by the reference); sum += e;
+ * row (exact, so its order does not matter); e = expf(x - maxVal) (stored in
+ * place by the reference); sum of e in the block reduction order;
  * x = e / sum (true division).  Entries masked with -1e9f
  * (transformer.cu:221) come out exactly 0. */
 static void softmax_rows(void* c_, int64_t r0, int64_t r1)
@@ -290,8 +319,10 @@ static void softmax_rows(void* c_, int64_t r0, int64_t r1)
         float* orow = c->y + r * L;
         float m = -1e30f;
         for (int i = 0; i < L; i++) m = fmaxf(m, ir[i]);
-        float s = 0.0f;
-        for (int i = 0; i < L; i++) { float e = expf(ir[i] - m); orow[i] = e; s += e; }
+        for (int i = 0; i < L; i++) orow[i] = expf(ir[i] - m);
+        float s;
+#define ACC_E(acc, i) (acc) += orow[i]
+        REF_BLOCK_REDUCE(s, L, ACC_E);
         for (int i = 0; i < L; i++) orow[i] = orow[i] / s;
     }
 }
@@ -300,6 +331,41 @@ void gbxo_softmax_rows_mt(const float* in, float* out, int64_t rows, int L, int 
 {
     rows_ctx c = { in, 0, 0, out, 0, 0, 0, L, 0.0f };
     parallel_rows(softmax_rows, &c, rows, nthreads);
+}
+
+/* transformer.cu:213-232 then :126-166.  The reference's score kernel writes
+ * scores[h][p][s] = -1e9f when s > p (:220-221) and sum / scale otherwise
+ * (:228, true division, scale = sqrtf(headDim) from :836); softmaxKernel then
+ * runs on those rows.  Here row r of `in` holds the raw dot products of query
+ * p = r % S, which sees keys 0 .. p + q_off (q_off = 0 in the reference's
+ * prefill, where the key count equals the query count). */
+typedef struct { const float* in; float* out; int L, S, q_off, causal; float scale; } attn_ctx;
+
+static void attn_rows(void* c_, int64_t r0, int64_t r1)
+{
+    attn_ctx* c = (attn_ctx*)c_;
+    int L = c->L;
+    for (int64_t r = r0; r < r1; r++) {
+        const float* ir = c->in + r * L;
+        float* orow = c->out + r * L;
+        int64_t last = c->causal ? (r % c->S) + (int64_t)c->q_off : (int64_t)L - 1;
+        float m = -1e30f;
+        for (int i = 0; i < L; i++) {
+            orow[i] = i > last ? -1e9f : ir[i] / c->scale;
+            m = fmaxf(m, orow[i]);
+        }
+        for (int i = 0; i < L; i++) orow[i] = expf(orow[i] - m);
+        float s;
+        REF_BLOCK_REDUCE(s, L, ACC_E);
+        for (int i = 0; i < L; i++) orow[i] = orow[i] / s;
+    }
+}
+
+void gbxo_attn_softmax_mt(const float* in, float* out, int64_t rows, int L, int S, int q_off,
+                          float scale, int causal, int nthreads)
+{
+    attn_ctx c = { in, out, L, S > 0 ? S : 1, q_off, causal, scale };
+    parallel_rows(attn_rows, &c, rows, nthreads);
 }
 
 /* Single-thread entry points (the checker's default). */

@@ -39,8 +39,17 @@ import oracle  # noqa: E402
 from gguf_writer import GGML_F16, gpt2_kv, write_gguf  # noqa: E402
 
 
+_KEEP = []
+
+
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    """Device copy of `a`.  Every copy stays referenced until the script ends:
+    a pointer taken from a temporary tensor would be handed back to torch's
+    caching allocator as soon as the temporary dies, and a later copy could
+    overwrite it before the kernel that was given the pointer has run."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def host(t):

@@ -173,7 +173,7 @@ def test_embed_decode_position_2047(gbx, orc, cuda):
 # ---------------------------------------------------------------------------
 # LayerNorm and residual + LayerNorm
 
-LN_DIMS = [1, 3, 4, 5, 8, 64, 100, 132, 768, 772, 1024, 1600, 2048, 4096, 8192, 8196, 12000]
+LN_DIMS = [1, 3, 4, 5, 8, 64, 100, 132, 768, 772, 1024, 1600, 2048, 4096, 8192, 8196, 12000, 16384, 16388]
 
 
 def _ln_params(rng, d, with_params):
@@ -290,7 +290,7 @@ def test_gelu_sweep_specials_in_place(gbx, orc, cuda):
 # ---------------------------------------------------------------------------
 # softmax
 
-@pytest.mark.parametrize("L", [1, 2, 3, 4, 33, 64, 100, 1024, 1028, 2048, 4096, 8192, 8196, 40000])
+@pytest.mark.parametrize("L", [1, 2, 3, 4, 33, 64, 100, 132, 516, 1024, 1028, 2048, 4096, 8192, 8196, 16384, 16388, 40000])
 def test_softmax(gbx, orc, cuda, L):
     import torch
     rng = np.random.default_rng(L)
@@ -363,3 +363,71 @@ def test_runs_on_a_side_stream(gbx, orc, cuda):
         gbx.softmax_rows(xd, out, rows=300, L=1024, stream=s)
     s.synchronize()
     assert_close(out.cpu().numpy(), orc.softmax_rows(x), what="side stream")
+
+
+# ---------------------------------------------------------------------------
+# attention-score epilogue + softmax
+
+@pytest.mark.parametrize("S,H,scale", [(64, 3, 8.0), (1024, 2, 8.0), (128, 2, float(np.sqrt(np.float32(128)))),
+                                       (33, 2, 8.0), (256, 1, 11.3137)])
+def test_attn_softmax_causal_prefill(gbx, orc, cuda, S, H, scale):
+    import torch
+    rng = np.random.default_rng(S + H)
+    raw = (scale * rng.standard_normal((H, S, S))).astype(np.float32)
+    iu = np.triu_indices(S, 1)
+    ref = orc.attn_softmax_rows(raw, S=S, scale=scale)
+    raw_nan = raw.copy()
+    raw_nan[:, iu[0], iu[1]] = np.nan          # past the causal limit: never read
+    full, out = _guarded((H * S, S), torch)
+    gbx.attn_softmax_rows(_t(raw_nan, torch), out, rows=H * S, L=S, S=S, scale=scale)
+    got = out.cpu().numpy().reshape(H, S, S)
+    assert np.all(got[:, iu[0], iu[1]] == 0.0)
+    assert_close(got, ref, what=f"attn softmax S={S}")
+    _check_guards(full)
+
+
+@pytest.mark.parametrize("S,L", [(4, 40), (1, 2048), (7, 1031), (16, 1024)])
+def test_attn_softmax_query_offset(gbx, orc, cuda, S, L):
+    """S new queries after L - S cached keys: query p sees keys 0 .. p + L - S."""
+    import torch
+    rng = np.random.default_rng(S * L)
+    raw = (8.0 * rng.standard_normal((3 * S, L))).astype(np.float32)
+    ref = orc.attn_softmax_rows(raw, S=S, scale=8.0, q_off=L - S)
+    out = torch.empty((3 * S, L), device="cuda")
+    gbx.attn_softmax_rows(_t(raw, torch), out, rows=3 * S, L=L, S=S, scale=8.0, q_off=L - S)
+    assert_close(out.cpu().numpy(), ref, what=f"attn softmax q_off S={S} L={L}")
+
+
+def test_attn_softmax_non_causal_and_in_place(gbx, orc, cuda):
+    import torch
+    rng = np.random.default_rng(21)
+    raw = (np.sqrt(2.0) * 8.0 * rng.standard_normal((64, 2048))).astype(np.float32)
+    ref = orc.attn_softmax_rows(raw, S=1, scale=8.0, causal=False)
+    xd = _t(raw, torch)
+    gbx.attn_softmax_rows(xd, xd, rows=64, L=2048, S=1, scale=8.0, causal=False)
+    assert_close(xd.cpu().numpy(), ref, what="non-causal in place")
+
+
+def test_attn_softmax_unaligned_general_path(gbx, orc, cuda):
+    import torch
+    rng = np.random.default_rng(22)
+    S = 37
+    raw = (8.0 * rng.standard_normal((2 * S, S))).astype(np.float32)
+    ref = orc.attn_softmax_rows(raw, S=S, scale=8.0)
+    src = torch.empty(raw.size + 1, device="cuda")
+    src[1:] = torch.from_numpy(raw.ravel()).cuda()
+    out = torch.empty(raw.size + 1, device="cuda")
+    gbx.attn_softmax_rows(src.data_ptr() + 4, out.data_ptr() + 4, rows=2 * S, L=S, S=S, scale=8.0)
+    assert_close(out[1:].cpu().numpy().reshape(raw.shape), ref, what="unaligned attn softmax")
+
+
+def test_attn_softmax_argument_errors(gbx, cuda):
+    import torch
+    a = torch.zeros((4, 8), device="cuda")
+    for kw in (dict(scale=0.0), dict(scale=-1.0), dict(scale=float("inf")), dict(scale=1.0, S=0),
+               dict(scale=1.0, q_off=-1)):
+        args = dict(rows=4, L=8, S=4, q_off=0)
+        args.update(kw)
+        with pytest.raises(gbx.GbxError) as e:
+            gbx.attn_softmax_rows(a, a, **args)
+        assert e.value.status == 1

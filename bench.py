@@ -471,6 +471,14 @@ def run_kernel(args, shape):
         out = torch.empty_like(x)
         fn = lambda: G.softmax_rows(x, out, rows=R, L=L)
         nbytes = 8 * R * L
+    elif name == "attn_softmax_rows":
+        # causal prefill score matrices [R/L, L, L] of raw dot products, hd 64
+        S = L
+        R = (R // S) * S
+        x = 8.0 * torch.randn((R, L), generator=g, **f32)
+        out = torch.empty_like(x)
+        fn = lambda: G.attn_softmax_rows(x, out, rows=R, L=L, S=S, scale=8.0)
+        nbytes = 4 * (R // S) * (S * (S + 1) // 2) + 4 * R * L   # visible entries read, all written
     elif name in ("layernorm", "residual_layernorm"):
         x = torch.randn((R, d), generator=g, **f32)
         r = torch.randn((R, d), generator=g, **f32)
@@ -530,7 +538,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
-    ap.add_argument("--kernel", choices=["embed", "layernorm", "residual_layernorm", "softmax_rows", "bias_gelu"],
+    ap.add_argument("--kernel", choices=["embed", "layernorm", "residual_layernorm", "softmax_rows", "attn_softmax_rows",
+                                         "bias_gelu"],
                     help="time one kernel alone on --rows rows of the workload's shape")
     ap.add_argument("--rows", type=int, default=65536)
     args = ap.parse_args()

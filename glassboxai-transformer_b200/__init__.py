@@ -50,6 +50,7 @@ SIGNATURES = {
     "gbx_bias_gelu": [_vp, _vp, _vp, _i64, _int, _vp],
     "gbx_softmax_rows": [_vp, _vp, _i64, _int, _vp],
     "gbx_attn_softmax_rows": [_vp, _vp, _i64, _int, _int, _int, _f, _int, _vp],
+    "gbx_logits": [_vp, _i64, _vp, _int, _vp, _int, _int, _vp],
 }
 _RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
 
@@ -136,3 +137,7 @@ def softmax_rows(x, out, *, rows, L, stream=None):
 def attn_softmax_rows(scores, probs, *, rows, L, S, scale, q_off=0, causal=True, stream=None):
     _check(lib().gbx_attn_softmax_rows(_p(scores), _p(probs), rows, L, S, q_off, scale, 1 if causal else 0,
                                        _stream(stream)))
+
+
+def logits(h, wte, wte_dtype, out, *, rows, vocab, d, stream=None):
+    _check(lib().gbx_logits(_p(h), rows, _p(wte), wte_dtype, _p(out), vocab, d, _stream(stream)))

@@ -7,59 +7,20 @@
 // the reference's exact rules and added in fp32.  Output rows are written
 // with streaming 16-byte stores.
 #include "gbx_common.cuh"
+#include "decode.cuh"
 
 namespace gbx {
-
-// GGUF dtype code -> template index.
-enum { TF32 = 0, TF16 = 1, TBF16 = 2 };
-
-// Reference float16ToFloat32 (transformer.cu:508-527), as fp32 bits:
-// normal halves re-biased exactly; +-0 -> +0 (sign dropped, :514);
-// subnormals mantissa * 2^-24 (exact); +-inf kept; any NaN -> 0x7fc00000 (:521).
-__device__ __forceinline__ uint32_t f16_to_f32_bits(uint32_t h)
-{
-    const uint32_t sign = (h & 0x8000u) << 16;
-    const uint32_t ex = (h >> 10) & 0x1fu;
-    const uint32_t man = h & 0x3ffu;
-    const uint32_t normal = sign | ((ex + 112u) << 23) | (man << 13);
-    const uint32_t sub = sign | __float_as_uint(__uint2float_rn(man) * 5.9604644775390625e-8f);
-    const uint32_t infnan = man ? 0x7fc00000u : (sign | 0x7f800000u);
-    return ex == 0 ? (man ? sub : 0u) : (ex == 31 ? infnan : normal);
-}
-
-__device__ __forceinline__ float f16_to_f32(uint32_t h) { return __uint_as_float(f16_to_f32_bits(h)); }
-
-// Decode the 4 consecutive elements starting at element `e` (a multiple of 4)
-// of a table of type T: one 16-byte load for f32, one 8-byte load for
-// f16/bf16 (aligned by construction: rows are a multiple of 4 elements).
-template <int T>
-__device__ __forceinline__ float4 load4(const void* base, int64_t e)
-{
-    if (T == TF32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(base) + e));
-    const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + e));
-    if (T == TF16)
-        return make_float4(f16_to_f32(w.x & 0xffffu), f16_to_f32(w.x >> 16), f16_to_f32(w.y & 0xffffu),
-                           f16_to_f32(w.y >> 16));
-    return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
-                       __uint_as_float(w.y & 0xffff0000u));
-}
-
-template <int T>
-__device__ __forceinline__ float load1(const void* base, int64_t e)
-{
-    if (T == TF32) return __ldg(static_cast<const float*>(base) + e);
-    uint32_t h = __ldg(static_cast<const unsigned short*>(base) + e);
-    return T == TF16 ? f16_to_f32(h) : __uint_as_float(h << 16);
-}
 
 // ---------------------------------------------------------------------------
 // Embedding, vector path.  Work item = (token t, 4-element chunk c), numbered
 // t*n4 + c, so the 32 lanes of a warp read 32 consecutive 8- or 16-byte pieces
 // of table rows and write 512 consecutive bytes of output.  A full grid of
-// CTAs, each thread taking kEmbedU items spaced one CTA width apart and
-// issuing all their loads before any arithmetic.  (On B200, 8-element items
-// written as two half-coalesced stores per lane, in a persistent grid,
-// reached 68% of the copy bandwidth on a bf16 gather; this layout 92%.)
+// CTAs, each thread taking kEmbedU items spaced one CTA width apart: all
+// table loads are issued before any arithmetic, the loaded words stay raw
+// (2 registers per f16/bf16 item) and are decoded only at the store.  (On
+// B200, 8-element items written as two half-coalesced stores per lane, in a
+// persistent grid, reached 68% of the copy bandwidth on a bf16 gather; the
+// same items decoded right after their loads, 54%; this form 82-90%.)
 constexpr int kEmbedThreads = 256;
 constexpr int kEmbedU = 4;
 
@@ -73,8 +34,10 @@ embed_vec4_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
     const uint32_t n4 = div_n4.d;
     const uint32_t seq = div_seq.d;
     const uint32_t base = blockIdx.x * (uint32_t)(kEmbedThreads * kEmbedU) + threadIdx.x;
+    typename Raw4<WT>::type a[kEmbedU];
+    typename Raw4<PT>::type b[kEmbedU];
     uint32_t tok[kEmbedU], col[kEmbedU];
-    int32_t id[kEmbedU], pos[kEmbedU];
+    int bad[kEmbedU];
 #pragma unroll
     for (int u = 0; u < kEmbedU; ++u) {
         const uint32_t i = base + u * kEmbedThreads;
@@ -82,32 +45,26 @@ embed_vec4_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
         const uint32_t t = fast_div(ii, div_n4);
         tok[u] = t;
         col[u] = ii - t * n4;
-        id[u] = __ldg(ids + t);
-        pos[u] = pos_ids ? __ldg(pos_ids + t) : pos_off + (int32_t)(t - fast_div(t, div_seq) * seq);
-    }
-    float4 a[kEmbedU], b[kEmbedU];
-#pragma unroll
-    for (int u = 0; u < kEmbedU; ++u) {
-        const bool ok = (uint32_t)id[u] < (uint32_t)vocab && (uint32_t)pos[u] < (uint32_t)n_ctx;
-        if (base + u * kEmbedThreads < total && ok) {
-            a[u] = load4<WT>(wte, (int64_t)id[u] * d + 4 * col[u]);
-            b[u] = load4<PT>(wpe, (int64_t)pos[u] * d + 4 * col[u]);
+        const int32_t id = __ldg(ids + t);
+        const int32_t pos = pos_ids ? __ldg(pos_ids + t) : pos_off + (int32_t)(t - fast_div(t, div_seq) * seq);
+        bad[u] = ((uint32_t)id >= (uint32_t)vocab ? GBX_EMBED_BAD_ID : 0) |
+                 ((uint32_t)pos >= (uint32_t)n_ctx ? GBX_EMBED_BAD_POS : 0);
+        if (i < total && !bad[u]) {
+            a[u] = load_raw4<WT>(wte, (int64_t)id * d + 4 * col[u]);
+            b[u] = load_raw4<PT>(wpe, (int64_t)pos * d + 4 * col[u]);
         } else {
-            a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            b[u] = a[u];
+            a[u] = zero_raw4<WT>();
+            b[u] = zero_raw4<PT>();
         }
     }
 #pragma unroll
     for (int u = 0; u < kEmbedU; ++u) {
         if (base + u * kEmbedThreads >= total) continue;
-        const bool bad_id = (uint32_t)id[u] >= (uint32_t)vocab;
-        const bool bad_pos = (uint32_t)pos[u] >= (uint32_t)n_ctx;
-        if ((bad_id || bad_pos) && col[u] == 0 && err)
-            atomicOr(err, (bad_id ? GBX_EMBED_BAD_ID : 0) | (bad_pos ? GBX_EMBED_BAD_POS : 0));
+        if (bad[u] && col[u] == 0 && err) atomicOr(err, bad[u]);
         // one fp32 add per element, as embedTokensKernel (transformer.cu:183);
         // a rejected token's row is zeros (0 + 0).
-        st_stream(out + (int64_t)tok[u] * d + 4 * col[u],
-                  make_float4(a[u].x + b[u].x, a[u].y + b[u].y, a[u].z + b[u].z, a[u].w + b[u].w));
+        const float4 x = decode4<WT>(a[u]), y = decode4<PT>(b[u]);
+        st_stream(out + (int64_t)tok[u] * d + 4 * col[u], make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w));
     }
 }
 
@@ -143,7 +100,7 @@ __global__ void __launch_bounds__(256)
 dequant_vec4_kernel(const void* __restrict__ src, float* __restrict__ dst, int64_t n4)
 {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n4) st_stream(dst + i * 4, load4<T>(src, i * 4));
+    if (i < n4) st_stream(dst + i * 4, decode4<T>(load_raw4<T>(src, i * 4)));
 }
 
 template <int T>
@@ -153,16 +110,6 @@ dequant_scalar_kernel(const void* __restrict__ src, float* __restrict__ dst, int
     for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)
         dst[i] = load1<T>(src, i);
-}
-
-static int dtype_index(int dt)
-{
-    switch (dt) {
-    case GBX_DT_F32: return TF32;
-    case GBX_DT_F16: return TF16;
-    case GBX_DT_BF16: return TBF16;
-    default: return -1;
-    }
 }
 
 template <int WT, int PT>

@@ -17,7 +17,8 @@
 // subnormal outputs (absolute error below 1e-38).  The per-element IEEE
 // divide has a slow path that every masked entry (e = 0) takes; on B200 it
 // cut the kernel's throughput from 6.5 to 4.3 TB/s on causal score rows.
-// The same identity gives the score scaling x / scale.
+// The same identity gives the score scaling x / scale (an exact multiply when
+// scale is a power of two, as sqrt(64) = 8 is for GPT-2's 64-wide heads).
 //
 // Because max is exact and expf is the same CUDA function, every e is
 // bit-identical to the reference's; only the order of the sum differs.
@@ -39,9 +40,11 @@ struct ScoreEpilogue {
     int q_off;
     float scale;
     bool causal;
+    FastDiv div_S;   // S, for the 32-bit row index of the vector path
 };
 
-template <int TPR, int V4, bool ATTN>
+// POW2: scale is a power of two, so raw / scale == raw * (1/scale) exactly.
+template <int TPR, int V4, bool ATTN, bool POW2>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads)
 softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep)
 {
@@ -52,11 +55,15 @@ softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilog
     const bool valid = row < rows;
     const int64_t off = row * L;
 
-    // last visible column of this row (attention variant)
+    // last visible column of this row (attention variant; rows < 2^32 there)
     int last = L - 1;
     float rscale = 1.0f;
     if (ATTN) {
-        if (ep.causal) last = (int)min((int64_t)L - 1, (valid ? row % ep.S : 0) + (int64_t)ep.q_off);
+        if (ep.causal) {
+            const uint32_t r32 = valid ? (uint32_t)row : 0u;
+            const uint32_t p = r32 - fast_div(r32, ep.div_S) * (uint32_t)ep.S;
+            last = (int)min((int64_t)L - 1, (int64_t)p + ep.q_off);
+        }
         rscale = 1.0f / ep.scale;
     }
 
@@ -69,8 +76,16 @@ softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilog
         v[k] = need ? ld_stream(in + off + 4 * c) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         if (ATTN && c < n4) {
             float* e = &v[k].x;
+            if (4 * c + 3 <= last) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) e[j] = (4 * c + j > last) ? -1e9f : div_by(e[j], ep.scale, rscale);
+                for (int j = 0; j < 4; ++j) e[j] = POW2 ? e[j] * rscale : div_by(e[j], ep.scale, rscale);
+            } else if (4 * c > last) {
+                v[k] = make_float4(-1e9f, -1e9f, -1e9f, -1e9f);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    e[j] = (4 * c + j > last) ? -1e9f : (POW2 ? e[j] * rscale : div_by(e[j], ep.scale, rscale));
+            }
         }
     }
     float m = -1e30f;
@@ -78,14 +93,21 @@ softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilog
     for (int k = 0; k < V4; ++k) m = fmaxf(m, fmaxf(fmaxf(v[k].x, v[k].y), fmaxf(v[k].z, v[k].w)));
     m = row_max<TPR>(m, red[0]);
 
+    // every masked entry holds -1e9f, so they all share one exponential
+    const float e_mask = ATTN ? expf(-1e9f - m) : 0.0f;
     float s = 0.0f;
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
-        if (k * TPR + lane < n4) {
-            v[k].x = expf(v[k].x - m);
-            v[k].y = expf(v[k].y - m);
-            v[k].z = expf(v[k].z - m);
-            v[k].w = expf(v[k].w - m);
+        const int c = k * TPR + lane;
+        if (c < n4) {
+            if (ATTN && 4 * c > last) {
+                v[k] = make_float4(e_mask, e_mask, e_mask, e_mask);
+            } else {
+                v[k].x = expf(v[k].x - m);
+                v[k].y = expf(v[k].y - m);
+                v[k].z = expf(v[k].z - m);
+                v[k].w = expf(v[k].w - m);
+            }
             s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
         }
     }
@@ -135,13 +157,24 @@ softmax_general_kernel(const float* in, float* out, int64_t rows, int L, ScoreEp
     }
 }
 
+static bool is_pow2(float x)
+{
+    int e;
+    return x > 0.0f && frexpf(x, &e) == 0.5f;
+}
+
 template <int TPR, int V4, bool ATTN>
 static int launch_softmax_vec(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep,
                               cudaStream_t stream)
 {
     const int64_t grid = row_grid<TPR>(rows);
     if (grid < 0) return GBX_ERANGE;
-    softmax_vec_kernel<TPR, V4, ATTN><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(in, out, rows, L, ep);
+    if (ATTN && is_pow2(ep.scale))
+        softmax_vec_kernel<TPR, V4, ATTN, true><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(in, out, rows,
+                                                                                                   L, ep);
+    else
+        softmax_vec_kernel<TPR, V4, ATTN, false><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(in, out, rows,
+                                                                                                    L, ep);
     return GBX_OK;
 }
 
@@ -151,7 +184,8 @@ static int launch_softmax(const char* what, const float* in, float* out, int64_t
 {
     RowShape shape;
     int rc;
-    if (L % 4 == 0 && aligned16(in) && aligned16(out) && row_shape(L / 4, &shape)) {
+    // the vector path numbers rows in 32 bits for the causal position
+    if (L % 4 == 0 && aligned16(in) && aligned16(out) && row_shape(L / 4, &shape) && rows <= 0xffffffffLL) {
 #define GBX_SM_CALL(T, V) launch_softmax_vec<T, V, ATTN>(in, out, rows, L, ep, s)
         rc = GBX_ROW_DISPATCH(shape, GBX_SM_CALL, GBX_ERANGE);
 #undef GBX_SM_CALL
@@ -173,7 +207,7 @@ extern "C" int gbx_softmax_rows(const float* in, float* out, int64_t rows, int L
     if (rows < 0 || L <= 0) return set_error(GBX_EINVAL, "gbx_softmax_rows: rows=%lld L=%d", (long long)rows, L);
     if (rows == 0) return GBX_OK;
     if (!in || !out) return set_error(GBX_EINVAL, "gbx_softmax_rows: null pointer");
-    ScoreEpilogue ep{1, 0, 1.0f, false};
+    ScoreEpilogue ep{1, 0, 1.0f, false, make_fastdiv(1)};
     return launch_softmax<false>("gbx_softmax_rows", in, out, rows, L, ep, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -183,11 +217,12 @@ extern "C" int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t 
     if (rows < 0 || L <= 0 || S <= 0 || q_off < 0)
         return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: rows=%lld L=%d S=%d q_off=%d", (long long)rows, L, S,
                          q_off);
-    if (!(scale > 0.0f) || scale == INFINITY)
-        return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: scale=%g must be finite and > 0", (double)scale);
+    if (!(scale >= 1.17549435e-38f) || scale == INFINITY)   // a normal, finite, positive float
+        return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: scale=%g must be a normal positive float",
+                         (double)scale);
     if (rows == 0) return GBX_OK;
     if (!scores || !probs) return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: null pointer");
-    ScoreEpilogue ep{S, q_off, scale, causal != 0};
+    ScoreEpilogue ep{S, q_off, scale, causal != 0, make_fastdiv((uint32_t)S)};
     return launch_softmax<true>("gbx_attn_softmax_rows", scores, probs, rows, L, ep,
                                 reinterpret_cast<cudaStream_t>(stream));
 }

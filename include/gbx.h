@@ -19,9 +19,10 @@
  *   - Rows are contiguous (row stride = row length).  Outputs may alias the
  *     matching input where stated; rows are processed whole, so aliasing is
  *     safe exactly as stated.
- *   - Fast paths need 16-byte aligned pointers and a row length that is a
- *     multiple of 4 floats (8 elements for the embed tables); other shapes
- *     run a slower general kernel on the GPU with the same results.
+ *   - Fast paths need 16-byte aligned activation pointers and a row length
+ *     that is a multiple of 4 (embed: d a multiple of 4 and tables aligned
+ *     to 4 elements); other shapes run a slower general kernel on the GPU
+ *     with the same results.
  */
 #ifndef GBX_H
 #define GBX_H
@@ -141,10 +142,23 @@ int gbx_softmax_rows(const float* in, float* out, int64_t rows, int L, gbx_strea
  * `scores` holds the raw dot products q.k; entries past the causal limit
  * are never read (they may hold anything).  q_off shifts the diagonal:
  * 0 for prefill (L == S), L - S when S new queries follow L - S cached keys.
- * rows = matrices * S; probs may alias scores.
+ * rows = matrices * S; probs may alias scores.  scale must be a normal,
+ * finite, positive float (GBX_EINVAL otherwise).
  */
 int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t rows, int L, int S, int q_off,
                           float scale, int causal, gbx_stream_t stream);
+
+/*
+ * Tied-weight logits, replacing computeLogitsKernel (transformer.cu:296-307,
+ * launched at :898-900 on the final-LayerNorm row):
+ *   logits[r*vocab + v] = sum_j h[r*d + j] * dec(wte[v*d + j])
+ * for `rows` hidden rows (the reference has one), reading the token table in
+ * its GGUF dtype (dec() as in gbx_embed; no fp32 copy of the table).  The
+ * table crosses HBM once per 8 rows.  fp32 accumulation in a different order
+ * from the reference's sequential sum.
+ */
+int gbx_logits(const float* h, int64_t rows, const void* wte, int wte_dtype, float* logits, int vocab, int d,
+               gbx_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -60,6 +60,7 @@ def lib():
         L.gbxo_residual_ln_mt.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_int, ctypes.c_float, _c_int]
         L.gbxo_bias_gelu_mt.argtypes = [_vp, _vp, _vp, _c_i64, _c_int, _c_int]
         L.gbxo_softmax_rows_mt.argtypes = [_vp, _vp, _c_i64, _c_int, _c_int]
+        L.gbxo_logits_mt.argtypes = [_vp, _c_i64, _vp, _c_int, _vp, _c_int, _c_int, _c_int]
         L.gbxo_attn_softmax_mt.argtypes = [_vp, _vp, _c_i64, _c_int, _c_int, _c_int, ctypes.c_float, _c_int,
                                            _c_int]
         L.gbxo_max_threads.restype = _c_int
@@ -133,6 +134,29 @@ def softmax_rows(x, nthreads=1):
     return out
 
 
+def logits(h, wte, dtype, nthreads=1):
+    """Tied-weight logits [rows, vocab] of hidden rows h [rows, d] against a
+    GGUF-encoded token table wte [vocab, d]."""
+    h = np.ascontiguousarray(h, dtype=np.float32)
+    wte = np.ascontiguousarray(wte)
+    rows, d = h.reshape(-1, h.shape[-1]).shape
+    vocab = wte.shape[0]
+    out = np.empty((rows, vocab), dtype=np.float32)
+    lib().gbxo_logits_mt(_ptr(h), rows, _ptr(wte), dtype, _ptr(out), vocab, d, nthreads)
+    return out
+
+
+def dot_tolerance(h, wte_f32):
+    """Bound on the difference of two fp32 dot-product evaluations in different
+    orders: each is within gamma_d * sum_j |h_j w_j| of the exact value
+    (gamma_d = d u / (1 - d u), u = 2^-24), so they differ by at most twice
+    that.  Returns the [rows, vocab] bound (+1e-6 absolute)."""
+    d = h.shape[-1]
+    u = 2.0 ** -24
+    gamma = d * u / (1 - d * u)
+    return 1e-6 + 2 * gamma * (np.abs(h.astype(np.float64)) @ np.abs(wte_f32.astype(np.float64)).T)
+
+
 def attn_softmax_rows(raw, S, scale, q_off=0, causal=True, nthreads=1):
     """Score epilogue (raw / scale, -1e9 past the causal limit) + softmax."""
     raw = np.ascontiguousarray(raw, dtype=np.float32)
@@ -164,6 +188,11 @@ def ref():
         R.ref_gguf_has_tensor.argtypes = [_vp, ctypes.c_char_p]
         R.ref_gguf_has_tensor.restype = _c_int
         R.ref_gguf_config.argtypes = [_vp, _vp]
+        R.ref_model_open.argtypes = [ctypes.c_char_p]
+        R.ref_model_open.restype = _vp
+        R.ref_model_close.argtypes = [_vp]
+        R.ref_model_forward.argtypes = [_vp, _vp, _c_int, _vp, _c_i64]
+        R.ref_model_forward.restype = _c_i64
         for name, args in (("ref_launch_embed", [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp]),
                            ("ref_launch_layernorm", [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp]),
                            ("ref_launch_softmax", [_vp, _c_int, _c_int, _vp]),
@@ -203,6 +232,36 @@ class RefGGUF:
     def close(self):
         if self.h:
             ref().ref_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class RefModel:
+    """The reference's TransformerModel (transformer.cu:744-1051) loaded from a
+    GGUF file; forward() runs its whole GPU forward and returns the last
+    token's 50257 logits."""
+
+    def __init__(self, path: str):
+        self.h = ref().ref_model_open(path.encode())
+        if not self.h:
+            raise RuntimeError(f"reference TransformerModel failed to load {path}")
+
+    def forward(self, ids) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty(50257, dtype=np.float32)
+        n = ref().ref_model_forward(self.h, _ptr(ids), ids.size, _ptr(out), out.size)
+        if n < 0:
+            raise ValueError("reference logits larger than expected")
+        return out[:n].copy()
+
+    def close(self):
+        if self.h:
+            ref().ref_model_close(self.h)
             self.h = None
 
     def __del__(self):

@@ -19,6 +19,7 @@
  *   gbxo_bias_gelu       transformer.cu:272,276-277  ffnUpKernel epilogue
  *                        (same formula as geluKernel transformer.cu:68-75)
  *   gbxo_softmax_rows    transformer.cu:126-166   softmaxKernel
+ *   gbxo_logits          transformer.cu:296-307   computeLogitsKernel
  *   gbxo_attn_softmax    transformer.cu:213-232   attentionScoresKernel's
  *                        epilogue (dot / scale, -1e9f above the diagonal),
  *                        then transformer.cu:126-166 softmaxKernel
@@ -366,6 +367,31 @@ void gbxo_attn_softmax_mt(const float* in, float* out, int64_t rows, int L, int 
 {
     attn_ctx c = { in, out, L, S > 0 ? S : 1, q_off, causal, scale };
     parallel_rows(attn_rows, &c, rows, nthreads);
+}
+
+/* transformer.cu:296-307: logits[i] = sum_j hidden[j] * tokenEmb[i*d + j],
+ * accumulated sequentially from 0.0f (nvcc contracts each step into an FMA);
+ * tokenEmb is the fp32 table the reference's loader produced, i.e. the GGUF
+ * table decoded by the rules above.  `rows` hidden rows. */
+typedef struct { const float* h; const void* wte; int dtype; float* out; int vocab, d; int64_t rows; } logits_ctx;
+
+static void logits_part(void* c_, int64_t v0, int64_t v1)
+{
+    logits_ctx* c = (logits_ctx*)c_;
+    for (int64_t r = 0; r < c->rows; r++)
+        for (int64_t v = v0; v < v1; v++) {
+            const float* hr = c->h + r * c->d;
+            float sum = 0.0f;
+            for (int j = 0; j < c->d; j++) sum = fmaf(hr[j], decode_elem(c->wte, c->dtype, v * c->d + j), sum);
+            c->out[r * c->vocab + v] = sum;
+        }
+}
+
+void gbxo_logits_mt(const float* h, int64_t rows, const void* wte, int dtype, float* out, int vocab, int d,
+                    int nthreads)
+{
+    logits_ctx c = { h, wte, dtype, out, vocab, d, rows };
+    parallel_rows(logits_part, &c, vocab, nthreads);
 }
 
 /* Single-thread entry points (the checker's default). */

@@ -16,6 +16,12 @@
 //                         transformer.cu:839-842, one launch per head there)
 //   ref_launch_gelu       geluKernel (1 thread per element, block 256)
 //   ref_launch_add        addResidualKernel (1 thread per element, block 256)
+//   ref_model_*           TransformerModel::loadModel / forward (transformer.cu:
+//                         913-949): the reference's whole GPU forward, for the
+//                         end-to-end parity test of the drop-in TransformerModel.
+//                         forward is a private member there, so the reference's
+//                         source is compiled with `private` spelled `public`;
+//                         that changes access checking only, not code.
 //
 // The only deviation from the reference's launches is the stream argument:
 // the reference uses the legacy default stream; these take one.
@@ -35,8 +41,13 @@
 #include <limits>
 #include <iomanip>
 
+#include <cuda_runtime.h>
+#include <device_launch_parameters.h>
+
 #define main glassbox_reference_main
+#define private public
 #include "transformer.cu"
+#undef private
 #undef main
 
 extern "C" {
@@ -112,5 +123,26 @@ int ref_launch_add(float* out, const float* residual, int size, void* stream)
 }
 
 int ref_block_size(void) { return BLOCK_SIZE; }
+
+void* ref_model_open(const char* path)
+{
+    TransformerModel* m = new TransformerModel();
+    if (!m->loadModel(path)) { delete m; return nullptr; }
+    return m;
+}
+
+void ref_model_close(void* m) { delete static_cast<TransformerModel*>(m); }
+
+// TransformerModel::forward(tokenIDs): the last token's logits
+// (vocabSize = 50257 of them, transformer.cu:492).  Returns the count, or -1
+// when `cap` is too small.
+int64_t ref_model_forward(void* m, const int* ids, int n, float* logits, int64_t cap)
+{
+    std::vector<int> v(ids, ids + n);
+    std::vector<float> out = static_cast<TransformerModel*>(m)->forward(v);
+    if ((int64_t)out.size() > cap) return -1;
+    std::memcpy(logits, out.data(), out.size() * sizeof(float));
+    return (int64_t)out.size();
+}
 
 }  // extern "C"

@@ -22,7 +22,8 @@ def pytest_configure(config):
     # (the built .so files are not committed).
     if not os.path.exists(os.path.join(ROOT, "oracle", "libgbx_oracle.so")):
         subprocess.run(["make", "-C", os.path.join(ROOT, "oracle")], check=True)
-    if not os.path.exists(os.path.join(PKG_DIR, "libgbx.so")):
+    if not (os.path.exists(os.path.join(PKG_DIR, "libgbx.so")) and
+            os.path.exists(os.path.join(PKG_DIR, "libgbx_model.so"))):
         subprocess.run(["make", "-C", PKG_DIR, "-j8"], check=True)
 
 

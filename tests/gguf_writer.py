@@ -100,3 +100,44 @@ def raw_of(arr: np.ndarray, gtype: int) -> bytes:
         rounded = ((f + 0x7FFF + ((f >> 16) & 1)) >> 16).astype(np.uint16)
         return rounded.tobytes()
     raise ValueError(gtype)
+
+
+def tiny_gpt2_tensors(d=64, heads=4, ff=256, layers=2, ctx=32, vocab=50257, seed=0):
+    """Random-init GPT-2 weights under the reference's tensor names
+    (transformer.cu:806-807, 818-825, 860-865, 884-886), as fp32 numpy arrays
+    (outermost dimension first).  GPT-2-like scales: tables and matrices
+    ~N(0, 0.02), LayerNorm gains 1 + N(0, 0.1), biases ~N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    n = lambda *shape: (0.02 * rng.standard_normal(shape)).astype(np.float32)  # noqa: E731
+    gain = lambda k: (1 + 0.1 * rng.standard_normal(k)).astype(np.float32)    # noqa: E731
+    t = {"token_embd.weight": n(vocab, d), "position_embd.weight": n(ctx, d)}
+    for l in range(layers):
+        p = f"blk.{l}."
+        t[p + "attn_norm.weight"] = gain(d)
+        t[p + "attn_norm.bias"] = n(d)
+        t[p + "attn_qkv.weight"] = n(3 * d, d)
+        t[p + "attn_qkv.bias"] = n(3 * d)
+        t[p + "attn_output.weight"] = n(d, d)
+        t[p + "attn_output.bias"] = n(d)
+        t[p + "ffn_norm.weight"] = gain(d)
+        t[p + "ffn_norm.bias"] = n(d)
+        t[p + "ffn_up.weight"] = n(ff, d)
+        t[p + "ffn_up.bias"] = n(ff)
+        t[p + "ffn_down.weight"] = n(d, ff)
+        t[p + "ffn_down.bias"] = n(d)
+    t["output_norm.weight"] = gain(d)
+    t["output_norm.bias"] = n(d)
+    return t
+
+
+def write_tiny_gpt2(path, gtype=GGML_F32, d=64, heads=4, ff=256, layers=2, ctx=32, vocab=50257, seed=0,
+                    table_gtype=None):
+    """A complete GPT-2 GGUF the reference's TransformerModel loads.  Every
+    tensor in `gtype`; the two embedding tables in `table_gtype` when given."""
+    tensors = tiny_gpt2_tensors(d, heads, ff, layers, ctx, vocab, seed)
+    items = []
+    for name, arr in tensors.items():
+        gt = table_gtype if (table_gtype is not None and name.endswith("embd.weight")) else gtype
+        items.append((name, list(arr.shape), gt, raw_of(arr, gt)))
+    write_gguf(path, gpt2_kv(d=d, layers=layers, heads=heads, ff=ff, ctx=ctx), items)
+    return tensors

@@ -22,18 +22,30 @@ def test_header_declares_entry_points():
         assert n in names
 
 
-def test_library_exports_every_declared_symbol(gbx):
-    L = ctypes.CDLL(gbx.LIB_PATH)
+def _libraries(gbx):
+    import importlib
+    gm = importlib.import_module("glassboxai-transformer_b200.model")
+    return {"gbx.h": (gbx.LIB_PATH, gbx.SIGNATURES), "gbx_model.h": (gm.LIB_PATH, gm.SIGNATURES)}
+
+
+def test_every_header_has_a_library(gbx):
     import glob
-    for header in glob.glob(os.path.join(ROOT, "include", "*.h")):
-        for name in _declared(header):
-            assert hasattr(L, name), f"{name} declared in {os.path.basename(header)} but not exported"
+    headers = {os.path.basename(h) for h in glob.glob(os.path.join(ROOT, "include", "*.h"))}
+    assert headers == set(_libraries(gbx))
+
+
+def test_library_exports_every_declared_symbol(gbx):
+    for header, (path, _) in _libraries(gbx).items():
+        L = ctypes.CDLL(path)
+        for name in _declared(os.path.join(ROOT, "include", header)):
+            assert hasattr(L, name), f"{name} declared in {header} but not exported by {os.path.basename(path)}"
 
 
 def test_binding_signatures_cover_header(gbx):
-    names = _declared(os.path.join(ROOT, "include", "gbx.h"))
-    missing = [n for n in names if n not in gbx.SIGNATURES]
-    assert not missing, missing
+    for header, (_, sigs) in _libraries(gbx).items():
+        names = _declared(os.path.join(ROOT, "include", header))
+        missing = [n for n in names if n not in sigs]
+        assert not missing, (header, missing)
 
 
 def test_status_strings(gbx):

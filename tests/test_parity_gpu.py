@@ -424,10 +424,43 @@ def test_attn_softmax_unaligned_general_path(gbx, orc, cuda):
 def test_attn_softmax_argument_errors(gbx, cuda):
     import torch
     a = torch.zeros((4, 8), device="cuda")
-    for kw in (dict(scale=0.0), dict(scale=-1.0), dict(scale=float("inf")), dict(scale=1.0, S=0),
+    for kw in (dict(scale=0.0), dict(scale=-1.0), dict(scale=float("inf")), dict(scale=1e-39), dict(scale=1.0, S=0),
                dict(scale=1.0, q_off=-1)):
         args = dict(rows=4, L=8, S=4, q_off=0)
         args.update(kw)
         with pytest.raises(gbx.GbxError) as e:
             gbx.attn_softmax_rows(a, a, **args)
         assert e.value.status == 1
+
+
+# ---------------------------------------------------------------------------
+# tied-weight logits
+
+@pytest.mark.parametrize("dtype", [0, 1, 30])
+@pytest.mark.parametrize("rows,d", [(1, 1600), (3, 768), (8, 1024), (11, 64), (2, 30)])
+def test_logits(gbx, orc, cuda, dtype, rows, d):
+    import torch
+    rng = np.random.default_rng(rows * 1000 + d + dtype)
+    V = 3001
+    wte = _table(rng, V, d, dtype, 0.02)
+    h = rng.standard_normal((rows, d)).astype(np.float32)
+    full, out = _guarded((rows, V), torch)
+    gbx.logits(_t(h, torch), _t(wte, torch), dtype, out, rows=rows, vocab=V, d=d)
+    ref = orc.logits(h, wte, dtype)
+    tol = orc.dot_tolerance(h, orc.dequant(wte, dtype).reshape(V, d))
+    err = np.abs(out.cpu().numpy().astype(np.float64) - ref)
+    assert np.all(err <= tol), f"logits: worst excess {np.max(err - tol):.3g}"
+    _check_guards(full)
+
+
+def test_logits_unaligned_rows_general_path(gbx, orc, cuda):
+    import torch
+    rng = np.random.default_rng(5)
+    V, d = 517, 101
+    wte = _table(rng, V, d, 30, 0.02)
+    h = rng.standard_normal((2, d)).astype(np.float32)
+    out = torch.empty((2, V), device="cuda")
+    gbx.logits(_t(h, torch), _t(wte, torch), 30, out, rows=2, vocab=V, d=d)
+    ref = orc.logits(h, wte, 30)
+    tol = orc.dot_tolerance(h, orc.dequant(wte, 30).reshape(V, d))
+    assert np.all(np.abs(out.cpu().numpy() - ref) <= tol)

@@ -37,24 +37,31 @@ sys.path.insert(0, ROOT)
 
 METRIC = "layer-kernel HBM GB/s (% of B200 peak); tokens/s at GPT-2 XL shape, 1-8 GPU"
 
-# name -> (ChainShape kwargs, description, Chain kwargs)
+# name -> (ChainShape kwargs, description, Chain kwargs, scaling)
+#   weak:   every rank runs the whole batch given here (per-GPU work fixed as N grows)
+#   strong: the batch given here is the global batch, split across ranks by whole sequences
 WORKLOADS = {
     "gpt2-xl-prefill": (dict(batch=32, seq=1024, d=1600, ff=6400, heads=25, layers=48, vocab=50257, n_ctx=1024,
                              table_dtype=30),
                         "GPT-2 XL prefill B32xS1024 per GPU, d1600, ff6400, 25 heads, 48 layers, bf16 GGUF tables",
-                        dict(score_std=1.0)),
+                        dict(score_std=1.0), "weak"),
     "gpt2-medium-prefill": (dict(batch=8, seq=1024, d=1024, ff=4096, heads=16, layers=24, vocab=50257, n_ctx=1024,
                                  table_dtype=1),
                             "GPT-2 medium prefill B8xS1024, d1024, ff4096, 16 heads, 24 layers, f16 GGUF tables",
-                            dict(score_std=1.0)),
+                            dict(score_std=1.0), "weak"),
     "gpt2-xl-decode": (dict(batch=256, seq=1, d=1600, ff=6400, heads=25, layers=48, vocab=50257, n_ctx=2048,
                             table_dtype=30, kv_len=2048, pos_off=2047),
                        "GPT-2 XL decode step B256xS1 at position 2047, 2048-long softmax rows, d1600, ff6400, "
-                       "25 heads, 48 layers, bf16 tables", dict(score_std=math.sqrt(2.0))),
+                       "25 heads, 48 layers, bf16 tables", dict(score_std=math.sqrt(2.0)), "weak"),
     "gpt2-small-chain": (dict(batch=1, seq=64, d=768, ff=3072, heads=12, layers=12, vocab=50257, n_ctx=1024,
                               table_dtype=0),
                          "GPT-2 small chain B1xS64, d768, ff3072, 12 heads, 12 layers, f32 tables",
-                         dict(score_std=1.0)),
+                         dict(score_std=1.0), "weak"),
+    "tokens-1m-sharded": (dict(batch=512, seq=2048, d=4096, ff=16384, heads=32, layers=1, vocab=50257, n_ctx=2048,
+                               table_dtype=1, chunk=64),
+                          "1,048,576 tokens (B512xS2048) split by whole sequences across the GPUs, d4096, ff16384, "
+                          "32 heads, f16 tables; embed + one layer of the chain + final LN per step, in passes of "
+                          "64 sequences", dict(score_std=1.0), "strong"),
 }
 DEFAULT_WORKLOAD = "gpt2-xl-prefill"
 
@@ -153,7 +160,8 @@ def dist_setup(n_gpus):
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        timeout = float(os.environ.get("GBX_PG_TIMEOUT_S", "120"))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout))
     return rank, world, local
 
 
@@ -239,7 +247,8 @@ def cpu_baseline(shape, budget_s=12.0):
 
 # ---------------------------------------------------------------------------
 
-def run_ours(args, shape, desc, chain_kw):
+def run_ours(args, shape, desc, chain_kw, scaling):
+    import dataclasses
     import torch
     rank, world, local = dist_setup(args.gpus)
     assert torch.cuda.is_available(), "bench.py needs a CUDA device"
@@ -247,6 +256,11 @@ def run_ours(args, shape, desc, chain_kw):
     torch.cuda.set_device(device)
     from importlib import import_module
     chain_mod = import_module("glassboxai-transformer_b200.chain")
+    shard = import_module("glassboxai-transformer_b200.shard")
+    global_batch = shape.batch * (world if scaling == "weak" else 1)
+    if scaling == "strong":
+        first, count = shard.shard_sequences(shape.batch, rank, world)
+        shape = dataclasses.replace(shape, batch=count)
     chain = chain_mod.Chain(shape, device, seed=1000 + rank, **chain_kw)
     stream = torch.cuda.current_stream(device)
     torch.cuda.synchronize(device)
@@ -256,15 +270,23 @@ def run_ours(args, shape, desc, chain_kw):
     torch.cuda.synchronize(device)
     assert int(chain.err.item()) == 0, "embed reported out-of-range ids"
 
-    # --- device-resident timing -------------------------------------------------
     timers = {}
+    if args.graph:
+        chain.capture_graph(timers=timers)
+        chain.replay()
+        torch.cuda.synchronize(device)
+
+    # --- device-resident timing -------------------------------------------------
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize(device)
     with ClockSampler(device.index if device.index is not None else 0) as clk:
         start.record(stream)
         for _ in range(args.steps):
-            chain.step(stream, timers=timers)
+            if args.graph:
+                chain.replay()
+            else:
+                chain.step(stream, timers=timers)
         end.record(stream)
         torch.cuda.synchronize(device)
     barrier(world)
@@ -278,7 +300,7 @@ def run_ours(args, shape, desc, chain_kw):
         kernels[name] = {"launches": len(durs), "avg_us": 1000.0 * sum(durs) / len(durs)}
     byte_of = {"embed": shape.bytes_embed(), "layernorm": shape.bytes_ln(),
                "residual_layernorm": shape.bytes_residual_ln(), "softmax_rows": shape.bytes_softmax(),
-               "bias_gelu": shape.bytes_gelu(), "final_layernorm": 16 * shape.batch * shape.d + 8 * shape.d}
+               "bias_gelu": shape.bytes_gelu(), "final_layernorm": shape.bytes_final()}
     peak, peak_kind = load_peak()
     for name, k in kernels.items():
         k["bytes_per_launch"] = byte_of[name]
@@ -288,27 +310,32 @@ def run_ours(args, shape, desc, chain_kw):
     # --- end to end through the API with host buffers -----------------------------
     ids_host = chain.ids.cpu().pin_memory()
     out_host = torch.empty(chain.out.shape, dtype=torch.float32).pin_memory()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def e2e_step():
+        chain.ids.copy_(ids_host, non_blocking=True)      # H2D of the step's token ids
+        if args.graph:
+            chain.replay()
+        else:
+            chain.step(stream)
+        out_host.copy_(chain.out, non_blocking=True)      # D2H of the step's result
+        stream.synchronize()                              # the caller reads the result
+
     for _ in range(2):
-        chain.ids.copy_(ids_host, non_blocking=True)
-        chain.step(stream)
-        out_host.copy_(chain.out, non_blocking=True)
-        stream.synchronize()
+        e2e_step()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize(device)
     e_start.record(stream)
     for _ in range(args.steps):
-        chain.ids.copy_(ids_host, non_blocking=True)      # H2D of the step's token ids
-        chain.step(stream)
-        out_host.copy_(chain.out, non_blocking=True)      # D2H of the step's result
-        stream.synchronize()                              # the caller reads the result
+        e2e_step()
     e_end.record(stream)
     torch.cuda.synchronize(device)
     barrier(world)
     e_ms = max_over_ranks(e_start.elapsed_time(e_end), world, device) / args.steps
 
-    tokens_total = shape.tokens * world
-    sm = kernels["softmax_rows"]
+    tokens_total = global_batch * shape.seq
+    top = "softmax_rows" if "softmax_rows" in kernels else max(kernels, key=lambda k: kernels[k]["avg_us"])
+    sm = kernels[top]
     result = {
         "metric": METRIC,
         "value": tokens_total / (ms_per_step * 1e-3),
@@ -318,35 +345,40 @@ def run_ours(args, shape, desc, chain_kw):
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": "f32 (activations; tables " + {0: "f32", 1: "f16", 30: "bf16"}[shape.table_dtype] + ")",
         "data": "synthetic (seeded torch.randn / randint on device; random-init tables)",
         "config": {"workload": args.workload, "description": desc, "tokens_per_gpu": shape.tokens,
-                   "global_batch": shape.batch * world, "seq_len": shape.seq, "layers": shape.layers,
+                   "global_batch": global_batch, "seq_len": shape.seq, "layers": shape.layers,
+                   "chunks_per_step": shape.n_chunks, "cuda_graph": bool(args.graph),
                    "parallelism": f"row shards of whole sequences over {world} GPU(s), no collective",
                    "l2": "no flush; every streamed buffer is larger than the 126 MB L2 "
-                         f"(smallest: {shape.tokens * shape.d * 4 / 1e6:.0f} MB)"},
+                         f"(smallest: {shape.chunk_tokens * shape.d * 4 / 1e6:.0f} MB)"
+                   if shape.chunk_tokens * shape.d * 4 > 126e6 else
+                   "inputs smaller than L2 (decode-sized rows); no flush"},
         "hbm": {"bytes_per_step": shape.bytes_per_step(),
                 "gbs": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
                 "frac": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9 / peak,
                 "peak": peak, "peak_kind": peak_kind},
-        "roofline": {"kernel": "softmax_rows", "bound": "hbm", "achieved": sm["gbs"], "peak": peak,
+        "roofline": {"kernel": top, "bound": "hbm", "achieved": sm["gbs"], "peak": peak,
                      "unit": "GB/s", "frac": sm["gbs"] / peak, "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_launch": shape.bytes_softmax(),
-                     "traffic": traffic_from_profiles("softmax_rows", args.workload)},
+                     "algorithmic_bytes_per_launch": byte_of[top],
+                     "traffic": traffic_from_profiles(top, args.workload)},
         "kernels": kernels,
         "gpu_launches": shape.launches_per_step() * args.steps,
         "clocks": clk.summary(),
         "e2e": {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(chain.ids.numel() * 4), "d2h_bytes_per_step": int(chain.out.numel() * 4),
                 "ms_per_step": e_ms,
-                "path": "C ABI launches (ctypes) with pinned host token ids in, final LayerNorm rows out"},
+                "path": "C ABI launches with pinned host token ids in, final LayerNorm rows out"
+                        + (" (step replayed as a CUDA graph)" if args.graph else "")},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(shape)
     if rank == 0:
         print(json.dumps(result), flush=True)
+    chain.graph = None
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -361,7 +393,7 @@ def reference_gpu_kernels(shape):
         return {"unavailable": "reference build (oracle/_ref) not present"}
     R = oracle.ref()
     dev = torch.device("cuda", 0)
-    N, d, F = shape.tokens, shape.d, shape.ff
+    N, d, F = shape.chunk_tokens, shape.d, shape.ff
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     f32 = dict(dtype=torch.float32, device=dev)
@@ -371,9 +403,9 @@ def reference_gpu_kernels(shape):
     gam = torch.randn((d,), generator=g, **f32)
     bet = torch.randn((d,), generator=g, **f32)
     ffn = torch.randn((N, F), generator=g, **f32)
-    scores = torch.randn((shape.batch * shape.heads * shape.seq, shape.L), generator=g, **f32)
+    scores = torch.randn((shape.chunk_seqs * shape.heads * shape.seq, shape.L), generator=g, **f32)
     per_launch_rows = shape.seq          # one launch per head of one sequence (transformer.cu:839-842)
-    n_sm_launch = shape.batch * shape.heads
+    n_sm_launch = shape.chunk_seqs * shape.heads
 
     def timed(fn, reps=3):
         fn()
@@ -409,7 +441,7 @@ def reference_gpu_kernels(shape):
     del h, x, y, ffn, scores
     torch.cuda.empty_cache()
     emb = ("launch failure as shipped: embedTokensKernel uses blockDim = d = %d > 1024" % d) if d > 1024 else None
-    return {"tokens_per_s_chain_without_embed": shape.tokens / (shape.layers * layer),
+    return {"tokens_per_s_chain_without_embed": N / (shape.layers * layer),
             "per_kernel": {k: {"ms": v * 1e3, "algorithmic_gbs": algo[k] / v / 1e9} for k, v in t.items()},
             "embed": emb or "not timed",
             "note": "one layer timed (LN x2, residual add x2, softmax per head of each sequence, GELU in place), "
@@ -542,12 +574,14 @@ def main():
                                          "bias_gelu"],
                     help="time one kernel alone on --rows rows of the workload's shape")
     ap.add_argument("--rows", type=int, default=65536)
+    ap.add_argument("--graph", action="store_true",
+                    help="capture one step in a CUDA graph and replay it (launch-bound workloads)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
         relaunch_distributed(args.gpus)
-    shape_kw, desc, chain_kw = WORKLOADS[args.workload]
+    shape_kw, desc, chain_kw, scaling = WORKLOADS[args.workload]
     chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
     shape = chain_mod.ChainShape(**shape_kw)
     if args.kernel:
@@ -555,7 +589,7 @@ def main():
     elif args.impl == "reference":
         run_reference(args, shape, desc)
     else:
-        run_ours(args, shape, desc, chain_kw)
+        run_ours(args, shape, desc, chain_kw, scaling)
 
 
 if __name__ == "__main__":

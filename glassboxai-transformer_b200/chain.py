@@ -22,7 +22,13 @@ kernels would:
                                                         sequence's last row)
 
 Rows are independent, so a batch of B whole sequences is one call per
-kernel (the reference launches per head and has no batch dimension).
+kernel (the reference launches per head and has no batch dimension).  When
+the batch needs more device memory than one pass should hold, it runs in
+chunks of ``chunk`` sequences through the same buffers, one chain pass per
+chunk (each chunk's token ids are its own slice).
+
+``capture_graph`` records one step into a CUDA graph; ``replay`` launches it
+(the decode-sized chains are launch-bound without it).
 """
 from __future__ import annotations
 
@@ -45,10 +51,23 @@ class ChainShape:
     table_dtype: int = 30     # GGUF dtype of wte / wpe
     kv_len: int | None = None  # softmax row length (defaults to seq: causal prefill)
     pos_off: int = 0
+    chunk: int | None = None   # sequences per pass (default: the whole batch)
 
     @property
     def tokens(self):
         return self.batch * self.seq
+
+    @property
+    def chunk_seqs(self):
+        return min(self.batch, self.chunk or self.batch)
+
+    @property
+    def n_chunks(self):
+        return -(-self.batch // self.chunk_seqs)
+
+    @property
+    def chunk_tokens(self):
+        return self.chunk_seqs * self.seq
 
     @property
     def L(self):
@@ -56,39 +75,48 @@ class ChainShape:
 
     @property
     def softmax_rows(self):
-        return self.batch * self.heads * self.seq
+        return self.chunk_seqs * self.heads * self.seq
 
     def table_es(self):
         return 4 if self.table_dtype == 0 else 2
 
-    # Algorithmic bytes per launch (each input read once, each output written once).
+    # Algorithmic bytes per launch (each input read once, each output written
+    # once), for one chunk.
     def bytes_embed(self):
         # ids + gathered wte rows + distinct wpe rows + output
         distinct_pos = min(self.seq, self.n_ctx)
-        return 4 * self.tokens + self.tokens * self.d * self.table_es() + distinct_pos * self.d * self.table_es() \
-            + 4 * self.tokens * self.d
+        t = self.chunk_tokens
+        return 4 * t + t * self.d * self.table_es() + distinct_pos * self.d * self.table_es() + 4 * t * self.d
 
     def bytes_ln(self, rows=None):
-        rows = self.tokens if rows is None else rows
+        rows = self.chunk_tokens if rows is None else rows
         return 8 * rows * self.d + 8 * self.d
 
     def bytes_residual_ln(self, rows=None):
-        rows = self.tokens if rows is None else rows
+        rows = self.chunk_tokens if rows is None else rows
         return 16 * rows * self.d + 8 * self.d
 
     def bytes_gelu(self):
-        return 8 * self.tokens * self.ff + 4 * self.ff
+        return 8 * self.chunk_tokens * self.ff + 4 * self.ff
 
     def bytes_softmax(self):
         return 8 * self.softmax_rows * self.L
 
-    def launches_per_step(self):
+    def bytes_final(self):
+        return 16 * self.chunk_seqs * self.d + 8 * self.d
+
+    def launches_per_chunk(self):
         return 1 + 1 + 4 * self.layers - 1 + 1
 
-    def bytes_per_step(self):
-        final = 16 * self.batch * self.d + 8 * self.d
+    def launches_per_step(self):
+        return self.n_chunks * self.launches_per_chunk()
+
+    def bytes_per_chunk(self):
         return (self.bytes_embed() + self.bytes_ln() + (2 * self.layers - 1) * self.bytes_residual_ln()
-                + self.layers * (self.bytes_softmax() + self.bytes_gelu()) + final)
+                + self.layers * (self.bytes_softmax() + self.bytes_gelu()) + self.bytes_final())
+
+    def bytes_per_step(self):
+        return self.n_chunks * self.bytes_per_chunk()
 
 
 class Chain:
@@ -121,7 +149,7 @@ class Chain:
         self.wte = table(s.vocab)
         self.wpe = table(s.n_ctx)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
-        N, d, F = s.tokens, s.d, s.ff
+        N, d, F = s.chunk_tokens, s.d, s.ff
         self.h = torch.empty((N, d), **f32)
         self.ln = torch.empty((N, d), **f32)
         self.attn_out = normal((N, d), act_std)
@@ -141,28 +169,18 @@ class Chain:
         self.up_bias = normal((s.layers, F), 0.02)
         self.gf = normal((d,), 0.1, 1.0)
         self.bf = normal((d,), 0.02)
-        self.last_h = torch.empty((s.batch, d), **f32)
-        self.last_f = torch.empty((s.batch, d), **f32)
+        B = s.chunk_seqs
+        self.last_h = torch.empty((B, d), **f32)
+        self.last_f = torch.empty((B, d), **f32)
         self.out = torch.empty((s.batch, d), **f32)
+        self.graph = None
 
-    def step(self, stream=None, timers=None):
+    def _chunk(self, c, st, run):
         import torch
         s, G = self.s, _gbx
-        st = stream if stream is not None else torch.cuda.current_stream(self.device)
-
-        def run(name, fn):
-            if timers is None:
-                fn()
-                return
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record(st)
-            fn()
-            b.record(st)
-            timers.setdefault(name, []).append((a, b))
-
-        N, d = s.tokens, s.d
-        run("embed", lambda: G.embed(self.ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, self.h, n_tok=N,
+        N, d, B = s.chunk_tokens, s.d, s.chunk_seqs
+        ids = self.ids[c * N:(c + 1) * N]
+        run("embed", lambda: G.embed(ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, self.h, n_tok=N,
                                      d=d, vocab=s.vocab, n_ctx=s.n_ctx, seq=s.seq, pos_off=s.pos_off,
                                      err_flag=self.err, stream=st))
         for l in range(s.layers):
@@ -182,8 +200,43 @@ class Chain:
                                                  stream=st))
         # final residual add + ln_f on each sequence's last row (transformer.cu:890-896)
         with torch.cuda.stream(st):
-            self.last_h.copy_(self.h.view(s.batch, s.seq, d)[:, -1])
-            self.last_f.copy_(self.ffn_out.view(s.batch, s.seq, d)[:, -1])
-        run("final_layernorm", lambda: G.residual_layernorm(self.last_f, self.last_h, None, self.out, self.gf,
-                                                            self.bf, rows=s.batch, d=d, stream=st))
+            self.last_h.copy_(self.h.view(B, s.seq, d)[:, -1])
+            self.last_f.copy_(self.ffn_out.view(B, s.seq, d)[:, -1])
+        out = self.out[c * B:(c + 1) * B]
+        run("final_layernorm", lambda: G.residual_layernorm(self.last_f, self.last_h, None, out, self.gf,
+                                                            self.bf, rows=B, d=d, stream=st))
+
+    def step(self, stream=None, timers=None):
+        import torch
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+
+        def run(name, fn):
+            if timers is None:
+                fn()
+                return
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            timers.setdefault(name, []).append((a, b))
+
+        for c in range(self.s.n_chunks):
+            self._chunk(c, st, run)
+        return self.out
+
+    def capture_graph(self, timers=None):
+        """Record one step into a CUDA graph (launches on the capture stream).
+        With ``timers``, the graph also records an event pair around every
+        launch; after a replay they time that replay's kernels."""
+        import torch
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.step(torch.cuda.current_stream(self.device), timers=timers)
+        torch.cuda.synchronize(self.device)
+        return self.graph
+
+    def replay(self):
+        self.graph.replay()
         return self.out

@@ -158,10 +158,12 @@ def dist_setup(n_gpus):
         import torch
         import torch.distributed as dist
         backend = "nccl" if torch.cuda.is_available() else "gloo"
+        timeout = datetime.timedelta(seconds=float(os.environ.get("GBX_PG_TIMEOUT_S", "120")))
         if backend == "nccl":
             torch.cuda.set_device(local)
-        timeout = float(os.environ.get("GBX_PG_TIMEOUT_S", "120"))
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout))
+            dist.init_process_group(backend, timeout=timeout, device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group(backend, timeout=timeout)
     return rank, world, local
 
 

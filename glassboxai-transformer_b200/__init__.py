@@ -51,6 +51,7 @@ SIGNATURES = {
     "gbx_softmax_rows": [_vp, _vp, _i64, _int, _vp],
     "gbx_attn_softmax_rows": [_vp, _vp, _i64, _int, _int, _int, _f, _int, _vp],
     "gbx_logits": [_vp, _i64, _vp, _int, _vp, _int, _int, _vp],
+    "gbx_select_tokens": [_vp, _i64, _int, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
 }
 _RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
 
@@ -141,3 +142,9 @@ def attn_softmax_rows(scores, probs, *, rows, L, S, scale, q_off=0, causal=True,
 
 def logits(h, wte, wte_dtype, out, *, rows, vocab, d, stream=None):
     _check(lib().gbx_logits(_p(h), rows, _p(wte), wte_dtype, _p(out), vocab, d, _stream(stream)))
+
+
+def select_tokens(logits, out_ids, *, rows, vocab, temperature=0.0, uniforms=None, out_best=None,
+                  out_best_logit=None, stream=None):
+    _check(lib().gbx_select_tokens(_p(logits), rows, vocab, float(temperature), _p(uniforms), _p(out_ids),
+                                   _p(out_best), _p(out_best_logit), _stream(stream)))

@@ -125,4 +125,19 @@ int gbx_model_forward(gbx_model* m, const int32_t* ids_host, int64_t n_ids, int 
     return GBX_OK;
 }
 
+int gbx_model_next_token(gbx_model* m, const int32_t* ids_host, int64_t n_ids, double temperature, double u,
+                         int32_t* out_id, int32_t* best, float* best_logit)
+{
+    if (!m || !ids_host || !out_id || n_ids <= 0) return gbx::set_error(GBX_EINVAL, "gbx_model_next_token: bad argument");
+    std::vector<int> ids(ids_host, ids_host + n_ids);
+    int b = 0;
+    float bl = 0.0f;
+    const int sel = m->model.nextTokenWithDraw(ids, temperature, u, &b, &bl);
+    if (sel < 0) return gbx::set_error(GBX_EINVAL, "%s", m->model.lastError().c_str());
+    *out_id = sel;
+    if (best) *best = b;
+    if (best_logit) *best_logit = bl;
+    return GBX_OK;
+}
+
 }  // extern "C"

@@ -27,6 +27,7 @@
 //   gbx_residual_layernorm on each sequence's last row
 //                                          last = LN_f(h + down + b_down)  (:890-896)
 //   gbx_logits                             logits = last . wte^T           (:898-900)
+//   (nextToken) gbx_select_tokens          argmax / temperature sampling   (:994-1028)
 //
 // The GEMMs are fp32 cuBLAS (CUBLAS_COMPUTE_32F, no TF32), the reference's
 // precision; their outputs differ from the reference's sequential GEMV sums
@@ -35,6 +36,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <random>
 
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
@@ -94,6 +96,10 @@ struct TransformerModel::Impl {
     int32_t* ids = nullptr;
     size_t ids_n = 0;
     int32_t* err = nullptr;
+    // next-token selection: [selected, best], best logit, the uniform draw
+    int32_t* sel_ids = nullptr;
+    float* sel_logit = nullptr;
+    double* sel_u = nullptr;
     // weights (device pointers owned by the loader)
     struct Layer {
         const float *ln1_g, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b, *ln2_g, *ln2_b, *up_w, *up_b, *down_w,
@@ -110,6 +116,9 @@ struct TransformerModel::Impl {
             b->release();
         if (ids) cudaFree(ids);
         if (err) cudaFree(err);
+        if (sel_ids) cudaFree(sel_ids);
+        if (sel_logit) cudaFree(sel_logit);
+        if (sel_u) cudaFree(sel_u);
         if (blas) cublasDestroy(blas);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -139,7 +148,9 @@ bool TransformerModel::loadModel(const std::string& ggufPath)
     if (cublasCreate(&m.blas) != CUBLAS_STATUS_SUCCESS) return fail("cublasCreate failed");
     cublasSetStream(m.blas, m.stream);
     cublasSetMathMode(m.blas, CUBLAS_DEFAULT_MATH);   // fp32 SGEMM; TF32 is never enabled
-    if (cudaMalloc(&m.err, sizeof(int32_t)) != cudaSuccess) return fail("cudaMalloc");
+    if (cudaMalloc(&m.err, sizeof(int32_t)) != cudaSuccess || cudaMalloc(&m.sel_ids, 2 * sizeof(int32_t)) != cudaSuccess ||
+        cudaMalloc(&m.sel_logit, sizeof(float)) != cudaSuccess || cudaMalloc(&m.sel_u, sizeof(double)) != cudaSuccess)
+        return fail("cudaMalloc");
 
     embedDim_ = loader_.getEmbedDim();
     numLayers_ = loader_.getNumLayers();
@@ -218,23 +229,81 @@ std::vector<float> TransformerModel::forward(const std::vector<int>& tokenIDs) {
 std::vector<float> TransformerModel::forwardBatch(const std::vector<int>& tokenIDs, int batch)
 {
     Impl& m = *impl_;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    std::vector<float> out;
+    if (runForward(tokenIDs, batch)) {
+        out.resize((size_t)batch * vocab_);
+        if (cudaMemcpyAsync(out.data(), m.logits.p, out.size() * sizeof(float), cudaMemcpyDeviceToHost, m.stream) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(m.stream) != cudaSuccess) {
+            fail("device-to-host copy of the logits failed");
+            out.clear();
+        }
+    }
+    if (cur >= 0 && cur != m.device) cudaSetDevice(cur);
+    return out;
+}
+
+int TransformerModel::nextToken(const std::vector<int>& tokenIDs, double temperature, std::mt19937& rng, int* bestID,
+                                float* bestLogit)
+{
+    // the reference draws only when it samples (transformer.cu:1017-1018),
+    // after its forward; the draw does not depend on the logits
+    double u = 0.0;
+    if (temperature > 0.01) u = std::uniform_real_distribution<double>(0.0, 1.0)(rng);
+    return nextTokenWithDraw(tokenIDs, temperature, u, bestID, bestLogit);
+}
+
+int TransformerModel::nextTokenWithDraw(const std::vector<int>& tokenIDs, double temperature, double u, int* bestID,
+                                        float* bestLogit)
+{
+    Impl& m = *impl_;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    int selected = -1;
+    if (runForward(tokenIDs, 1)) {
+        int32_t host[2] = {0, 0};
+        float blog = 0.0f;
+        int rc = GBX_OK;
+        if (cudaMemcpyAsync(m.sel_u, &u, sizeof(double), cudaMemcpyHostToDevice, m.stream) != cudaSuccess)
+            rc = GBX_ECUDA;
+        if (rc == GBX_OK)
+            rc = gbx_select_tokens(m.logits.p, 1, vocab_, temperature, m.sel_u, m.sel_ids, m.sel_ids + 1, m.sel_logit,
+                                   reinterpret_cast<gbx_stream_t>(m.stream));
+        if (rc == GBX_OK &&
+            (cudaMemcpyAsync(host, m.sel_ids, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, m.stream) != cudaSuccess ||
+             cudaMemcpyAsync(&blog, m.sel_logit, sizeof(float), cudaMemcpyDeviceToHost, m.stream) != cudaSuccess ||
+             cudaStreamSynchronize(m.stream) != cudaSuccess))
+            rc = GBX_ECUDA;
+        if (rc == GBX_OK) {
+            selected = host[0];
+            if (bestID) *bestID = host[1];
+            if (bestLogit) *bestLogit = blog;
+        } else {
+            fail(std::string("token selection failed: ") + gbx_last_error());
+        }
+    }
+    if (cur >= 0 && cur != m.device) cudaSetDevice(cur);
+    return selected;
+}
+
+bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
+{
+    Impl& m = *impl_;
     err_.clear();
-    if (!loader_.isLoaded() || !m.blas) return fail("model not loaded"), std::vector<float>();
+    if (!loader_.isLoaded() || !m.blas) return fail("model not loaded");
     if (batch <= 0 || tokenIDs.empty() || tokenIDs.size() % (size_t)batch)
-        return fail("forward: need batch > 0 sequences of equal, non-zero length"), std::vector<float>();
+        return fail("forward: need batch > 0 sequences of equal, non-zero length");
     const int64_t N = (int64_t)tokenIDs.size();
     const int S = (int)(N / batch);
     if (S > nCtx_)
         return fail("forward: " + std::to_string(S) + " tokens exceed the " + std::to_string(nCtx_) +
-                    " position rows"),
-               std::vector<float>();
+                    " position rows");
     for (int id : tokenIDs)
-        if (id < 0 || id >= vocab_)
-            return fail("forward: token id " + std::to_string(id) + " outside the token table"), std::vector<float>();
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (cur != m.device) cudaSetDevice(m.device);
-    if (!ensureBuffers(N, S)) return {};
+        if (id < 0 || id >= vocab_) return fail("forward: token id " + std::to_string(id) + " outside the token table");
+    cudaSetDevice(m.device);
+    if (!ensureBuffers(N, S)) return false;
 
     const int d = embedDim_, H = numHeads_, hd = headDim_, F = ffnDim_, V = vocab_;
     const float one = 1.0f, zero = 0.0f;
@@ -257,7 +326,7 @@ std::vector<float> TransformerModel::forwardBatch(const std::vector<int>& tokenI
 
     if (cudaMemcpyAsync(m.ids, tokenIDs.data(), N * sizeof(int32_t), cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemsetAsync(m.err, 0, sizeof(int32_t), st) != cudaSuccess)
-        return fail("host-to-device copy of token ids failed"), std::vector<float>();
+        return fail("host-to-device copy of token ids failed");
     check(gbx_embed(m.ids, m.wte, m.wte_dt, m.wpe, m.wpe_dt, nullptr, m.h.p, N, S, 0, d, V, nCtx_, m.err, gs));
 
     const float scale = sqrtf((float)hd);   // transformer.cu:836
@@ -312,21 +381,15 @@ std::vector<float> TransformerModel::forwardBatch(const std::vector<int>& tokenI
         }
         check(gbx_logits(m.last_y.p, batch, m.wte, m.wte_dt, m.logits.p, V, d, gs));
     }
-    std::vector<float> out;
     int32_t err_host = 0;
-    if (rc == GBX_OK && blas_ok) {
-        out.resize((size_t)batch * V);
-        if (cudaMemcpyAsync(out.data(), m.logits.p, out.size() * sizeof(float), cudaMemcpyDeviceToHost, st) !=
-                cudaSuccess ||
-            cudaMemcpyAsync(&err_host, m.err, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
-            rc = GBX_ECUDA;
-    }
+    if (rc == GBX_OK && blas_ok &&
+        cudaMemcpyAsync(&err_host, m.err, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        rc = GBX_ECUDA;
     if (cudaStreamSynchronize(st) != cudaSuccess && rc == GBX_OK) rc = GBX_ECUDA;
-    if (cur >= 0 && cur != m.device) cudaSetDevice(cur);
-    if (!blas_ok) return fail("cuBLAS call failed"), std::vector<float>();
-    if (rc != GBX_OK) return fail(std::string(gbx_status_string(rc)) + ": " + gbx_last_error()), std::vector<float>();
-    if (err_host) return fail("embedding reported out-of-range ids or positions"), std::vector<float>();
-    return out;
+    if (!blas_ok) return fail("cuBLAS call failed");
+    if (rc != GBX_OK) return fail(std::string(gbx_status_string(rc)) + ": " + gbx_last_error());
+    if (err_host) return fail("embedding reported out-of-range ids or positions");
+    return true;
 }
 
 }  // namespace gbx

@@ -41,6 +41,7 @@ SIGNATURES = {
     "gbx_model_close": ([_vp], None),
     "gbx_model_config": ([_vp, _vp], _int),
     "gbx_model_forward": ([_vp, _vp, _i64, _int, _vp], _int),
+    "gbx_model_next_token": ([_vp, _vp, _i64, ctypes.c_double, ctypes.c_double, _vp, _vp, _vp], _int),
 }
 
 _lib = None
@@ -155,3 +156,13 @@ class Model:
         if rc != 0:
             raise _err(rc)
         return out[0] if batch == 1 else out
+
+    def next_token(self, ids, temperature=0.0, u=0.0):
+        """(selected, best, best_logit) of one generate step with draw u."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32).ravel()
+        sel, best, bl = ctypes.c_int32(0), ctypes.c_int32(0), ctypes.c_float(0)
+        rc = lib().gbx_model_next_token(self.h, _np_ptr(ids), ids.size, float(temperature), float(u),
+                                        ctypes.byref(sel), ctypes.byref(best), ctypes.byref(bl))
+        if rc != 0:
+            raise _err(rc)
+        return sel.value, best.value, bl.value

@@ -160,6 +160,27 @@ int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t rows, int L
 int gbx_logits(const float* h, int64_t rows, const void* wte, int wte_dtype, float* logits, int vocab, int d,
                gbx_stream_t stream);
 
+/*
+ * Next-token selection over `rows` logits rows of length vocab, replacing the
+ * host loop of TransformerModel::generate (transformer.cu:994-1028):
+ *   out_best[r]       first index of the row maximum (the reference's strict
+ *                     `>` scan from index 0; a NaN in entry 0 gives 0)
+ *   out_best_logit[r] that maximum
+ *   out_ids[r]        out_best[r] when temperature <= 0.01; otherwise, with
+ *                     l = (float)(logit / temperature) (a double division),
+ *                     p = expf(l - max l) / (fp32 sum), the first j with
+ *                     uniforms[r] <= sum_{i<=j} p_i accumulated in double,
+ *                     or 0 when none qualifies
+ * uniforms: device doubles in [0, 1), one per row: the caller's draws (the
+ * reference draws uniform_real_distribution<double>(0, 1) from an mt19937);
+ * may be NULL when temperature <= 0.01.  out_best and out_best_logit may be
+ * NULL.  All outputs are device arrays of `rows` entries.  The fp32 sum
+ * runs in a different order from the reference's, so a draw within ~1e-7
+ * of a cumulative boundary may select the neighbouring token.
+ */
+int gbx_select_tokens(const float* logits, int64_t rows, int vocab, double temperature, const double* uniforms,
+                      int32_t* out_ids, int32_t* out_best, float* out_best_logit, gbx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,6 +48,14 @@ int gbx_model_config(gbx_model* m, int32_t out6[6]);
  * logits of each sequence's last token. */
 int gbx_model_forward(gbx_model* m, const int32_t* ids_host, int64_t n_ids, int batch, float* logits_host);
 
+/* One step of generate's loop without the tokenizer (transformer.cu:986-1028):
+ * forward, then the reference's argmax / temperature sampling on the device
+ * with the caller's uniform draw u in [0, 1) (used when temperature > 0.01).
+ * *out_id receives the selected token; best / best_logit (may be NULL) the
+ * argmax and its logit, as the reference prints them. */
+int gbx_model_next_token(gbx_model* m, const int32_t* ids_host, int64_t n_ids, double temperature, double u,
+                         int32_t* out_id, int32_t* best, float* best_logit);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,9 @@
 //     size of the logits is the token table's row count (the reference's
 //     getVocabSize() is the constant 50257, transformer.cu:492).
 //   - forwardBatch (new) runs `batch` equal-length sequences in one pass.
+//   - nextToken (new) is one step of generate without the tokenizer: the
+//     argmax / temperature sampling of transformer.cu:994-1028 runs on the
+//     device (gbx_select_tokens), so the logits never cross to the host.
 //   - The contractions around the hot path (QKV, scores, P.V, projections,
 //     FFN up/down) run as fp32 cuBLAS GEMMs; the hot path itself (embed,
 //     LayerNorm, residual + LayerNorm, score epilogue + softmax,
@@ -47,6 +50,7 @@
 #include <cstdint>
 #include <map>
 #include <memory>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -139,6 +143,16 @@ public:
     // `batch` sequences of tokenIDs.size()/batch tokens each, concatenated;
     // returns batch rows of logits (each sequence's last token).
     std::vector<float> forwardBatch(const std::vector<int>& tokenIDs, int batch);
+    // One step of generate's loop (transformer.cu:986-1036) without the
+    // tokenizer: forward, then the reference's argmax / temperature sampling
+    // (:994-1028) on the device, drawing from `rng` exactly when the
+    // reference draws (temperature > 0.01).  Returns the selected id (-1 on
+    // failure, see lastError()); bestID / bestLogit as the reference prints.
+    int nextToken(const std::vector<int>& tokenIDs, double temperature, std::mt19937& rng, int* bestID = nullptr,
+                  float* bestLogit = nullptr);
+    // The same with the uniform draw in [0, 1) supplied by the caller.
+    int nextTokenWithDraw(const std::vector<int>& tokenIDs, double temperature, double u, int* bestID = nullptr,
+                          float* bestLogit = nullptr);
 
     bool isModelLoaded() const { return loader_.isLoaded(); }
     void printTensorNames() { loader_.printAllTensorNames(); }
@@ -159,6 +173,7 @@ private:
     std::string err_;
     bool fail(const std::string& msg);
     bool ensureBuffers(int64_t tokens, int seq);
+    bool runForward(const std::vector<int>& tokenIDs, int batch);   // logits stay on the device
 };
 
 }  // namespace gbx

@@ -61,6 +61,8 @@ def lib():
         L.gbxo_bias_gelu_mt.argtypes = [_vp, _vp, _vp, _c_i64, _c_int, _c_int]
         L.gbxo_softmax_rows_mt.argtypes = [_vp, _vp, _c_i64, _c_int, _c_int]
         L.gbxo_logits_mt.argtypes = [_vp, _c_i64, _vp, _c_int, _vp, _c_int, _c_int, _c_int]
+        L.gbxo_select_token.argtypes = [_vp, _c_int, ctypes.c_double, ctypes.c_double, _vp, _vp, _vp]
+        L.gbxo_select_token.restype = _c_int
         L.gbxo_attn_softmax_mt.argtypes = [_vp, _vp, _c_i64, _c_int, _c_int, _c_int, ctypes.c_float, _c_int,
                                            _c_int]
         L.gbxo_max_threads.restype = _c_int
@@ -155,6 +157,25 @@ def dot_tolerance(h, wte_f32):
     u = 2.0 ** -24
     gamma = d * u / (1 - d * u)
     return 1e-6 + 2 * gamma * (np.abs(h.astype(np.float64)) @ np.abs(wte_f32.astype(np.float64)).T)
+
+
+def select_tokens(logits, temperature, uniforms=None):
+    """generate's selection loop (transformer.cu:994-1028) for each row of
+    logits: returns (selected, best, best_logit) arrays."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32).reshape(-1, logits.shape[-1])
+    rows, vocab = logits.shape
+    work = np.empty(vocab, dtype=np.float32)
+    sel = np.empty(rows, np.int32)
+    best = np.empty(rows, np.int32)
+    blog = np.empty(rows, np.float32)
+    b = ctypes.c_int(0)
+    bl = ctypes.c_float(0)
+    for r in range(rows):
+        u = 0.0 if uniforms is None else float(uniforms[r])
+        sel[r] = lib().gbxo_select_token(_ptr(logits[r]), vocab, temperature, u, _ptr(work), ctypes.byref(b),
+                                         ctypes.byref(bl))
+        best[r], blog[r] = b.value, bl.value
+    return sel, best, blog
 
 
 def attn_softmax_rows(raw, S, scale, q_off=0, causal=True, nthreads=1):

@@ -20,6 +20,8 @@
  *                        (same formula as geluKernel transformer.cu:68-75)
  *   gbxo_softmax_rows    transformer.cu:126-166   softmaxKernel
  *   gbxo_logits          transformer.cu:296-307   computeLogitsKernel
+ *   gbxo_select_tokens   transformer.cu:994-1028  generate's argmax /
+ *                        temperature sampling (host code in the reference)
  *   gbxo_attn_softmax    transformer.cu:213-232   attentionScoresKernel's
  *                        epilogue (dot / scale, -1e9f above the diagonal),
  *                        then transformer.cu:126-166 softmaxKernel
@@ -392,6 +394,39 @@ void gbxo_logits_mt(const float* h, int64_t rows, const void* wte, int dtype, fl
 {
     logits_ctx c = { h, wte, dtype, out, vocab, d, rows };
     parallel_rows(logits_part, &c, vocab, nthreads);
+}
+
+/* transformer.cu:994-1028, for each row: bestID / bestLogit by a strict `>`
+ * scan from entry 0; temperature <= 0.01 selects bestID; otherwise
+ * l /= temperature (float l, double temperature: the division is in
+ * double), maxVal = the first largest l (std::max_element), l = expf(l -
+ * maxVal) with a sequential float sum, l /= sum, then the first j whose
+ * double cumulative sum reaches u (0 when none does).  `work` holds vocab
+ * floats.  Returns the selected id; *best and *best_logit as the reference
+ * prints them. */
+int gbxo_select_token(const float* logits, int vocab, double temperature, double u, float* work,
+                      int* best, float* best_logit)
+{
+    int bestID = 0;
+    float bestLogit = logits[0];
+    for (int j = 1; j < vocab; j++)
+        if (logits[j] > bestLogit) { bestLogit = logits[j]; bestID = j; }
+    *best = bestID;
+    *best_logit = bestLogit;
+    if (temperature <= 0.01) return bestID;
+    for (int j = 0; j < vocab; j++) work[j] = (float)((double)logits[j] / temperature);
+    float maxVal = work[0];
+    for (int j = 1; j < vocab; j++)
+        if (maxVal < work[j]) maxVal = work[j];
+    float sum = 0.0f;
+    for (int j = 0; j < vocab; j++) { work[j] = expf(work[j] - maxVal); sum += work[j]; }
+    for (int j = 0; j < vocab; j++) work[j] = work[j] / sum;
+    double cum = 0.0;
+    for (int j = 0; j < vocab; j++) {
+        cum += work[j];
+        if (u <= cum) return j;
+    }
+    return 0;
 }
 
 /* Single-thread entry points (the checker's default). */

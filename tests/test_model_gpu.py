@@ -86,3 +86,17 @@ def test_loader_device_tensors(gm, cuda, tmp_path):
     assert np.array_equal(dev.cpu().numpy().view(np.uint32), host.view(np.uint32))
     raw, dt, ne = f.tensor_gpu_raw("token_embd.weight")
     assert dt == GGML_BF16 and ne == 512 * 64 and raw
+
+
+def test_next_token_matches_reference_selection(gm, orc, cuda, tmp_path):
+    path = str(tmp_path / "tiny.gguf")
+    write_tiny_gpt2(path, GGML_F32, seed=13)
+    model = gm.Model(path)
+    rng = np.random.default_rng(8)
+    ids = rng.integers(0, 50257, 9).astype(np.int32)
+    logits = model.forward(ids)
+    for T, u in ((0.0, 0.0), (0.7, 0.25), (1.0, 0.9), (2.0, 0.5)):
+        sel, best, bl = model.next_token(ids, T, u)
+        wsel, wbest, wbl = orc.select_tokens(logits[None, :], T, [u])
+        assert best == int(wbest[0]) and np.float32(bl) == wbl[0]
+        assert sel == int(wsel[0])

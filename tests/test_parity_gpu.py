@@ -464,3 +464,79 @@ def test_logits_unaligned_rows_general_path(gbx, orc, cuda):
     ref = orc.logits(h, wte, 30)
     tol = orc.dot_tolerance(h, orc.dequant(wte, 30).reshape(V, d))
     assert np.all(np.abs(out.cpu().numpy() - ref) <= tol)
+
+
+# ---------------------------------------------------------------------------
+# next-token selection (generate's host loop, on the device)
+
+def _select(gbx, logits, T, u, torch):
+    rows, V = logits.shape
+    ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+    best = torch.empty(rows, dtype=torch.int32, device="cuda")
+    bl = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ud = None if u is None else torch.from_numpy(np.ascontiguousarray(u, np.float64)).cuda()
+    gbx.select_tokens(_t(logits, torch), ids, rows=rows, vocab=V, temperature=T, uniforms=ud, out_best=best,
+                      out_best_logit=bl)
+    return ids.cpu().numpy(), best.cpu().numpy(), bl.cpu().numpy()
+
+
+def _selection_consistent(logits_row, T, got, want):
+    """The reference normalises by a sequential fp32 sum over the vocabulary
+    (relative error up to ~1e-5 at 60k entries); the device sums in a tree.
+    Two selections may differ only by the probability mass that the two sums
+    can move: the exact mass strictly between them must stay within the
+    relative difference of the reference's sum from the exact one (+1e-6)
+    times the cumulative probability there."""
+    if got == want:
+        return True
+    l = (logits_row.astype(np.float64) / T).astype(np.float32)
+    e = np.exp((l - l.max()).astype(np.float64))
+    s_exact = e.sum()
+    s_seq = float(np.cumsum(e.astype(np.float32), dtype=np.float32)[-1])   # the reference's order
+    c = np.cumsum(e / s_exact)
+    lo, hi = sorted((int(got), int(want)))
+    between = c[hi - 1] - c[lo]
+    return between <= (abs(s_seq / s_exact - 1.0) + 1e-6) * c[hi] + 1e-7
+
+
+@pytest.mark.parametrize("V", [50257, 1000, 60001])
+@pytest.mark.parametrize("T", [0.0, 0.005, 0.7, 1.0, 2.5])
+def test_select_tokens(gbx, orc, cuda, V, T):
+    import torch
+    rng = np.random.default_rng(V + int(T * 100))
+    rows = 6
+    logits = (3.0 * rng.standard_normal((rows, V))).astype(np.float32)
+    logits[1, 17] = logits[1, 900 % V] = logits[1].max() + 1.0     # tie: the first index wins
+    u = rng.random(rows)
+    u[2] = 0.0
+    got, gbest, gbl = _select(gbx, logits, T, u if T > 0.01 else None, torch)
+    want, wbest, wbl = orc.select_tokens(logits, T, u)
+    assert np.array_equal(gbest, wbest) and np.array_equal(gbl.view(np.uint32), wbl.view(np.uint32))
+    assert gbest[1] == 17
+    for r in range(rows):
+        if T <= 0.01:
+            assert got[r] == want[r], (r, got[r], want[r])
+        else:
+            assert _selection_consistent(logits[r], T, got[r], want[r]), (r, got[r], want[r])
+
+
+def test_select_tokens_specials(gbx, orc, cuda):
+    import torch
+    V = 4096
+    logits = np.zeros((4, V), np.float32)
+    logits[0, :] = -np.inf                      # nothing beats entry 0
+    logits[1, 0] = np.nan; logits[1, 5] = 7.0   # NaN first: the reference keeps index 0
+    logits[2, 3] = np.nan; logits[2, 9] = 2.0   # later NaN is never greater
+    logits[3, :] = 1.5                          # all equal: index 0
+    got, best, bl = _select(gbx, logits, 0.0, None, torch)
+    _, wbest, wbl = orc.select_tokens(logits, 0.0)
+    assert list(best) == list(wbest) == [0, 0, 9, 0]
+    assert np.array_equal(np.isnan(bl), np.isnan(wbl))
+
+
+def test_select_tokens_needs_uniforms_when_sampling(gbx, cuda):
+    import torch
+    x = torch.zeros((2, 8), device="cuda")
+    ids = torch.zeros(2, dtype=torch.int32, device="cuda")
+    with pytest.raises(gbx.GbxError):
+        gbx.select_tokens(x, ids, rows=2, vocab=8, temperature=1.0)

@@ -386,7 +386,7 @@ def test_attn_softmax_causal_prefill(gbx, orc, cuda, S, H, scale):
     _check_guards(full)
 
 
-@pytest.mark.parametrize("S,L", [(4, 40), (1, 2048), (7, 1031), (16, 1024)])
+@pytest.mark.parametrize("S,L", [(4, 40), (1, 2048), (7, 1031), (16, 1024), (37, 40), (2, 8), (33, 36), (5, 2048)])
 def test_attn_softmax_query_offset(gbx, orc, cuda, S, L):
     """S new queries after L - S cached keys: query p sees keys 0 .. p + L - S."""
     import torch

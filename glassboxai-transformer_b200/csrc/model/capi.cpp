@@ -17,6 +17,10 @@ struct gbx_model {
     gbx::TransformerModel model;
 };
 
+struct gbx_sharded {
+    gbx::ShardedModel model;
+};
+
 extern "C" {
 
 gbx_gguf* gbx_gguf_open(const char* path)
@@ -137,6 +141,38 @@ int gbx_model_next_token(gbx_model* m, const int32_t* ids_host, int64_t n_ids, d
     *out_id = sel;
     if (best) *best = b;
     if (best_logit) *best_logit = bl;
+    return GBX_OK;
+}
+
+gbx_sharded* gbx_sharded_open(const char* gguf_path, const int32_t* devices, int n)
+{
+    if (!gguf_path || !devices || n <= 0) {
+        gbx::set_error(GBX_EINVAL, "gbx_sharded_open: bad argument");
+        return nullptr;
+    }
+    gbx_sharded* s = new (std::nothrow) gbx_sharded;
+    if (!s) {
+        gbx::set_error(GBX_ENOMEM, "gbx_sharded_open: out of memory");
+        return nullptr;
+    }
+    if (!s->model.loadModel(gguf_path, std::vector<int>(devices, devices + n))) {
+        gbx::set_error(GBX_EIO, "%s", s->model.lastError().c_str());
+        delete s;
+        return nullptr;
+    }
+    return s;
+}
+
+void gbx_sharded_close(gbx_sharded* s) { delete s; }
+
+int gbx_sharded_forward(gbx_sharded* s, const int32_t* ids_host, int64_t n_ids, int batch, float* logits_host)
+{
+    if (!s || !ids_host || !logits_host || n_ids <= 0 || batch <= 0)
+        return gbx::set_error(GBX_EINVAL, "gbx_sharded_forward: bad argument");
+    std::vector<int> ids(ids_host, ids_host + n_ids);
+    std::vector<float> out = s->model.forwardBatch(ids, batch);
+    if (out.empty()) return gbx::set_error(GBX_EINVAL, "%s", s->model.lastError().c_str());
+    std::memcpy(logits_host, out.data(), out.size() * sizeof(float));
     return GBX_OK;
 }
 

@@ -42,6 +42,9 @@ SIGNATURES = {
     "gbx_model_config": ([_vp, _vp], _int),
     "gbx_model_forward": ([_vp, _vp, _i64, _int, _vp], _int),
     "gbx_model_next_token": ([_vp, _vp, _i64, ctypes.c_double, ctypes.c_double, _vp, _vp, _vp], _int),
+    "gbx_sharded_open": ([_cp, _vp, _int], _vp),
+    "gbx_sharded_close": ([_vp], None),
+    "gbx_sharded_forward": ([_vp, _vp, _i64, _int, _vp], _int),
 }
 
 _lib = None
@@ -166,3 +169,35 @@ class Model:
         if rc != 0:
             raise _err(rc)
         return sel.value, best.value, bl.value
+
+
+class ShardedModel:
+    """ShardedModel: a TransformerModel replica per listed device, one host
+    thread per device, batches split into whole-sequence shards and the
+    logits gathered on the host."""
+
+    def __init__(self, path: str, devices, vocab: int):
+        dev = np.ascontiguousarray(devices, dtype=np.int32)
+        self.vocab = vocab
+        self.h = lib().gbx_sharded_open(path.encode(), _np_ptr(dev), dev.size)
+        if not self.h:
+            raise _err()
+
+    def close(self):
+        if self.h:
+            lib().gbx_sharded_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, ids, batch: int) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32).ravel()
+        out = np.empty((batch, self.vocab), dtype=np.float32)
+        rc = lib().gbx_sharded_forward(self.h, _np_ptr(ids), ids.size, batch, _np_ptr(out))
+        if rc != 0:
+            raise _err(rc)
+        return out

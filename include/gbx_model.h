@@ -18,6 +18,7 @@ extern "C" {
 
 typedef struct gbx_gguf gbx_gguf;
 typedef struct gbx_model gbx_model;
+typedef struct gbx_sharded gbx_sharded;
 
 /* GGUFLoader::loadFromFile (transformer.cu:657-674). */
 gbx_gguf* gbx_gguf_open(const char* path);
@@ -55,6 +56,14 @@ int gbx_model_forward(gbx_model* m, const int32_t* ids_host, int64_t n_ids, int 
  * argmax and its logit, as the reference prints them. */
 int gbx_model_next_token(gbx_model* m, const int32_t* ids_host, int64_t n_ids, double temperature, double u,
                          int32_t* out_id, int32_t* best, float* best_logit);
+
+/* ShardedModel: a model replica on each of the n devices listed, one host
+ * thread per device; gbx_sharded_forward splits `batch` sequences of
+ * n_ids/batch tokens into contiguous shards, one per replica, and gathers
+ * batch x vocab logits in order (no collective; per-shard D2H only). */
+gbx_sharded* gbx_sharded_open(const char* gguf_path, const int32_t* devices, int n);
+void gbx_sharded_close(gbx_sharded* s);
+int gbx_sharded_forward(gbx_sharded* s, const int32_t* ids_host, int64_t n_ids, int batch, float* logits_host);
 
 #ifdef __cplusplus
 }

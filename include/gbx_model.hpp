@@ -176,4 +176,32 @@ private:
     bool runForward(const std::vector<int>& tokenIDs, int batch);   // logits stay on the device
 };
 
+// Row sharding across GPUs with one host thread per device: a replica of
+// the model on each listed device, a batch of sequences split into
+// contiguous whole-sequence shards (shares within one of each other), each
+// shard run on its device's thread, the logits gathered in order on the
+// host.  No collective and no peer memory: the only exchange is the final
+// device-to-host copy of each shard's logits.  A device may be listed twice
+// (two replicas on one GPU).
+class ShardedModel {
+public:
+    ShardedModel();
+    ~ShardedModel();
+    ShardedModel(const ShardedModel&) = delete;
+    ShardedModel& operator=(const ShardedModel&) = delete;
+
+    bool loadModel(const std::string& ggufPath, const std::vector<int>& devices);
+    // As TransformerModel::forwardBatch: `batch` equal-length sequences,
+    // batch rows of logits.  Fails as a whole if any shard fails.
+    std::vector<float> forwardBatch(const std::vector<int>& tokenIDs, int batch);
+    int replicas() const { return (int)models_.size(); }
+    int getVocabSize() const { return models_.empty() ? 0 : models_[0]->getVocabSize(); }
+    const std::string& lastError() const { return err_; }
+
+private:
+    std::vector<std::unique_ptr<TransformerModel>> models_;
+    std::vector<int> devices_;
+    std::string err_;
+};
+
 }  // namespace gbx

@@ -100,3 +100,39 @@ def test_next_token_matches_reference_selection(gm, orc, cuda, tmp_path):
         wsel, wbest, wbl = orc.select_tokens(logits[None, :], T, [u])
         assert best == int(wbest[0]) and np.float32(bl) == wbl[0]
         assert sel == int(wsel[0])
+
+
+def _devices():
+    import torch
+    return list(range(torch.cuda.device_count()))
+
+
+def test_sharded_model_equals_single_replica(gm, cuda, tmp_path):
+    """One host thread per replica, whole-sequence shards, host gather: the
+    result equals one model's forward of the whole batch (two replicas on
+    GPU 0, and on GPUs 0 and 1 where a second GPU exists)."""
+    path = str(tmp_path / "tiny.gguf")
+    write_tiny_gpt2(path, GGML_BF16, seed=21)
+    rng = np.random.default_rng(2)
+    seqs = rng.integers(0, 50257, (5, 10)).astype(np.int32)
+    single = gm.Model(path).forward(seqs.ravel(), batch=5)
+    layouts = [[0, 0]] + ([[0, 1]] if len(_devices()) > 1 else [])
+    for devs in layouts:
+        sm = gm.ShardedModel(path, devs, vocab=50257)
+        got = sm.forward(seqs.ravel(), batch=5)
+        assert np.allclose(got, single, atol=1e-6, rtol=1e-5), devs
+        sm.close()
+
+
+def test_sharded_model_fails_as_a_whole(gm, cuda, tmp_path):
+    path = str(tmp_path / "tiny.gguf")
+    write_tiny_gpt2(path, GGML_F32, ctx=8, seed=22)
+    sm = gm.ShardedModel(path, [0, 0], vocab=50257)
+    ids = np.zeros((2, 4), np.int32)
+    ids[1, 2] = 50257                      # out of range in the second shard only
+    with pytest.raises(Exception) as e:
+        sm.forward(ids.ravel(), batch=2)
+    assert "device 0" in str(e.value)
+    assert sm.forward(np.zeros(8, np.int32), batch=2).shape == (2, 50257)   # still usable
+    with pytest.raises(Exception):
+        gm.ShardedModel(path, [99], vocab=50257)

@@ -1,0 +1,81 @@
+"""Parity of the whole hot-path chain (glassboxai-transformer_b200/chain.py,
+the step bench.py times) at the shapes of the benchmark configurations,
+against the same chain replayed on the CPU through the oracle:
+
+* config 0: GPT-2 small, 1 x 64 tokens, d 768, ff 3072, 12 heads, 12 layers,
+  f32 tables;
+* config 3: GPT-2 XL decode, 256 sequences of 1 token at position 2047,
+  softmax rows of 2048, 48 layers, bf16 tables;
+* config 1 (2 of its 24 layers): GPT-2 medium prefill, 8 x 1024 tokens,
+  d 1024, f16 tables.
+
+The residual stream h is compared bit for bit (each layer adds in fp32 in
+the same order); the LayerNorm outputs, softmax and GELU rows and the final
+LayerNorm rows within |a-b| <= 1e-6 + 1e-5|b|."""
+import importlib
+import math
+
+import numpy as np
+import pytest
+
+from conftest import assert_bits_equal, assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_chain(orc, c, s):
+    """The chain step on the CPU from the GPU chain's own inputs."""
+    import torch
+    t = lambda x: x.detach().cpu().numpy()   # noqa: E731
+
+    def table(x):
+        if s.table_dtype == 0:
+            return t(x)
+        return t(x.view(torch.int16)).view(np.uint16)
+    wte, wpe = table(c.wte), table(c.wpe)
+    ids = t(c.ids)
+    h, bad = orc.embed(ids, wte, s.table_dtype, wpe, s.table_dtype, s.d, s.vocab, s.n_ctx, seq=s.seq,
+                       pos_off=s.pos_off)
+    assert bad == 0
+    attn_out, ffn_out, ffn_pre, scores = t(c.attn_out), t(c.ffn_out), t(c.ffn_pre), t(c.scores)
+    g1, b1, g2, b2, ub = t(c.g1), t(c.b1), t(c.g2), t(c.b2), t(c.up_bias)
+    # the scores and the GELU input are the same every layer: their last
+    # layer's outputs are computed once
+    probs = orc.softmax_rows(scores, nthreads=orc.max_threads())
+    act = orc.bias_gelu(ffn_pre, ub[s.layers - 1], nthreads=orc.max_threads())
+    ln = None
+    for l in range(s.layers):
+        if l == 0:
+            ln = orc.layernorm(h, g1[0], b1[0])
+        else:
+            h, ln = orc.residual_layernorm(ffn_out, h, g1[l], b1[l])
+        h, ln = orc.residual_layernorm(attn_out, h, g2[l], b2[l])
+    B = s.chunk_seqs
+    last_h = h.reshape(B, s.seq, s.d)[:, -1].copy()
+    last_f = ffn_out.reshape(B, s.seq, s.d)[:, -1].copy()
+    _, out = orc.residual_layernorm(last_f, last_h, t(c.gf), t(c.bf))
+    return h, ln, probs, act, out
+
+
+@pytest.mark.parametrize("name,kw,chain_kw", [
+    ("config0-gpt2-small", dict(batch=1, seq=64, d=768, ff=3072, heads=12, layers=12, vocab=50257, n_ctx=1024,
+                                table_dtype=0), dict(score_std=1.0)),
+    ("config3-gpt2-xl-decode", dict(batch=256, seq=1, d=1600, ff=6400, heads=25, layers=48, vocab=50257, n_ctx=2048,
+                                    table_dtype=30, kv_len=2048, pos_off=2047), dict(score_std=math.sqrt(2.0))),
+    ("config1-gpt2-medium-2-layers", dict(batch=8, seq=1024, d=1024, ff=4096, heads=16, layers=2, vocab=50257,
+                                          n_ctx=1024, table_dtype=1), dict(score_std=1.0)),
+])
+def test_chain_matches_oracle_chain(orc, cuda, name, kw, chain_kw):
+    import torch
+    chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
+    s = chain_mod.ChainShape(**kw)
+    c = chain_mod.Chain(s, torch.device("cuda:0"), seed=11, **chain_kw)
+    c.step()
+    torch.cuda.synchronize()
+    assert int(c.err.item()) == 0
+    h, ln, probs, act, out = _oracle_chain(orc, c, s)
+    assert_bits_equal(c.h.cpu().numpy(), h, f"{name}: residual stream")
+    assert_close(c.ln.cpu().numpy(), ln, what=f"{name}: last LayerNorm")
+    assert_close(c.probs.cpu().numpy(), probs, what=f"{name}: softmax")
+    assert_close(c.ffn_act.cpu().numpy(), act, what=f"{name}: bias+GELU")
+    assert_close(c.out.cpu().numpy(), out, what=f"{name}: final LayerNorm rows")

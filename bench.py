@@ -306,6 +306,8 @@ def run_ours(args, shape, desc, chain_kw, scaling):
     if scaling == "strong":
         first, count = shard.shard_sequences(shape.batch, rank, world)
         shape = dataclasses.replace(shape, batch=count)
+    if args.pdl:
+        import_module("glassboxai-transformer_b200").set_pdl(True)
     chain = chain_mod.Chain(shape, device, seed=1000 + rank, **chain_kw)
     stream = torch.cuda.current_stream(device)
     torch.cuda.synchronize(device)
@@ -402,6 +404,7 @@ def run_ours(args, shape, desc, chain_kw, scaling):
         "config": {"workload": args.workload, "description": desc, "tokens_per_gpu": shape.tokens,
                    "global_batch": global_batch, "seq_len": shape.seq, "layers": shape.layers,
                    "chunks_per_step": shape.n_chunks, "cuda_graph": bool(args.graph),
+                   "programmatic_dependent_launch": bool(args.pdl),
                    "parallelism": f"row shards of whole sequences over {world} GPU(s), no collective",
                    "l2": "no flush; every streamed buffer is larger than the 126 MB L2 "
                          f"(smallest: {shape.chunk_tokens * shape.d * 4 / 1e6:.0f} MB)"
@@ -630,6 +633,8 @@ def main():
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--graph", action="store_true",
                     help="capture one step in a CUDA graph and replay it (launch-bound workloads)")
+    ap.add_argument("--pdl", action="store_true",
+                    help="launch the row kernels with programmatic dependent launch (gbx_set_pdl)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -43,6 +43,7 @@ SIGNATURES = {
     "gbx_version": [],
     "gbx_status_string": [_int],
     "gbx_last_error": [],
+    "gbx_set_pdl": [_int],
     "gbx_dequant": [_vp, _int, _vp, _i64, _vp],
     "gbx_embed": [_vp, _vp, _int, _vp, _int, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, _vp],
     "gbx_layernorm": [_vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
@@ -105,6 +106,12 @@ def _check(rc: int):
 
 def version() -> int:
     return lib().gbx_version()
+
+
+def set_pdl(enable: bool) -> bool:
+    """Programmatic dependent launch for the row kernels (process-wide);
+    returns the previous setting."""
+    return bool(lib().gbx_set_pdl(1 if enable else 0))
 
 
 def dequant(src, dtype: int, dst, n: int, stream=None):

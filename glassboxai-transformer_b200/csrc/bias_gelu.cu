@@ -31,6 +31,8 @@ template <bool BIAS>
 __global__ void __launch_bounds__(512)
 bias_gelu_vec_kernel(const float* in, float* out, const float* __restrict__ bias, int64_t rows, int n4, int bands)
 {
+    grid_dependency_wait();   // see launch_row_kernel
+    allow_dependents();
     const int band = (int)(blockIdx.x % (unsigned)bands);
     const int64_t r0 = (int64_t)(blockIdx.x / (unsigned)bands) * kGeluU;
     const int c = band * blockDim.x + threadIdx.x;
@@ -82,7 +84,8 @@ static int launch_gelu_vec(const float* in, float* out, const float* bias, int64
     const int64_t grid = (int64_t)bands * ((rows + kGeluU - 1) / kGeluU);
     if (grid > 0x7fffffffLL)
         return set_error(GBX_ERANGE, "gbx_bias_gelu: rows=%lld F=%d needs too many CTAs", (long long)rows, 4 * n4);
-    bias_gelu_vec_kernel<BIAS><<<(unsigned)grid, T, 0, stream>>>(in, out, bias, rows, n4, bands);
+    launch_row_kernel(bias_gelu_vec_kernel<BIAS>, dim3((unsigned)grid), dim3(T), 0, stream, in, out, bias, rows, n4,
+                      bands);
     return check_launch("gbx_bias_gelu");
 }
 

@@ -31,6 +31,8 @@ embed_vec4_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
                   float* __restrict__ out, uint32_t total, FastDiv div_n4, FastDiv div_seq,
                   int pos_off, int d, int vocab, int n_ctx, int32_t* __restrict__ err)
 {
+    grid_dependency_wait();   // see launch_row_kernel
+    allow_dependents();
     const uint32_t n4 = div_n4.d;
     const uint32_t seq = div_seq.d;
     const uint32_t base = blockIdx.x * (uint32_t)(kEmbedThreads * kEmbedU) + threadIdx.x;
@@ -127,9 +129,9 @@ static int launch_embed(const int32_t* ids, const void* wte, const void* wpe, co
     if (vec) {
         const int64_t per_cta = (int64_t)kEmbedThreads * kEmbedU;
         const int64_t grid = (total + per_cta - 1) / per_cta;
-        embed_vec4_kernel<WT, PT><<<(unsigned)grid, kEmbedThreads, 0, stream>>>(
-            ids, wte, wpe, pos_ids, out, (uint32_t)total, make_fastdiv((uint32_t)n4), make_fastdiv((uint32_t)seq),
-            pos_off, d, vocab, n_ctx, err);
+        launch_row_kernel(embed_vec4_kernel<WT, PT>, dim3((unsigned)grid), dim3(kEmbedThreads), 0, stream, ids, wte,
+                          wpe, pos_ids, out, (uint32_t)total, make_fastdiv((uint32_t)n4),
+                          make_fastdiv((uint32_t)seq), pos_off, d, vocab, n_ctx, err);
     } else {
         auto k = embed_scalar_kernel<WT, PT>;
         const int64_t total_e = n_tok * (int64_t)d;

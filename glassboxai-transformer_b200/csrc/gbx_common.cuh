@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "gbx.h"
 
 namespace gbx {
@@ -41,6 +43,41 @@ inline int persistent_grid(K kernel, int block, size_t smem, int64_t work_blocks
 }
 
 inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  With gbx_set_pdl(1) the row kernels are
+// launched with programmatic stream serialization: the next grid may be
+// scheduled while this one drains (its launch and CTA set-up overlap our
+// tail), and each such kernel starts with grid_dependency_wait(), which
+// returns once every earlier grid on the stream has completed and its
+// memory is visible.  No global memory is touched before that wait, so a
+// kernel never reads an input early or overwrites one an earlier kernel is
+// still reading.  allow_dependents() lets the next grid be scheduled once
+// every CTA of this one has started.  Both are no-ops for a kernel launched
+// without the attribute.
+bool pdl_enabled();
+
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <class... KArgs, class... Args>
+inline cudaError_t launch_row_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     Args&&... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // Memory access.  Activations are streamed exactly once per kernel, so loads

@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(RowCTA<TPR>::threads)
 ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out, float* y,
               const float* __restrict__ gamma, const float* __restrict__ beta, int64_t rows, int d, float eps)
 {
+    grid_dependency_wait();   // see launch_row_kernel
+    allow_dependents();
     __shared__ float red[2][RowCTA<TPR>::warps];
     const int n4 = d >> 2;
     const int lane = threadIdx.x & (TPR - 1);
@@ -145,8 +147,8 @@ static int launch_ln_vec(const float* x, const float* r, const float* xbias, flo
 {
     const int64_t grid = row_grid<TPR>(rows);
     if (grid < 0) return GBX_ERANGE;
-    ln_vec_kernel<TPR, V4, RESID><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(x, r, xbias, h_out, y, g, b,
-                                                                                     rows, d, eps);
+    launch_row_kernel(ln_vec_kernel<TPR, V4, RESID>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads), 0, stream, x,
+                      r, xbias, h_out, y, g, b, rows, d, eps);
     return GBX_OK;
 }
 

@@ -48,6 +48,8 @@ template <int TPR, int V4, bool ATTN, bool POW2>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads)
 softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep)
 {
+    grid_dependency_wait();   // see launch_row_kernel
+    allow_dependents();
     __shared__ float red[2][RowCTA<TPR>::warps];
     const int n4 = L >> 2;
     const int lane = threadIdx.x & (TPR - 1);
@@ -170,11 +172,11 @@ static int launch_softmax_vec(const float* in, float* out, int64_t rows, int L, 
     const int64_t grid = row_grid<TPR>(rows);
     if (grid < 0) return GBX_ERANGE;
     if (ATTN && is_pow2(ep.scale))
-        softmax_vec_kernel<TPR, V4, ATTN, true><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(in, out, rows,
-                                                                                                   L, ep);
+        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, true>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads), 0,
+                          stream, in, out, rows, L, ep);
     else
-        softmax_vec_kernel<TPR, V4, ATTN, false><<<(unsigned)grid, RowCTA<TPR>::threads, 0, stream>>>(in, out, rows,
-                                                                                                    L, ep);
+        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, false>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads),
+                          0, stream, in, out, rows, L, ep);
     return GBX_OK;
 }
 

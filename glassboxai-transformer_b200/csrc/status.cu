@@ -2,6 +2,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "gbx_common.cuh"
@@ -51,9 +52,15 @@ int device_info(DeviceInfo* out)
     return GBX_OK;
 }
 
+static std::atomic<int> g_pdl{0};
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
 }  // namespace gbx
 
 extern "C" {
+
+int gbx_set_pdl(int enable) { return gbx::g_pdl.exchange(enable ? 1 : 0); }
 
 int gbx_version(void) { return 100; }
 

@@ -60,6 +60,17 @@ const char* gbx_status_string(int status);
 const char* gbx_last_error(void);
 
 /*
+ * Programmatic dependent launch for the row kernels (embed, LayerNorm,
+ * residual + LayerNorm, bias + GELU, softmax), process-wide, off by default.
+ * When on, each of these kernels may be scheduled while the previous kernel
+ * on its stream drains, and waits on the device for that kernel's
+ * completion before touching memory: results are unchanged, launch gaps
+ * shrink (most visible in chains of small launches and in CUDA graphs).
+ * Returns the previous setting.
+ */
+int gbx_set_pdl(int enable);
+
+/*
  * GGUF tensor decode to fp32 on the device, bit-identical to the reference's
  * host dequant GGUFLoader::loadTensorByIndex (transformer.cu:635-650) with
  * float16ToFloat32 (:508-527: -0 -> +0, every NaN -> 0x7fc00000, subnormals

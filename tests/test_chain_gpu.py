@@ -79,3 +79,38 @@ def test_chain_matches_oracle_chain(orc, cuda, name, kw, chain_kw):
     assert_close(c.probs.cpu().numpy(), probs, what=f"{name}: softmax")
     assert_close(c.ffn_act.cpu().numpy(), act, what=f"{name}: bias+GELU")
     assert_close(c.out.cpu().numpy(), out, what=f"{name}: final LayerNorm rows")
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_programmatic_dependent_launch_changes_nothing(gbx, cuda, graph):
+    """With gbx_set_pdl(1) every row kernel waits on the device for the
+    previous kernel before touching memory: the chain's outputs are bit for
+    bit those of plain stream order (config 0 and the decode shape, eager and
+    captured in a CUDA graph)."""
+    import torch
+    chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
+    for kw, ckw in ((dict(batch=1, seq=64, d=768, ff=3072, heads=12, layers=12, vocab=50257, n_ctx=1024,
+                          table_dtype=0), {}),
+                    (dict(batch=256, seq=1, d=1600, ff=6400, heads=25, layers=8, vocab=50257, n_ctx=2048,
+                          table_dtype=30, kv_len=2048, pos_off=2047), {})):
+        s = chain_mod.ChainShape(**kw)
+        outs = []
+        for pdl in (False, True):
+            prev = gbx.set_pdl(pdl)
+            try:
+                c = chain_mod.Chain(s, torch.device("cuda:0"), seed=5, **ckw)
+                if graph:
+                    c.step()
+                    c.capture_graph()
+                    for _ in range(3):
+                        c.replay()
+                else:
+                    for _ in range(3):
+                        c.step()
+                torch.cuda.synchronize()
+                outs.append([t.cpu().numpy().copy() for t in (c.h, c.ln, c.probs, c.ffn_act, c.out)])
+                c.graph = None
+            finally:
+                gbx.set_pdl(prev)
+        for a, b in zip(*outs):
+            assert_bits_equal(a, b, "pdl on vs off")

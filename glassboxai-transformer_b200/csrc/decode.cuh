@@ -6,6 +6,8 @@
 // 8-byte load for f16/bf16.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "gbx_common.cuh"
 
 namespace gbx {
@@ -72,6 +74,25 @@ __device__ __forceinline__ float4 decode4(typename Raw4<T>::type w)
     } else {
         return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
                            __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+    }
+}
+
+// The same 4 elements through the hardware conversion (cvt.f32.f16, exact
+// for every finite half and for +-inf), without the reference's two f16
+// quirks: -0 stays -0 and a NaN keeps its payload.  For consumers that add
+// the decoded value (the embedding sum, the logits dot product) only the
+// sign of a zero sum can differ, and the embedding restores it (see
+// embed_vec4_kernel); a GPU fp32 add returns the canonical NaN whatever the
+// payload.
+template <int T>
+__device__ __forceinline__ float4 decode4_arith(typename Raw4<T>::type w)
+{
+    if constexpr (T == TF16) {
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
+        return make_float4(lo.x, lo.y, hi.x, hi.y);
+    } else {
+        return decode4<T>(w);
     }
 }
 

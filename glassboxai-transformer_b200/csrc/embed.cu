@@ -64,9 +64,16 @@ embed_vec4_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
         if (base + u * kEmbedThreads >= total) continue;
         if (bad[u] && col[u] == 0 && err) atomicOr(err, bad[u]);
         // one fp32 add per element, as embedTokensKernel (transformer.cu:183);
-        // a rejected token's row is zeros (0 + 0).
-        const float4 x = decode4<WT>(a[u]), y = decode4<PT>(b[u]);
-        st_stream(out + (int64_t)tok[u] * d + 4 * col[u], make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w));
+        // a rejected token's row is zeros (0 + 0).  f16 words are converted
+        // by the hardware; the reference's decode turns an f16 -0 into +0,
+        // so with an f16 table the reference's sum is never -0: adding +0
+        // maps a -0 sum (-0 + -0) to +0 and leaves every other value as it
+        // is.  A NaN element gives the GPU's canonical NaN either way.
+        constexpr bool kF16 = WT == TF16 || PT == TF16;
+        const float4 x = decode4_arith<WT>(a[u]), y = decode4_arith<PT>(b[u]);
+        float4 o = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+        if (kF16) o = make_float4(__fadd_rn(o.x, 0.0f), __fadd_rn(o.y, 0.0f), __fadd_rn(o.z, 0.0f), __fadd_rn(o.w, 0.0f));
+        st_stream(out + (int64_t)tok[u] * d + 4 * col[u], o);
     }
 }
 

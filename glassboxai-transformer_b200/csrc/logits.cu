@@ -2,9 +2,10 @@
 // transformer.cu:296-307, launched at :898-900 on the final-LayerNorm row):
 //   logits[r, v] = sum_j h[r, j] * dec(wte[v, j])
 // for up to kLogitsMaxRows hidden rows per pass, reading the token table in
-// its GGUF encoding (dec() is the embedding's decode, bit-identical to the
-// reference's host dequant), so the [vocab, d] table crosses HBM once per
-// pass whatever the number of rows.  This is an HBM-bound GEMV: one warp per
+// its GGUF encoding (dec() gives the values of the reference's host dequant;
+// f16 goes through the hardware conversion, whose only differences, the sign
+// of zero and NaN payloads, cannot change the sum), so the [vocab, d] table
+// crosses HBM once per pass whatever the number of rows.  This is an HBM-bound GEMV: one warp per
 // vocabulary row, lanes striding the row in 4-element chunks (8-byte
 // f16/bf16 or 16-byte f32 loads), the hidden rows staged once per CTA in
 // shared memory, fp32 accumulation, one shuffle reduction per row.  The
@@ -54,7 +55,10 @@ logits_vec_kernel(const float* __restrict__ h, int rows, const void* __restrict_
             for (int u = 0; u < UNROLL; ++u) {
                 const int c = c0 + 32 * u;
                 if (c < n4) {
-                    const float4 x = decode4<T>(w[u]);
+                    // the sign of a zero product or the payload of a NaN
+                    // cannot change the fp32 sum, so the hardware f16
+                    // conversion serves
+                    const float4 x = decode4_arith<T>(w[u]);
 #pragma unroll
                     for (int r = 0; r < R; ++r) {
                         const float4 hh = s_h[r * n4 + c];

@@ -540,3 +540,23 @@ def test_select_tokens_needs_uniforms_when_sampling(gbx, cuda):
     ids = torch.zeros(2, dtype=torch.int32, device="cuda")
     with pytest.raises(gbx.GbxError):
         gbx.select_tokens(x, ids, rows=2, vocab=8, temperature=1.0)
+
+
+@pytest.mark.parametrize("wdt,pdt,want_bits", [(1, 1, 0x00000000), (1, 0, 0x00000000), (0, 1, 0x00000000),
+                                               (0, 0, 0x80000000), (30, 30, 0x80000000), (30, 1, 0x00000000)])
+def test_embed_negative_zero_sums(gbx, orc, cuda, wdt, pdt, want_bits):
+    """The reference decodes an f16 -0 to +0 (transformer.cu:514) but keeps
+    f32 and bf16 -0: a sum of two -0 elements is +0 when either table is f16
+    and -0 otherwise."""
+    import torch
+    d, V, C = 64, 4, 4
+    neg0 = {0: np.full((V, d), -0.0, np.float32), 1: np.full((V, d), 0x8000, np.uint16),
+            30: np.full((V, d), 0x8000, np.uint16)}
+    wte, wpe = neg0[wdt], neg0[pdt][:C].copy()
+    ids = np.arange(4, dtype=np.int32)
+    out = torch.empty((4, d), device="cuda")
+    gbx.embed(_t(ids, torch), _t(wte, torch), wdt, _t(wpe, torch), pdt, out, n_tok=4, d=d, vocab=V, n_ctx=C)
+    ref, _ = orc.embed(ids, wte, wdt, wpe, pdt, d, V, C)
+    got = out.cpu().numpy()
+    assert_bits_equal(got, ref, f"-0 sums {wdt}/{pdt}")
+    assert np.all(got.view(np.uint32) == want_bits)

@@ -406,10 +406,7 @@ def run_ours(args, shape, desc, chain_kw, scaling):
                    "chunks_per_step": shape.n_chunks, "cuda_graph": bool(args.graph),
                    "programmatic_dependent_launch": bool(args.pdl),
                    "parallelism": f"row shards of whole sequences over {world} GPU(s), no collective",
-                   "l2": "no flush; every streamed buffer is larger than the 126 MB L2 "
-                         f"(smallest: {shape.chunk_tokens * shape.d * 4 / 1e6:.0f} MB)"
-                   if shape.chunk_tokens * shape.d * 4 > 126e6 else
-                   "inputs smaller than L2 (decode-sized rows); no flush"},
+                   "l2": chain.l2_note()},
         "hbm": {"bytes_per_step": shape.bytes_per_step(),
                 "gbs": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
                 "frac": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9 / peak,

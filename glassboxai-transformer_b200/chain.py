@@ -29,6 +29,13 @@ chunk (each chunk's token ids are its own slice).
 
 ``capture_graph`` records one step into a CUDA graph; ``replay`` launches it
 (the decode-sized chains are launch-bound without it).
+
+Inputs of the per-layer kernels (scores, GELU input, projection and
+ffn-down outputs) that are smaller than 512 MB get one copy per layer,
+cycling through at least 1 GB, so that no kernel finds its input left in the
+126 MB L2 by the previous layer (the real forward feeds each layer new
+data); larger buffers are streamed out of L2 by the traffic between two
+uses anyway.
 """
 from __future__ import annotations
 
@@ -150,18 +157,25 @@ class Chain:
         self.wpe = table(s.n_ctx)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         N, d, F = s.chunk_tokens, s.d, s.ff
+
+        def per_layer(shape_, std):
+            """[copies, *shape_] with copies = 1 for buffers of 512 MB and more."""
+            nbytes = 4 * shape_[0] * shape_[1]
+            copies = 1 if nbytes >= (512 << 20) else min(s.layers, -(-(1 << 30) // nbytes))
+            return normal((copies,) + tuple(shape_), std)
+
         self.h = torch.empty((N, d), **f32)
         self.ln = torch.empty((N, d), **f32)
-        self.attn_out = normal((N, d), act_std)
-        self.ffn_out = normal((N, d), act_std)
-        self.ffn_pre = normal((N, F), act_std)
+        self.attn_out_all = per_layer((N, d), act_std)
+        self.ffn_out_all = per_layer((N, d), act_std)
+        self.ffn_pre_all = per_layer((N, F), act_std)
         self.ffn_act = torch.empty((N, F), **f32)
-        self.scores = normal((s.softmax_rows, s.L), score_std)
+        self.scores_all = per_layer((s.softmax_rows, s.L), score_std)
         if causal and s.kv_len is None:
             # scores[b, h, p, q] = -1e9 for q > p (transformer.cu:220-221)
             mask = torch.triu(torch.ones(s.seq, s.seq, dtype=torch.bool, device=device), diagonal=1)
-            self.scores.view(-1, s.seq, s.seq).masked_fill_(mask, -1e9)
-        self.probs = torch.empty_like(self.scores)
+            self.scores_all.view(-1, s.seq, s.seq).masked_fill_(mask, -1e9)
+        self.probs = torch.empty_like(self.scores_all[0])
         self.g1 = normal((s.layers, d), 0.1, 1.0)
         self.b1 = normal((s.layers, d), 0.02)
         self.g2 = normal((s.layers, d), 0.1, 1.0)
@@ -174,6 +188,37 @@ class Chain:
         self.last_f = torch.empty((B, d), **f32)
         self.out = torch.empty((s.batch, d), **f32)
         self.graph = None
+
+    # the buffers layer l reads (copy l mod copies)
+    def scores(self, l=None):
+        return self.scores_all[(self.s.layers - 1 if l is None else l) % self.scores_all.shape[0]]
+
+    def attn_out(self, l=None):
+        return self.attn_out_all[(self.s.layers - 1 if l is None else l) % self.attn_out_all.shape[0]]
+
+    def ffn_out(self, l=None):
+        return self.ffn_out_all[(self.s.layers - 1 if l is None else l) % self.ffn_out_all.shape[0]]
+
+    def ffn_pre(self, l=None):
+        return self.ffn_pre_all[(self.s.layers - 1 if l is None else l) % self.ffn_pre_all.shape[0]]
+
+    def l2_note(self):
+        """How the step keeps its inputs out of the 126 MB L2 (for bench.py)."""
+        import torch
+        # the embedding tables are gathered by token id, not streamed
+        bufs = [t for k, t in vars(self).items() if isinstance(t, torch.Tensor) and k not in ("wte", "wpe")]
+        footprint = sum(t.numel() * t.element_size() for t in bufs)
+        copies = {k: getattr(self, k + "_all").shape[0] for k in ("scores", "ffn_pre", "attn_out", "ffn_out")}
+        multi = {k: c for k, c in copies.items() if c > 1}
+        if footprint < (252 << 20):
+            return (f"the step's working set ({footprint / 1e6:.1f} MB besides the gathered embedding tables) is "
+                    "about the size of the 126 MB L2: a launch-latency measurement, not a bandwidth one")
+        if not multi:
+            return ("no flush: every streamed buffer is larger than the 126 MB L2 (smallest "
+                    f"{self.h.numel() * 4 / 1e6:.0f} MB)")
+        return ("no flush: per-layer copies of the inputs smaller than 512 MB (" +
+                ", ".join(f"{k} x{c}" for k, c in multi.items()) + "), cycling through up to 1 GB each, so each "
+                "layer's kernels read their inputs from HBM")
 
     def _chunk(self, c, st, run):
         import torch
@@ -189,19 +234,19 @@ class Chain:
                                                      stream=st))
             else:
                 run("residual_layernorm",
-                    lambda: G.residual_layernorm(self.ffn_out, self.h, self.h, self.ln, self.g1[l], self.b1[l],
-                                                 rows=N, d=d, stream=st))
-            run("softmax_rows", lambda: G.softmax_rows(self.scores, self.probs, rows=s.softmax_rows, L=s.L,
+                    lambda: G.residual_layernorm(self.ffn_out(l - 1), self.h, self.h, self.ln, self.g1[l],
+                                                 self.b1[l], rows=N, d=d, stream=st))
+            run("softmax_rows", lambda: G.softmax_rows(self.scores(l), self.probs, rows=s.softmax_rows, L=s.L,
                                                        stream=st))
             run("residual_layernorm",
-                lambda: G.residual_layernorm(self.attn_out, self.h, self.h, self.ln, self.g2[l], self.b2[l],
+                lambda: G.residual_layernorm(self.attn_out(l), self.h, self.h, self.ln, self.g2[l], self.b2[l],
                                              rows=N, d=d, stream=st))
-            run("bias_gelu", lambda: G.bias_gelu(self.ffn_pre, self.ffn_act, self.up_bias[l], rows=N, F=s.ff,
+            run("bias_gelu", lambda: G.bias_gelu(self.ffn_pre(l), self.ffn_act, self.up_bias[l], rows=N, F=s.ff,
                                                  stream=st))
         # final residual add + ln_f on each sequence's last row (transformer.cu:890-896)
         with torch.cuda.stream(st):
             self.last_h.copy_(self.h.view(B, s.seq, d)[:, -1])
-            self.last_f.copy_(self.ffn_out.view(B, s.seq, d)[:, -1])
+            self.last_f.copy_(self.ffn_out(s.layers - 1).view(B, s.seq, d)[:, -1])
         out = self.out[c * B:(c + 1) * B]
         run("final_layernorm", lambda: G.residual_layernorm(self.last_f, self.last_h, None, out, self.gf,
                                                             self.bf, rows=B, d=d, stream=st))

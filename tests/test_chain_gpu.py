@@ -37,19 +37,19 @@ def _oracle_chain(orc, c, s):
     h, bad = orc.embed(ids, wte, s.table_dtype, wpe, s.table_dtype, s.d, s.vocab, s.n_ctx, seq=s.seq,
                        pos_off=s.pos_off)
     assert bad == 0
-    attn_out, ffn_out, ffn_pre, scores = t(c.attn_out), t(c.ffn_out), t(c.ffn_pre), t(c.scores)
     g1, b1, g2, b2, ub = t(c.g1), t(c.b1), t(c.g2), t(c.b2), t(c.up_bias)
-    # the scores and the GELU input are the same every layer: their last
-    # layer's outputs are computed once
-    probs = orc.softmax_rows(scores, nthreads=orc.max_threads())
-    act = orc.bias_gelu(ffn_pre, ub[s.layers - 1], nthreads=orc.max_threads())
+    L = s.layers
+    # each layer reads its own inputs; softmax and GELU outputs are the last layer's
+    probs = orc.softmax_rows(t(c.scores(L - 1)), nthreads=orc.max_threads())
+    act = orc.bias_gelu(t(c.ffn_pre(L - 1)), ub[L - 1], nthreads=orc.max_threads())
     ln = None
-    for l in range(s.layers):
+    for l in range(L):
         if l == 0:
             ln = orc.layernorm(h, g1[0], b1[0])
         else:
-            h, ln = orc.residual_layernorm(ffn_out, h, g1[l], b1[l])
-        h, ln = orc.residual_layernorm(attn_out, h, g2[l], b2[l])
+            h, ln = orc.residual_layernorm(t(c.ffn_out(l - 1)), h, g1[l], b1[l])
+        h, ln = orc.residual_layernorm(t(c.attn_out(l)), h, g2[l], b2[l])
+    ffn_out = t(c.ffn_out(L - 1))
     B = s.chunk_seqs
     last_h = h.reshape(B, s.seq, s.d)[:, -1].copy()
     last_f = ffn_out.reshape(B, s.seq, s.d)[:, -1].copy()

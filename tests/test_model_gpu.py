@@ -136,3 +136,21 @@ def test_sharded_model_fails_as_a_whole(gm, cuda, tmp_path):
     assert sm.forward(np.zeros(8, np.int32), batch=2).shape == (2, 50257)   # still usable
     with pytest.raises(Exception):
         gm.ShardedModel(path, [99], vocab=50257)
+
+
+def test_forward_gpt2_small_shapes_match_reference(gm, orc, cuda, tmp_path):
+    """GPT-2 small widths (d 768, 12 heads of 64, ff 3072; 2 layers, f16
+    weights) and 64 tokens, so every hot-path kernel runs its vector path
+    (the tiny model above sends the LayerNorm and softmax rows down the
+    general paths).  Same bar as above, against the reference's forward."""
+    orc = _ref_or_skip(orc)
+    path = str(tmp_path / "small.gguf")
+    write_tiny_gpt2(path, GGML_F16, d=768, heads=12, ff=3072, layers=2, ctx=128, seed=31)
+    ids = np.random.default_rng(6).integers(0, 50257, 64).astype(np.int32)
+    ref_model = orc.RefModel(path)
+    want = ref_model.forward(ids)
+    ref_model.close()
+    got = gm.Model(path).forward(ids)
+    err = np.abs(got.astype(np.float64) - want)
+    assert np.all(err <= 1e-5 + 1e-3 * np.abs(want)), f"max abs err {err.max():.3g}"
+    assert int(np.argmax(got)) == int(np.argmax(want))

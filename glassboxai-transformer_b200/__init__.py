@@ -53,6 +53,8 @@ SIGNATURES = {
     "gbx_attn_softmax_rows": [_vp, _vp, _i64, _int, _int, _int, _f, _int, _vp],
     "gbx_logits": [_vp, _i64, _vp, _int, _vp, _int, _int, _vp],
     "gbx_select_tokens": [_vp, _i64, _int, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
+    "gbx_split_tf32": [_vp, _vp, _vp, _i64, _vp],
+    "gbx_linear": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp],
 }
 _RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
 
@@ -155,3 +157,19 @@ def select_tokens(logits, out_ids, *, rows, vocab, temperature=0.0, uniforms=Non
                   out_best_logit=None, stream=None):
     _check(lib().gbx_select_tokens(_p(logits), rows, vocab, float(temperature), _p(uniforms), _p(out_ids),
                                    _p(out_best), _p(out_best_logit), _stream(stream)))
+
+
+ACT_NONE, ACT_GELU = 0, 1
+LINEAR_TIMEOUT = 4
+
+
+def split_tf32(x, hi, lo, *, n, stream=None):
+    """hi = tf32(x), lo = tf32(x - hi): the operand pair gbx_linear reads."""
+    _check(lib().gbx_split_tf32(_p(x), _p(hi), _p(lo), n, _stream(stream)))
+
+
+def linear(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, bias=None, resid=None, y_lo=None, act=ACT_NONE, err_flag=None,
+           stream=None):
+    """y = act(x . w^T + bias) + resid on the tensor cores (tf32 pairs, see gbx.h)."""
+    _check(lib().gbx_linear(_p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(resid), _p(y), _p(y_lo), M, N, K,
+                            act, _p(err_flag), _stream(stream)))

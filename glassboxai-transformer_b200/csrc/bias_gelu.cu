@@ -10,16 +10,11 @@
 // reference's nvcc build fuses it, and CUDA's tanhf (no fast-math):
 //   u = in + bias; out = u * (0.5f * (1.0f + tanhf(0.7978845608f * (u + 0.044715f*u*u*u))))
 #include "gbx_common.cuh"
+#include "gelu.cuh"
 
 namespace gbx {
 
 constexpr int kGeluU = 4;
-
-__device__ __forceinline__ float gelu_tanh(float u)
-{
-    const float inner = fmaf((0.044715f * u) * u, u, u);
-    return u * (0.5f * (1.0f + tanhf(0.7978845608f * inner)));
-}
 
 __device__ __forceinline__ float4 gelu4(float4 u)
 {

@@ -1,0 +1,490 @@
+// linear.cu -- the weight contractions either side of the hot path on the
+// sm_100a tensor cores, with the path's own epilogues fused:
+//   y = act(x . w^T + bias) + resid
+// replacing the GEMVs computeQKVKernel, projectionKernel, ffnUpKernel and
+// ffnDownKernel (transformer.cu:187-294).  The reference computes these in
+// fp32 on the CUDA cores; here every operand arrives as a tf32 pair
+// (hi, lo) and the tensor cores form hi.hi + hi.lo + lo.hi with f32
+// accumulation, which keeps each product within ~2^-21 of fp32's.
+//
+// Kernel layout (one CTA per SM, persistent over 128 x 256 output tiles):
+//   warp 0      TMA producer: per K block, the x_hi, x_lo, w_hi, w_lo tiles
+//               (K-major, 64- or 128-byte swizzled rows) into a ring of
+//               shared-memory stages, completion counted on full[stage]
+//   warp 1      owns the 512 TMEM columns (two 128 x 256 f32 accumulators);
+//               one thread issues tcgen05.mma (kind::tf32, M 128, N 256,
+//               K 8) per product term and K step, and tcgen05.commit frees a
+//               stage (empty[stage]) or hands an accumulator to the epilogue
+//               (acc_full)
+//   warps 2-5   epilogue: tcgen05.ld 16 columns of a row at a time, + bias,
+//               GELU, + resid, optional tf32 split, 16-byte stores; then
+//               acc_empty lets the MMA thread reuse the accumulator, so one
+//               tile's epilogue overlaps the next tile's MMAs
+// Every mbarrier wait is bounded (1 s, %globaltimer): a wait that runs out
+// sets the CTA's abort word, every role leaves its loop, the producer waits
+// (bounded) for its loads in flight, the MMA thread for its MMAs, TMEM is
+// freed, and GBX_LINEAR_TIMEOUT is OR-ed into err_flag.  No cluster
+// multicast: every TMA load fills this CTA's own shared memory.
+#include <cuda.h>
+#include <stdlib.h>
+
+#include <mutex>
+
+#include "gbx_common.cuh"
+#include "gelu.cuh"
+#include "tcgen05.cuh"
+
+namespace gbx {
+
+constexpr int kLinBM = 128;        // tile rows = TMEM lanes
+constexpr int kLinBN = 256;        // tile columns = TMEM columns of one accumulator
+constexpr int kLinThreads = 192;   // 6 warps
+constexpr int kLinAccums = 2;      // 2 x 256 = all 512 TMEM columns
+constexpr int kLinTmemCols = kLinAccums * kLinBN;
+constexpr int kLinEpiThreads = 128;
+constexpr uint64_t kLinWaitNs = 1000000000ull;
+
+template <int BK>
+struct LinCfg {
+    static constexpr int row_bytes = BK * 4;             // 64 or 128: the swizzle width
+    static constexpr int a_bytes = kLinBM * row_bytes;   // one x tile
+    static constexpr int b_bytes = kLinBN * row_bytes;   // one w tile
+    static constexpr int stage_bytes = 2 * a_bytes + 2 * b_bytes;
+    static constexpr int stages = (196 * 1024) / stage_bytes;   // BK 16: 4, BK 32: 2
+    static constexpr int ksteps = BK / 8;                       // tf32 MMA K = 8 (32 bytes)
+    static constexpr int nbars = 2 * stages + 2 * kLinAccums + 1;
+    static constexpr size_t smem = (size_t)stages * stage_bytes + 1024 + 8 * nbars + 16;
+    static_assert(BK == 16 || BK == 32, "swizzle width");
+    static_assert(stages >= 2, "pipeline depth");
+    static_assert(a_bytes % 1024 == 0 && b_bytes % 1024 == 0, "tiles stay aligned to the swizzle repeat");
+};
+
+struct LinearArgs {
+    const float* bias;
+    const float* resid;
+    float* y;
+    float* y_lo;
+    int* err;
+    int64_t M;
+    int N;
+    int K;
+    int n_blocks;
+    int k_blocks;
+    int tiles;
+    int act;
+    int has_xlo;
+    int has_wlo;
+};
+
+__device__ __forceinline__ void split_value(float x, float& hi, float& lo)
+{
+    hi = tc::to_tf32(x);
+    if (isinf(hi) && !isinf(x)) hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);   // rounding overflowed
+    lo = isfinite(hi) ? tc::to_tf32(x - hi) : 0.0f;
+}
+
+__device__ __forceinline__ float epi_value(float acc, int n, int64_t row, const LinearArgs& a)
+{
+    float v = acc;
+    if (a.bias) v = v + __ldg(a.bias + n);
+    if (a.act == GBX_ACT_GELU) v = gelu_tanh(v);
+    if (a.resid) v = a.resid[row * a.N + n] + v;
+    return v;
+}
+
+// 16 accumulator columns of one output row: columns n .. n+15 (n < N).
+template <bool VEC>
+__device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, int n, const LinearArgs& a)
+{
+    const int64_t off = row * a.N;
+    if (VEC) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            if (n + j >= a.N) break;   // N % 4 == 0: a float4 is all in or all out
+            float4 o;
+            if (a.bias || a.resid || a.act) {
+                float4 b = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + n + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                if (a.bias) o = make_float4(o.x + b.x, o.y + b.y, o.z + b.z, o.w + b.w);
+                if (a.act == GBX_ACT_GELU) o = make_float4(gelu_tanh(o.x), gelu_tanh(o.y), gelu_tanh(o.z), gelu_tanh(o.w));
+                if (a.resid) {
+                    const float4 r = *reinterpret_cast<const float4*>(a.resid + off + n + j);
+                    o = make_float4(r.x + o.x, r.y + o.y, r.z + o.z, r.w + o.w);
+                }
+            } else {
+                o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
+            if (a.y_lo) {
+                float4 h, l;
+                split_value(o.x, h.x, l.x);
+                split_value(o.y, h.y, l.y);
+                split_value(o.z, h.z, l.z);
+                split_value(o.w, h.w, l.w);
+                *reinterpret_cast<float4*>(a.y + off + n + j) = h;
+                *reinterpret_cast<float4*>(a.y_lo + off + n + j) = l;
+            } else {
+                *reinterpret_cast<float4*>(a.y + off + n + j) = o;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if (n + j >= a.N) break;
+            const float o = epi_value(v[j], n + j, row, a);
+            if (a.y_lo) {
+                float h, l;
+                split_value(o, h, l);
+                a.y[off + n + j] = h;
+                a.y_lo[off + n + j] = l;
+            } else {
+                a.y[off + n + j] = o;
+            }
+        }
+    }
+}
+
+template <int BK, bool VEC>
+__global__ void __launch_bounds__(kLinThreads, 1)
+linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constant__ CUtensorMap map_xl,
+                     const __grid_constant__ CUtensorMap map_wh, const __grid_constant__ CUtensorMap map_wl,
+                     const LinearArgs a)
+{
+    using C = LinCfg<BK>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::stages * C::stage_bytes);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::nbars);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const uint32_t full0 = tc::smem_u32(bars);                     // full[s]      = full0 + 8 s
+    const uint32_t empty0 = full0 + 8 * C::stages;                 // empty[s]
+    const uint32_t accf0 = empty0 + 8 * C::stages;                 // acc_full[b]
+    const uint32_t acce0 = accf0 + 8 * kLinAccums;                 // acc_empty[b]
+    const uint32_t drain = acce0 + 8 * kLinAccums;
+    const uint32_t smem0 = tc::smem_u32(smem);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::stages; ++s) {
+            tc::mbar_init(full0 + 8 * s, 1);
+            tc::mbar_init(empty0 + 8 * s, 1);
+        }
+        for (int b = 0; b < kLinAccums; ++b) {
+            tc::mbar_init(accf0 + 8 * b, 1);
+            tc::mbar_init(acce0 + 8 * b, kLinEpiThreads);
+        }
+        tc::mbar_init(drain, 1);
+        *abort = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch(&map_xh);
+        tc::tma_prefetch(&map_wh);
+        if (a.has_xlo) tc::tma_prefetch(&map_xl);
+        if (a.has_wlo) tc::tma_prefetch(&map_wl);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), kLinTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------------------------------------------- producer
+            const uint32_t bytes = (uint32_t)(C::a_bytes * (1 + a.has_xlo) + C::b_bytes * (1 + a.has_wlo));
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;    // bit s: stage s has had a load issued
+            uint32_t lastpar = 0;   // bit s: parity of the phase of its last load
+            for (int t = blockIdx.x; t < a.tiles && !*abort; t += gridDim.x) {
+                const int y_x = (t / a.n_blocks) * kLinBM;
+                const int y_w = (t % a.n_blocks) * kLinBN;
+                for (int kb = 0; kb < a.k_blocks; ++kb) {
+                    if (!tc::mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kLinWaitNs)) break;
+                    const uint32_t full = full0 + 8 * stage;
+                    const uint32_t base = smem0 + stage * C::stage_bytes;
+                    tc::mbar_arrive_expect_tx(full, bytes);
+                    const int x = kb * BK;
+                    tc::tma_load_2d(base, &map_xh, full, x, y_x);
+                    if (a.has_xlo) tc::tma_load_2d(base + C::a_bytes, &map_xl, full, x, y_x);
+                    tc::tma_load_2d(base + 2 * C::a_bytes, &map_wh, full, x, y_w);
+                    if (a.has_wlo) tc::tma_load_2d(base + 2 * C::a_bytes + C::b_bytes, &map_wl, full, x, y_w);
+                    issued |= 1u << stage;
+                    lastpar = (lastpar & ~(1u << stage)) | (phase << stage);
+                    if (++stage == C::stages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // every load issued has landed before the CTA may exit
+            for (int s = 0; s < C::stages; ++s)
+                if (issued & (1u << s)) tc::mbar_wait(full0 + 8 * s, (lastpar >> s) & 1, nullptr, kLinWaitNs);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------------------------------------------- MMA issuer
+            constexpr uint32_t idesc = tc::idesc_tf32(kLinBM, kLinBN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
+                if (!tc::mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kLinWaitNs)) break;
+                tc::fence_after_sync();
+                const uint32_t d = tmem + acc * kLinBN;
+                for (int kb = 0; kb < a.k_blocks; ++kb) {
+                    if (!tc::mbar_wait(full0 + 8 * stage, phase, abort, kLinWaitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t base = smem0 + stage * C::stage_bytes;
+#pragma unroll
+                    for (int ks = 0; ks < C::ksteps; ++ks) {
+                        const uint32_t off = ks * 32;
+                        const uint64_t xh = tc::smem_desc(base + off, C::row_bytes);
+                        const uint64_t wh = tc::smem_desc(base + 2 * C::a_bytes + off, C::row_bytes);
+                        tc::mma_tf32(d, xh, wh, idesc, (kb | ks) != 0);
+                        if (a.has_wlo)
+                            tc::mma_tf32(d, xh, tc::smem_desc(base + 2 * C::a_bytes + C::b_bytes + off, C::row_bytes),
+                                         idesc, 1);
+                        if (a.has_xlo)
+                            tc::mma_tf32(d, tc::smem_desc(base + C::a_bytes + off, C::row_bytes), wh, idesc, 1);
+                    }
+                    tc::mma_commit(empty0 + 8 * stage);   // the stage is free once these MMAs are done
+                    if (++stage == C::stages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc::mma_commit(accf0 + 8 * acc);   // accumulator complete
+                if (++acc == kLinAccums) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            // every MMA issued has completed before TMEM is freed
+            tc::mma_commit(drain);
+            tc::mbar_wait(drain, 0, nullptr, kLinWaitNs);
+        }
+    } else {
+        // -------------------------------------------------------- epilogue
+        const int quarter = warp & 3;   // the TMEM lanes this warp may read
+        const int row_in_tile = 32 * quarter + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < a.tiles; t += gridDim.x) {
+            // warp-uniform outcome: tcgen05.ld below needs the whole warp
+            const bool ready = tc::mbar_wait(accf0 + 8 * acc, acc_phase, abort, kLinWaitNs);
+            if (!__all_sync(0xffffffffu, ready)) break;
+            tc::fence_after_sync();
+            const int64_t row = (int64_t)(t / a.n_blocks) * kLinBM + row_in_tile;
+            const int n0 = (t % a.n_blocks) * kLinBN;
+            const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + acc * kLinBN;
+            for (int c = 0; c < kLinBN / 16; ++c) {
+                const int n = n0 + 16 * c;
+                if (n >= a.N) break;   // uniform over the warp
+                float v[16];
+                tc::tmem_ld16(tbase + 16 * c, v);
+                tc::tmem_ld_wait();
+                if (row < a.M) epi_store16<VEC>(v, row, n, a);
+            }
+            tc::fence_before_sync();
+            tc::mbar_arrive(acce0 + 8 * acc);
+            if (++acc == kLinAccums) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+
+    __syncthreads();   // every role has left its loop (all waits are bounded)
+    if (warp == 1) {
+        __syncwarp();
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kLinTmemCols);
+    }
+    if (threadIdx.x == 0 && *abort && a.err) atomicOr(a.err, GBX_LINEAR_TIMEOUT);
+}
+
+// ------------------------------------------------------------------ split
+__global__ void __launch_bounds__(256) split_tf32_vec_kernel(const float4* x, float4* hi, float4* lo, int64_t n4)
+{
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = x[i];
+        float4 h, l;
+        split_value(v.x, h.x, l.x);
+        split_value(v.y, h.y, l.y);
+        split_value(v.z, h.z, l.z);
+        split_value(v.w, h.w, l.w);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+__global__ void __launch_bounds__(256) split_tf32_scalar_kernel(const float* x, float* hi, float* lo, int64_t n)
+{
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float h, l;
+        split_value(x[i], h, l);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Row-major [rows, K] fp32, boxes of box_rows x BK with the BK-wide swizzle.
+static int make_map(CUtensorMap* m, const float* base, int64_t rows, int K, int box_rows, int BK)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return set_error(GBX_ECUDA, "gbx_linear: cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * sizeof(float)};
+    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GBX_EINVAL, "gbx_linear: tensor map rejected (CUresult %d)", (int)r);
+    return GBX_OK;
+}
+
+template <int BK, bool VEC>
+static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
+                         const LinearArgs& a, cudaStream_t s)
+{
+    using C = LinCfg<BK>;
+    DeviceInfo di;
+    if (device_info(&di) != GBX_OK) return GBX_ECUDA;
+    if ((size_t)di.max_smem_optin < C::smem)
+        return set_error(GBX_ERANGE, "gbx_linear: needs %zu bytes of shared memory per CTA", C::smem);
+    CUtensorMap mxh, mxl, mwh, mwl;
+    int rc;
+    if ((rc = make_map(&mxh, x_hi, a.M, a.K, kLinBM, BK)) != GBX_OK) return rc;
+    if ((rc = make_map(&mwh, w_hi, a.N, a.K, kLinBN, BK)) != GBX_OK) return rc;
+    if (a.has_xlo) {
+        if ((rc = make_map(&mxl, x_lo, a.M, a.K, kLinBM, BK)) != GBX_OK) return rc;
+    } else {
+        mxl = mxh;   // never loaded
+    }
+    if (a.has_wlo) {
+        if ((rc = make_map(&mwl, w_lo, a.N, a.K, kLinBN, BK)) != GBX_OK) return rc;
+    } else {
+        mwl = mwh;
+    }
+    auto k = linear_tf32x3_kernel<BK, VEC>;
+    // per device, so set on every call (a host-side attribute write)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::smem) != cudaSuccess)
+        return set_error(GBX_ECUDA, "gbx_linear: shared-memory attribute refused");
+    const int grid = a.tiles < di.sm_count ? a.tiles : di.sm_count;
+    k<<<grid, kLinThreads, C::smem, s>>>(mxh, mxl, mwh, mwl, a);
+    return check_launch("gbx_linear");
+}
+
+}  // namespace gbx
+
+using namespace gbx;
+
+extern "C" int gbx_split_tf32(const float* x, float* hi, float* lo, int64_t n, gbx_stream_t stream)
+{
+    if (n < 0) return set_error(GBX_EINVAL, "gbx_split_tf32: n=%lld", (long long)n);
+    if (n == 0) return GBX_OK;
+    if (!x || !hi || !lo) return set_error(GBX_EINVAL, "gbx_split_tf32: null pointer");
+    if (lo == x || lo == hi) return set_error(GBX_EINVAL, "gbx_split_tf32: lo must not alias x or hi");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (n % 4 == 0 && aligned16(x) && aligned16(hi) && aligned16(lo)) {
+        const int grid = persistent_grid(split_tf32_vec_kernel, 256, 0, (n / 4 + 255) / 256, 8);
+        if (grid < 1) return GBX_ECUDA;
+        split_tf32_vec_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(hi),
+                                                   reinterpret_cast<float4*>(lo), n / 4);
+    } else {
+        const int grid = persistent_grid(split_tf32_scalar_kernel, 256, 0, (n + 255) / 256, 8);
+        if (grid < 1) return GBX_ECUDA;
+        split_tf32_scalar_kernel<<<grid, 256, 0, s>>>(x, hi, lo, n);
+    }
+    return check_launch("gbx_split_tf32");
+}
+
+// Tile K width: 16 (64-byte rows, 4 pipeline stages) unless GBX_LINEAR_BK=32
+// (128-byte rows, 2 stages) is set in the environment, read once.
+static int linear_bk()
+{
+    static int bk = [] {
+        const char* e = getenv("GBX_LINEAR_BK");
+        return (e && atoi(e) == 32) ? 32 : 16;
+    }();
+    return bk;
+}
+
+extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
+                          const float* bias, const float* resid, float* y, float* y_lo, int64_t M, int N, int K,
+                          int act, int* err_flag, gbx_stream_t stream)
+{
+    if (M < 0 || N <= 0 || K <= 0)
+        return set_error(GBX_EINVAL, "gbx_linear: M=%lld N=%d K=%d", (long long)M, N, K);
+    if (M == 0) return GBX_OK;
+    if (!x_hi || !w_hi || !y) return set_error(GBX_EINVAL, "gbx_linear: null pointer");
+    if (act != GBX_ACT_NONE && act != GBX_ACT_GELU) return set_error(GBX_EINVAL, "gbx_linear: act=%d", act);
+    if (K % 4 != 0) return set_error(GBX_EINVAL, "gbx_linear: K=%d is not a multiple of 4", K);
+    if (!aligned16(x_hi) || !aligned16(w_hi) || (x_lo && !aligned16(x_lo)) || (w_lo && !aligned16(w_lo)))
+        return set_error(GBX_EINVAL, "gbx_linear: x and w must be 16-byte aligned");
+    if (y_lo == y || (const float*)y == x_hi || (const float*)y == w_hi || (x_lo && (const float*)y == x_lo) ||
+        (w_lo && (const float*)y == w_lo))
+        return set_error(GBX_EINVAL, "gbx_linear: y aliases an operand");
+    if (M > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: M=%lld", (long long)M);
+    const int64_t m_blocks = (M + kLinBM - 1) / kLinBM;
+    const int64_t n_blocks = ((int64_t)N + kLinBN - 1) / kLinBN;
+    if (m_blocks * n_blocks > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: too many tiles");
+
+    LinearArgs a;
+    a.bias = bias;
+    a.resid = resid;
+    a.y = y;
+    a.y_lo = y_lo;
+    a.err = err_flag;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.n_blocks = (int)n_blocks;
+    a.tiles = (int)(m_blocks * n_blocks);
+    a.act = act;
+    a.has_xlo = x_lo != nullptr;
+    a.has_wlo = w_lo != nullptr;
+    const bool vec = N % 4 == 0 && aligned16(y) && (!y_lo || aligned16(y_lo)) && (!resid || aligned16(resid)) &&
+                     (!bias || aligned16(bias));
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (linear_bk() == 32) {
+        a.k_blocks = (K + 31) / 32;
+        return vec ? launch_linear<32, true>(x_hi, x_lo, w_hi, w_lo, a, s)
+                   : launch_linear<32, false>(x_hi, x_lo, w_hi, w_lo, a, s);
+    }
+    a.k_blocks = (K + 15) / 16;
+    return vec ? launch_linear<16, true>(x_hi, x_lo, w_hi, w_lo, a, s)
+               : launch_linear<16, false>(x_hi, x_lo, w_hi, w_lo, a, s);
+}

@@ -192,6 +192,52 @@ int gbx_logits(const float* h, int64_t rows, const void* wte, int wte_dtype, flo
 int gbx_select_tokens(const float* logits, int64_t rows, int vocab, double temperature, const double* uniforms,
                       int32_t* out_ids, int32_t* out_best, float* out_best_logit, gbx_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * The contractions either side of the path, on the tcgen05 tensor cores.
+ *
+ * An fp32 operand enters as a tf32 pair: hi = x rounded to tf32 (10
+ * mantissa bits) and lo = (x - hi) rounded to tf32, so hi + lo carries
+ * 21 of x's 24 significant bits.  gbx_linear forms
+ *   x.w = hi_x.hi_w + hi_x.lo_w + lo_x.hi_w
+ * with f32 accumulation (the lo_x.lo_w term, below 2^-22 of |x w|, is
+ * dropped): each product is within ~2^-21 of fp32's, the sums are fp32.
+ * ------------------------------------------------------------------------ */
+
+/* Bit set in *err_flag by gbx_linear when a wait of its pipeline ran past
+ * one second (the output is then incomplete; the kernel returns without
+ * faulting). */
+enum { GBX_LINEAR_TIMEOUT = 4 };
+enum { GBX_ACT_NONE = 0, GBX_ACT_GELU = 1 };
+
+/* hi[i] = tf32(x[i]); lo[i] = tf32(x[i] - hi[i]) for n elements (0 when hi
+ * is not finite).  No counterpart in the reference: it prepares operands
+ * for gbx_linear (weights once at load, activations per step).  hi may
+ * alias x. */
+int gbx_split_tf32(const float* x, float* hi, float* lo, int64_t n, gbx_stream_t stream);
+
+/*
+ * y[m, n] = act(sum_k x[m, k] w[n, k] + bias[n]) + resid[m, n]
+ * for m < M, n < N, k < K: x [M, K] and w [N, K] row-major (the
+ * reference's weight layout, w[i * K + j]), given as tf32 pairs
+ * (x_hi, x_lo) and (w_hi, w_lo).  Replaces the GEMVs of computeQKVKernel
+ * (transformer.cu:187-210, bias only), projectionKernel (:251-264) and
+ * ffnDownKernel (:281-294) (bias + residual), and ffnUpKernel (:266-279)
+ * (bias + GELU, act = GBX_ACT_GELU), in one launch per call.
+ *   x_lo / w_lo  may be NULL when that operand is exact in tf32 (weights
+ *                decoded from f16 or bf16 are): one product term less
+ *   bias, resid  may be NULL; resid may alias y (read, then written, by
+ *                the same thread)
+ *   y_lo         NULL: y receives the fp32 result.  Otherwise y and y_lo
+ *                receive its tf32 pair (gbx_split_tf32 of it), ready to be
+ *                the x operand of the next gbx_linear
+ *   err_flag     device int32 (may be NULL): GBX_LINEAR_TIMEOUT
+ * K must be a multiple of 4 and x_hi, x_lo, w_hi, w_lo 16-byte aligned
+ * (the TMA row and base rules); M < 2^31.  y must not overlap x or w.
+ */
+int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo, const float* bias,
+               const float* resid, float* y, float* y_lo, int64_t M, int N, int K, int act, int* err_flag,
+               gbx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

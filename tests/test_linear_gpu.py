@@ -1,0 +1,301 @@
+"""Parity of gbx_linear (the tcgen05 tf32-pair GEMM with the reference's
+GEMV epilogues) and gbx_split_tf32, called through the C ABI.
+
+Reference semantics (transformer.cu:187-294): y[m, n] = act(bias[n] +
+sum_k x[m, k] w[n, k]) + resid[m, n], in fp32.  The check is against the
+exact value (float64 dot product of the same fp32 inputs) with the bound an
+fp32 evaluation in any order meets, widened by the split error:
+  |y - exact| <= (K 2^-23 + 2^-20) sum_k |x w| + 4 eps_32 (|exact| + |b| + |r|) + 1e-6
+(K 2^-23: twice fp32's worst-case accumulation bound, for an accumulator
+whose rounding is not specified; 2^-20: the dropped lo.lo term and the
+tf32 rounding of the lo parts, each below 2^-22 |x w|).  GELU is 1.13-
+Lipschitz, so after it the same bound times 1.2 applies.  A wrong tile,
+K block or descriptor gives errors of order |x w|, far above the bound.
+Every output sits between NaN-canary guard rows that must survive.
+"""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CANARY = np.uint32(0x7FBADBAD)
+
+
+def _tf32_rna(x):
+    """cvt.rna.tf32.f32 for finite x: round the 13 low mantissa bits to
+    nearest, ties away from zero."""
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    sign = b & 0x80000000
+    mag = ((b & 0x7FFFFFFF) + 0x1000) & 0xFFFFE000
+    return (sign | mag).astype(np.uint32).view(np.float32)
+
+
+def _guarded(torch, rows, cols):
+    full = torch.empty((rows + 2, cols), dtype=torch.float32, device="cuda")
+    full.view(torch.int32).fill_(int(CANARY.view(np.int32)))
+    return full, full[1:rows + 1]
+
+
+def _check_guards(full):
+    h = full.cpu().numpy().view(np.uint32)
+    assert np.all(h[0] == CANARY) and np.all(h[-1] == CANARY), "write outside the output rows"
+
+
+def _split(gbx, torch, a):
+    hi = torch.empty_like(a)
+    lo = torch.empty_like(a)
+    gbx.split_tf32(a, hi, lo, n=a.numel())
+    return hi, lo
+
+
+def _gelu64(u):
+    return u * (0.5 * (1.0 + np.tanh(0.7978845608 * (u + 0.044715 * u * u * u))))
+
+
+def _expected(x, w, bias, resid, act):
+    x64, w64 = x.astype(np.float64), w.astype(np.float64)
+    dot = x64 @ w64.T
+    mag = np.abs(x64) @ np.abs(w64).T
+    K = x.shape[1]
+    bound = (K * 2.0 ** -23 + 2.0 ** -20) * mag
+    v = dot + (bias.astype(np.float64) if bias is not None else 0.0)
+    extra = np.abs(v) + (np.abs(bias.astype(np.float64)) if bias is not None else 0.0)
+    if act == 1:
+        v = _gelu64(v)
+        bound = 1.2 * bound
+        extra = extra + np.abs(v)
+    if resid is not None:
+        v = resid.astype(np.float64) + v
+        extra = extra + np.abs(resid.astype(np.float64)) + np.abs(v)
+    tol = bound + 4 * np.finfo(np.float32).eps * extra + 1e-6
+    return v, tol
+
+
+def _assert_within(got, want, tol, what):
+    err = np.abs(got.astype(np.float64) - want)
+    bad = ~(err <= tol)
+    if bad.any():
+        i = np.unravel_index(int(np.argmax(np.where(bad, err - tol, -np.inf))), err.shape)
+        raise AssertionError(f"{what}: {int(bad.sum())} of {err.size} outside the bound; worst at {i}: "
+                             f"{got[i]!r} vs {want[i]!r} (|d| {err[i]:.3g} > {tol[i]:.3g})")
+
+
+def test_split_tf32_pairs(gbx, cuda):
+    import torch
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(4099).astype(np.float32) * np.float32(3e3),
+                        np.array([0.0, -0.0, 1.0, -1.5, 3.4028235e38, -3.4028235e38, 1e-30, np.inf, -np.inf,
+                                  np.nan, 1.0000001, 0.99999994, 65504.0, 1.1754944e-38], np.float32)])
+    # n not a multiple of 4 (scalar kernel), a multiple of 4 (vector kernel),
+    # and an operand 4 bytes off 16-byte alignment (scalar kernel)
+    for n, off in ((x.size, 0), (4096, 0), (4096, 1)):
+        xs = x[:n]
+        full = torch.from_numpy(np.concatenate([np.zeros(off, np.float32), xs])).cuda()
+        d = full[off:]
+        hi = torch.empty(n + off, dtype=torch.float32, device="cuda")[off:]
+        lo = torch.empty(n + off, dtype=torch.float32, device="cuda")[off:]
+        gbx.split_tf32(d, hi, lo, n=n)
+        torch.cuda.synchronize()
+        h, l = hi.cpu().numpy(), lo.cpu().numpy()
+        fin = np.isfinite(xs)
+        assert np.all((h[fin].view(np.uint32) & 0x1FFF) == 0), "hi is not a tf32 value"
+        assert np.all((l[fin].view(np.uint32) & 0x1FFF) == 0), "lo is not a tf32 value"
+        # hi is the nearest tf32 value (ties away) wherever that is finite
+        rna = _tf32_rna(xs[fin])
+        ok = np.isfinite(rna)
+        assert np.array_equal(h[fin][ok].view(np.uint32), rna[ok].view(np.uint32))
+        # largest finite values whose rounding overflows: hi is the truncation
+        assert np.all(np.isfinite(h[fin]))
+        err = np.abs(h[fin].astype(np.float64) + l[fin] - xs[fin])
+        assert np.all(err <= 2.0 ** -22 * np.abs(xs[fin]) + 2.0 ** -126)
+        assert np.array_equal(h[~fin & ~np.isnan(xs)], xs[~fin & ~np.isnan(xs)])
+        assert np.all(np.isnan(h[np.isnan(xs)]))
+        assert np.all(l[~fin] == 0)
+
+
+SHAPES = [
+    # (M, N, K)
+    (1, 8, 4),
+    (37, 100, 20),          # every tail: M, N (not a multiple of 16) and K (< one K block)
+    (128, 256, 32),         # one whole tile
+    (129, 257, 52),         # one past each tile edge
+    (300, 768, 768),        # GPT-2 small proj (N a multiple of 256)
+    (257, 2304, 768),       # GPT-2 small QKV
+    (96, 1600, 1600),       # GPT-2 XL proj (N = 6.25 tiles)
+    (64, 768, 3072),        # GPT-2 small down (K = 3072)
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_linear_bias(gbx, cuda, M, N, K):
+    import torch
+    rng = np.random.default_rng(M * 7 + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    xd, wd, bd = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    xh, xl = _split(gbx, torch, xd)
+    wh, wl = _split(gbx, torch, wd)
+    full, y = _guarded(torch, M, N)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=bd, err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    want, tol = _expected(x, w, b, None, 0)
+    _assert_within(y.cpu().numpy(), want, tol, f"linear {M}x{N}x{K}")
+    _check_guards(full)
+
+
+@pytest.mark.parametrize("M,N,K", [(129, 257, 52), (200, 3072, 768), (64, 6400, 1600)])
+def test_linear_gelu_and_split_output(gbx, cuda, M, N, K):
+    """ffnUpKernel's epilogue: GELU(bias + x.w); the output as a tf32 pair
+    (what the down projection reads) and as fp32."""
+    import torch
+    rng = np.random.default_rng(N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    xd, wd, bd = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    xh, xl = _split(gbx, torch, xd)
+    wh, wl = _split(gbx, torch, wd)
+    want, tol = _expected(x, w, b, None, 1)
+    full, y = _guarded(torch, M, N)
+    gbx.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=bd, act=gbx.ACT_GELU)
+    fh, yh = _guarded(torch, M, N)
+    fl, yl = _guarded(torch, M, N)
+    gbx.linear(xh, xl, wh, wl, yh, M=M, N=N, K=K, bias=bd, act=gbx.ACT_GELU, y_lo=yl)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    _assert_within(got, want, tol, "bias+GELU")
+    h, l = yh.cpu().numpy(), yl.cpu().numpy()
+    assert np.all((h.view(np.uint32) & 0x1FFF) == 0) and np.all((l.view(np.uint32) & 0x1FFF) == 0)
+    # the pair is the split of the same fp32 value
+    assert np.array_equal(h.view(np.uint32), _tf32_rna(got).view(np.uint32))
+    assert np.all(np.abs(h.astype(np.float64) + l - got) <= 2.0 ** -22 * np.abs(got) + 1e-30)
+    for f in (full, fh, fl):
+        _check_guards(f)
+
+
+@pytest.mark.parametrize("M,N,K", [(37, 100, 20), (300, 1600, 1600), (130, 768, 3072)])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_linear_residual(gbx, cuda, M, N, K, in_place):
+    """projectionKernel / ffnDownKernel: resid + (bias + x.w), also in place
+    on the residual stream."""
+    import torch
+    rng = np.random.default_rng(M + N + K + in_place)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    r = rng.standard_normal((M, N)).astype(np.float32)
+    xd, wd, bd = (torch.from_numpy(a).cuda() for a in (x, w, b))
+    xh, xl = _split(gbx, torch, xd)
+    wh, wl = _split(gbx, torch, wd)
+    full, y = _guarded(torch, M, N)
+    if in_place:
+        y.copy_(torch.from_numpy(r))
+        gbx.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=bd, resid=y)
+    else:
+        rd = torch.from_numpy(r).cuda()
+        gbx.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=bd, resid=rd)
+    torch.cuda.synchronize()
+    want, tol = _expected(x, w, b, r, 0)
+    _assert_within(y.cpu().numpy(), want, tol, "residual epilogue")
+    _check_guards(full)
+
+
+def test_linear_exact_operands_skip_terms(gbx, cuda):
+    """w decoded from f16 (exact in tf32) with w_lo = NULL, and x exact in
+    tf32 with x_lo = NULL: the dropped terms are zero, so the results match
+    the three-term product within the same bound."""
+    import torch
+    M, N, K = 200, 1000, 640
+    rng = np.random.default_rng(5)
+    x = _tf32_rna(rng.standard_normal((M, K)).astype(np.float32))
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float16).astype(np.float32)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    xh, xl = _split(gbx, torch, xd)
+    wh, wl = _split(gbx, torch, wd)
+    assert int(torch.count_nonzero(wl)) == 0 and int(torch.count_nonzero(xl)) == 0
+    want, tol = _expected(x, w, None, None, 0)
+    outs = []
+    for a, b in ((xl, wl), (None, wl), (xl, None), (None, None)):
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        gbx.linear(xh, a, wh, b, y, M=M, N=N, K=K)
+        outs.append(y)
+    torch.cuda.synchronize()
+    for y in outs:
+        _assert_within(y.cpu().numpy(), want, tol, "exact operands")
+    # the same products in the same order: identical bits
+    for y in outs[1:]:
+        assert torch.equal(y, outs[0])
+
+
+def test_linear_rows_independent_of_batch(gbx, cuda):
+    """Each row's sums run in the same order whatever M is (the forward's
+    batch-equals-single property)."""
+    import torch
+    N, K = 768, 768
+    rng = np.random.default_rng(9)
+    x = torch.from_numpy(rng.standard_normal((300, K)).astype(np.float32)).cuda()
+    w = torch.from_numpy((rng.standard_normal((N, K)) * 0.02).astype(np.float32)).cuda()
+    xh, xl = _split(gbx, torch, x)
+    wh, wl = _split(gbx, torch, w)
+    y_all = torch.empty((300, N), dtype=torch.float32, device="cuda")
+    gbx.linear(xh, xl, wh, wl, y_all, M=300, N=N, K=K)
+    y_one = torch.empty((1, N), dtype=torch.float32, device="cuda")
+    gbx.linear(xh[171:172].contiguous(), xl[171:172].contiguous(), wh, wl, y_one, M=1, N=N, K=K)
+    torch.cuda.synchronize()
+    assert torch.equal(y_all[171:172], y_one)
+
+
+def test_linear_rejects_bad_arguments(gbx, cuda):
+    import torch
+    x = torch.zeros((8, 8), dtype=torch.float32, device="cuda")
+    w = torch.zeros((8, 8), dtype=torch.float32, device="cuda")
+    y = torch.zeros((8, 8), dtype=torch.float32, device="cuda")
+    flat = torch.zeros(200, dtype=torch.float32, device="cuda")
+    for kw in (dict(K=6), dict(act=7), dict(M=-1)):
+        args = dict(M=8, N=8, K=8)
+        args.update(kw)
+        with pytest.raises(gbx.GbxError):
+            gbx.linear(x, None, w, None, y, **args)
+    with pytest.raises(gbx.GbxError):   # misaligned operand
+        gbx.linear(flat[1:], None, w, None, y, M=8, N=8, K=8)
+    with pytest.raises(gbx.GbxError):   # output aliases an operand
+        gbx.linear(x, None, w, None, x, M=8, N=8, K=8)
+
+
+def test_linear_kblock_32(cuda):
+    """The 128-byte-row variant (GBX_LINEAR_BK=32, two stages) on a few
+    shapes, in a fresh process (the setting is read once)."""
+    code = r"""
+import importlib, sys
+import numpy as np, torch
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
+gbx = importlib.import_module("glassboxai-transformer_b200")
+import test_linear_gpu as t
+for M, N, K in ((129, 257, 52), (300, 1600, 1600), (64, 768, 3072)):
+    rng = np.random.default_rng(M + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    r = rng.standard_normal((M, N)).astype(np.float32)
+    xd, wd, bd, rd = (torch.from_numpy(a).cuda() for a in (x, w, b, r))
+    xh, xl = t._split(gbx, torch, xd)
+    wh, wl = t._split(gbx, torch, wd)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    gbx.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=bd, resid=rd)
+    torch.cuda.synchronize()
+    want, tol = t._expected(x, w, b, r, 0)
+    t._assert_within(y.cpu().numpy(), want, tol, f"BK=32 {M}x{N}x{K}")
+print("ok")
+"""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, GBX_LINEAR_BK="32")
+    out = subprocess.run([sys.executable, "-c", code, root, os.path.join(root, "tests")], env=env,
+                         capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stdout + out.stderr

@@ -595,6 +595,8 @@ def run_kernel(args, shape):
         fn = lambda: G.embed(ids, wte, shape.table_dtype, wpe, shape.table_dtype, out, n_tok=R, d=d,
                              vocab=shape.vocab, n_ctx=shape.n_ctx, seq=seq, pos_off=shape.pos_off)
         nbytes = 4 * R + R * d * es + min(seq, shape.n_ctx) * d * es + 4 * R * d
+    elif name.startswith("linear_"):
+        return run_linear(args, shape, G, g, f32)
     else:
         raise SystemExit(f"unknown kernel {name}")
     for _ in range(args.warmup):
@@ -615,6 +617,85 @@ def run_kernel(args, shape):
                       "peak": peak, "peak_kind": kind}), flush=True)
 
 
+def load_tensor_peak():
+    """Dense tf32 tensor TFLOP/s: half the measured cuBLAS bf16 burst rate
+    (tf32 MMAs run at half the bf16 rate on sm_100)."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]) / 2, "half of measured bf16"
+    except Exception:
+        return 1590.0 / 2, "half of fallback bf16"
+
+
+LINEAR_KERNELS = {
+    # name: (N, K, epilogue) in units of the workload's d and ff
+    "linear_qkv": (lambda s: 3 * s.d, lambda s: s.d, "bias"),
+    "linear_proj": (lambda s: s.d, lambda s: s.d, "bias+resid"),
+    "linear_up": (lambda s: s.ff, lambda s: s.d, "bias+gelu, tf32-pair output"),
+    "linear_down": (lambda s: s.d, lambda s: s.ff, "bias+resid"),
+}
+
+
+def run_linear(args, shape, G, g, f32):
+    """One weight contraction of the workload's layer on --rows token rows:
+    gbx_linear (tcgen05, tf32 pairs, three product terms, fused epilogue)
+    against cuBLAS fp32 SGEMM (TF32 off) with torch's bias / GELU /
+    residual ops, each timed per launch with CUDA events."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    M = args.rows
+    nf, kf, epi = LINEAR_KERNELS[args.kernel]
+    N, K = nf(shape), kf(shape)
+    x = torch.randn((M, K), generator=g, **f32)
+    w = 0.02 * torch.randn((N, K), generator=g, **f32)
+    b = 0.02 * torch.randn((N,), generator=g, **f32)
+    r = torch.randn((M, N), generator=g, **f32) if "resid" in epi else None
+    xh, xl, wh, wl = (torch.empty_like(a) for a in (x, x, w, w))
+    G.split_tf32(x, xh, xl, n=x.numel())
+    G.split_tf32(w, wh, wl, n=w.numel())
+    y = torch.empty((M, N), **f32)
+    y_lo = torch.empty((M, N), **f32) if "gelu" in epi else None
+    err = torch.zeros(1, dtype=torch.int32, device=x.device)
+    act = G.ACT_GELU if "gelu" in epi else G.ACT_NONE
+    ours = lambda: G.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=b, resid=r, y_lo=y_lo, act=act,  # noqa: E731
+                            err_flag=err)
+    yr = torch.empty((M, N), **f32)
+
+    def cublas():
+        torch.addmm(b, x, w.t(), out=yr)
+        if "gelu" in epi:
+            torch.nn.functional.gelu(yr, approximate="tanh")
+        if r is not None:
+            yr.add_(r)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, e in evs:
+            a.record()
+            fn()
+            e.record()
+        torch.cuda.synchronize()
+        return statistics.median([1000.0 * a.elapsed_time(e) for a, e in evs])
+
+    us = timed(ours)
+    if int(err.item()) != 0:
+        raise SystemExit("gbx_linear reported a pipeline timeout")
+    sg = timed(cublas)
+    flop = 2.0 * M * N * K
+    peak, kind = load_tensor_peak()
+    terms = 3
+    print(json.dumps({"kernel": args.kernel, "workload": args.workload, "M": M, "N": N, "K": K, "epilogue": epi,
+                      "median_us": us, "tflops": flop / (us * 1e-6) / 1e12,
+                      "tensor_tflops": terms * flop / (us * 1e-6) / 1e12,
+                      "frac_of_tf32_peak": terms * flop / (us * 1e-6) / 1e12 / peak, "tf32_peak": peak,
+                      "peak_kind": kind, "cublas_sgemm_us": sg, "cublas_sgemm_tflops": flop / (sg * 1e-6) / 1e12,
+                      "speedup_vs_sgemm": sg / us}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -625,7 +706,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--kernel", choices=["embed", "layernorm", "residual_layernorm", "softmax_rows", "attn_softmax_rows",
-                                         "bias_gelu"],
+                                         "bias_gelu"] + sorted(LINEAR_KERNELS),
                     help="time one kernel alone on --rows rows of the workload's shape")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--graph", action="store_true",

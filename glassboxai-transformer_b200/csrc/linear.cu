@@ -4,22 +4,33 @@
 // replacing the GEMVs computeQKVKernel, projectionKernel, ffnUpKernel and
 // ffnDownKernel (transformer.cu:187-294).  The reference computes these in
 // fp32 on the CUDA cores; here every operand arrives as a tf32 pair
-// (hi, lo) and the tensor cores form hi.hi + hi.lo + lo.hi with f32
-// accumulation, which keeps each product within ~2^-21 of fp32's.
+// (hi, lo) and the tensor cores form hi.hi + hi.lo + lo.hi.
+//
+// Accuracy.  The pair products are within ~2^-22 of the fp32 products, but
+// the tensor core's f32 accumulator loses low-order bits on every addition
+// (measured on B200, RMS error over sum |x w|: with the whole K sum in TMEM
+// 3e-7 at K = 768 to 9e-7 at K = 6400, 10-30x an fp32 SGEMM's 2.8e-8, and
+// growing with K).  So TMEM only ever holds the partial sum of one K chunk
+// of kLinChunkK, and the epilogue warps add each chunk into fp32 registers
+// (round to nearest).  At 128 the RMS error is 5.5e-8 / 2.8e-8 / 1.9e-8 at
+// K = 768 / 3072 / 6400, fp32-grade; 64 halves it and costs 5% more time,
+// 256 doubles it and saves 5%.
 //
 // Kernel layout (one CTA per SM, persistent over 128 x 256 output tiles):
 //   warp 0      TMA producer: per K block, the x_hi, x_lo, w_hi, w_lo tiles
 //               (K-major, 64- or 128-byte swizzled rows) into a ring of
 //               shared-memory stages, completion counted on full[stage]
-//   warp 1      owns the 512 TMEM columns (two 128 x 256 f32 accumulators);
-//               one thread issues tcgen05.mma (kind::tf32, M 128, N 256,
-//               K 8) per product term and K step, and tcgen05.commit frees a
-//               stage (empty[stage]) or hands an accumulator to the epilogue
-//               (acc_full)
-//   warps 2-5   epilogue: tcgen05.ld 16 columns of a row at a time, + bias,
-//               GELU, + resid, optional tf32 split, 16-byte stores; then
-//               acc_empty lets the MMA thread reuse the accumulator, so one
-//               tile's epilogue overlaps the next tile's MMAs
+//   warp 1      owns the 512 TMEM columns (two 128 x 256 f32 chunk
+//               buffers); one thread issues tcgen05.mma (kind::tf32, M 128,
+//               N 256, K 8) per product term and K step; tcgen05.commit
+//               frees a stage (empty[stage]) or hands a finished chunk to the
+//               epilogue (chunk_full[buffer])
+//   warps 2-9   epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (one
+//               output row per thread) and columns 128 ((w - 2) / 4) .. +127;
+//               per chunk, tcgen05.ld and add into 128 fp32 registers, then
+//               chunk_empty lets the MMA thread refill the buffer (so the
+//               next chunk's MMAs overlap this chunk's read-out); per tile,
+//               + bias, GELU, + resid, optional tf32 split, 16-byte stores
 // Every mbarrier wait is bounded (1 s, %globaltimer): a wait that runs out
 // sets the CTA's abort word, every role leaves its loop, the producer waits
 // (bounded) for its loads in flight, the MMA thread for its MMAs, TMEM is
@@ -36,12 +47,18 @@
 
 namespace gbx {
 
-constexpr int kLinBM = 128;        // tile rows = TMEM lanes
-constexpr int kLinBN = 256;        // tile columns = TMEM columns of one accumulator
-constexpr int kLinThreads = 192;   // 6 warps
-constexpr int kLinAccums = 2;      // 2 x 256 = all 512 TMEM columns
-constexpr int kLinTmemCols = kLinAccums * kLinBN;
-constexpr int kLinEpiThreads = 128;
+constexpr int kLinBM = 128;           // tile rows = TMEM lanes
+constexpr int kLinBN = 256;           // tile columns = TMEM columns of one chunk buffer
+constexpr int kLinEpiWarps = 8;       // two per TMEM lane quarter, 128 columns each
+constexpr int kLinEpiThreads = 32 * kLinEpiWarps;
+constexpr int kLinThreads = 64 + kLinEpiThreads;
+constexpr int kLinEpiCols = kLinBN / 2;
+constexpr int kLinBuffers = 2;        // 2 x 256 = all 512 TMEM columns
+constexpr int kLinTmemCols = kLinBuffers * kLinBN;
+#ifndef GBX_LINEAR_CHUNK_K
+#define GBX_LINEAR_CHUNK_K 128
+#endif
+constexpr int kLinChunkK = GBX_LINEAR_CHUNK_K;   // K elements summed in TMEM before each fp32 promotion
 constexpr uint64_t kLinWaitNs = 1000000000ull;
 
 template <int BK>
@@ -52,7 +69,9 @@ struct LinCfg {
     static constexpr int stage_bytes = 2 * a_bytes + 2 * b_bytes;
     static constexpr int stages = (196 * 1024) / stage_bytes;   // BK 16: 4, BK 32: 2
     static constexpr int ksteps = BK / 8;                       // tf32 MMA K = 8 (32 bytes)
-    static constexpr int nbars = 2 * stages + 2 * kLinAccums + 1;
+    static constexpr int chunk_blocks = kLinChunkK / BK;          // K blocks per chunk
+    static_assert(kLinChunkK % 32 == 0, "a chunk is whole K blocks");
+    static constexpr int nbars = 2 * stages + 2 * kLinBuffers + 1;
     static constexpr size_t smem = (size_t)stages * stage_bytes + 1024 + 8 * nbars + 16;
     static_assert(BK == 16 || BK == 32, "swizzle width");
     static_assert(stages >= 2, "pipeline depth");
@@ -68,6 +87,7 @@ struct LinearArgs {
     int64_t M;
     int N;
     int K;
+    int m_blocks;
     int n_blocks;
     int k_blocks;
     int tiles;
@@ -75,6 +95,17 @@ struct LinearArgs {
     int has_xlo;
     int has_wlo;
 };
+
+// Tile t -> (row tile, column tile): consecutive tiles sweep the column
+// tiles of one row tile, so the CTAs in flight share a few rows of x (read
+// from HBM once) and the weight matrix, which L2 largely holds.  (Grouping
+// 8-32 row tiles per column tile measured no faster on B200: the kernel is
+// bound by shared-memory traffic, not by L2 misses.)
+__device__ __forceinline__ void tile_coords(int t, const LinearArgs& a, int& mb, int& nb)
+{
+    mb = t / a.n_blocks;
+    nb = t - mb * a.n_blocks;
+}
 
 __device__ __forceinline__ void split_value(float x, float& hi, float& lo)
 {
@@ -155,24 +186,25 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::stages * C::stage_bytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::nbars);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    const uint32_t full0 = tc::smem_u32(bars);                     // full[s]      = full0 + 8 s
+    const uint32_t full0 = tc::smem_u32(bars);                     // full[s]        = full0 + 8 s
     const uint32_t empty0 = full0 + 8 * C::stages;                 // empty[s]
-    const uint32_t accf0 = empty0 + 8 * C::stages;                 // acc_full[b]
-    const uint32_t acce0 = accf0 + 8 * kLinAccums;                 // acc_empty[b]
-    const uint32_t drain = acce0 + 8 * kLinAccums;
+    const uint32_t cfull0 = empty0 + 8 * C::stages;                // chunk_full[b]
+    const uint32_t cempty0 = cfull0 + 8 * kLinBuffers;             // chunk_empty[b]
+    const uint32_t drain = cempty0 + 8 * kLinBuffers;
     const uint32_t smem0 = tc::smem_u32(smem);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int chunks = (a.k_blocks + C::chunk_blocks - 1) / C::chunk_blocks;   // per tile
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::stages; ++s) {
             tc::mbar_init(full0 + 8 * s, 1);
             tc::mbar_init(empty0 + 8 * s, 1);
         }
-        for (int b = 0; b < kLinAccums; ++b) {
-            tc::mbar_init(accf0 + 8 * b, 1);
-            tc::mbar_init(acce0 + 8 * b, kLinEpiThreads);
+        for (int b = 0; b < kLinBuffers; ++b) {
+            tc::mbar_init(cfull0 + 8 * b, 1);
+            tc::mbar_init(cempty0 + 8 * b, kLinEpiThreads);
         }
         tc::mbar_init(drain, 1);
         *abort = 0;
@@ -200,8 +232,10 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
             uint32_t issued = 0;    // bit s: stage s has had a load issued
             uint32_t lastpar = 0;   // bit s: parity of the phase of its last load
             for (int t = blockIdx.x; t < a.tiles && !*abort; t += gridDim.x) {
-                const int y_x = (t / a.n_blocks) * kLinBM;
-                const int y_w = (t % a.n_blocks) * kLinBN;
+                int mb, nb;
+                tile_coords(t, a, mb, nb);
+                const int y_x = mb * kLinBM;
+                const int y_w = nb * kLinBN;
                 for (int kb = 0; kb < a.k_blocks; ++kb) {
                     if (!tc::mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kLinWaitNs)) break;
                     const uint32_t full = full0 + 8 * stage;
@@ -227,46 +261,59 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------------------------------------------- MMA issuer
-            constexpr uint32_t idesc = tc::idesc_tf32(kLinBM, kLinBN);
             int stage = 0;
             uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
+            int buf = 0;
+            uint32_t buf_phase = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
-                if (!tc::mbar_wait(acce0 + 8 * acc, acc_phase ^ 1, abort, kLinWaitNs)) break;
-                tc::fence_after_sync();
-                const uint32_t d = tmem + acc * kLinBN;
-                for (int kb = 0; kb < a.k_blocks; ++kb) {
-                    if (!tc::mbar_wait(full0 + 8 * stage, phase, abort, kLinWaitNs)) {
+                // the last column tile runs only as wide as N needs (a multiple of 16)
+                int mb, nb;
+                tile_coords(t, a, mb, nb);
+                const int n_left = a.N - nb * kLinBN;
+                const int n_mma = n_left >= kLinBN ? kLinBN : (n_left + 15) & ~15;
+                const uint32_t idesc = tc::idesc_tf32(kLinBM, n_mma);
+                for (int c = 0; c < chunks && ok; ++c) {
+                    if (!tc::mbar_wait(cempty0 + 8 * buf, buf_phase ^ 1, abort, kLinWaitNs)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const uint32_t base = smem0 + stage * C::stage_bytes;
+                    const uint32_t d = tmem + buf * kLinBN;
+                    const int kb0 = c * C::chunk_blocks;
+                    const int kb1 = kb0 + C::chunk_blocks < a.k_blocks ? kb0 + C::chunk_blocks : a.k_blocks;
+                    for (int kb = kb0; kb < kb1; ++kb) {
+                        if (!tc::mbar_wait(full0 + 8 * stage, phase, abort, kLinWaitNs)) {
+                            ok = false;
+                            break;
+                        }
+                        tc::fence_after_sync();
+                        const uint32_t base = smem0 + stage * C::stage_bytes;
 #pragma unroll
-                    for (int ks = 0; ks < C::ksteps; ++ks) {
-                        const uint32_t off = ks * 32;
-                        const uint64_t xh = tc::smem_desc(base + off, C::row_bytes);
-                        const uint64_t wh = tc::smem_desc(base + 2 * C::a_bytes + off, C::row_bytes);
-                        tc::mma_tf32(d, xh, wh, idesc, (kb | ks) != 0);
-                        if (a.has_wlo)
-                            tc::mma_tf32(d, xh, tc::smem_desc(base + 2 * C::a_bytes + C::b_bytes + off, C::row_bytes),
-                                         idesc, 1);
-                        if (a.has_xlo)
-                            tc::mma_tf32(d, tc::smem_desc(base + C::a_bytes + off, C::row_bytes), wh, idesc, 1);
+                        for (int ks = 0; ks < C::ksteps; ++ks) {
+                            const uint32_t off = ks * 32;
+                            const uint64_t xh = tc::smem_desc(base + off, C::row_bytes);
+                            const uint64_t wh = tc::smem_desc(base + 2 * C::a_bytes + off, C::row_bytes);
+                            tc::mma_tf32(d, xh, wh, idesc, (kb != kb0) | (ks != 0));
+                            if (a.has_wlo)
+                                tc::mma_tf32(d, xh,
+                                             tc::smem_desc(base + 2 * C::a_bytes + C::b_bytes + off, C::row_bytes),
+                                             idesc, 1);
+                            if (a.has_xlo)
+                                tc::mma_tf32(d, tc::smem_desc(base + C::a_bytes + off, C::row_bytes), wh, idesc, 1);
+                        }
+                        tc::mma_commit(empty0 + 8 * stage);   // the stage is free once these MMAs are done
+                        if (++stage == C::stages) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
                     }
-                    tc::mma_commit(empty0 + 8 * stage);   // the stage is free once these MMAs are done
-                    if (++stage == C::stages) {
-                        stage = 0;
-                        phase ^= 1;
+                    if (!ok) break;
+                    tc::mma_commit(cfull0 + 8 * buf);   // chunk complete
+                    if (++buf == kLinBuffers) {
+                        buf = 0;
+                        buf_phase ^= 1;
                     }
-                }
-                if (!ok) break;
-                tc::mma_commit(accf0 + 8 * acc);   // accumulator complete
-                if (++acc == kLinAccums) {
-                    acc = 0;
-                    acc_phase ^= 1;
                 }
             }
             // every MMA issued has completed before TMEM is freed
@@ -276,30 +323,57 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
     } else {
         // -------------------------------------------------------- epilogue
         const int quarter = warp & 3;   // the TMEM lanes this warp may read
+        const int col0 = ((warp - 2) >> 2) * kLinEpiCols;
         const int row_in_tile = 32 * quarter + lane;
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        for (int t = blockIdx.x; t < a.tiles; t += gridDim.x) {
-            // warp-uniform outcome: tcgen05.ld below needs the whole warp
-            const bool ready = tc::mbar_wait(accf0 + 8 * acc, acc_phase, abort, kLinWaitNs);
-            if (!__all_sync(0xffffffffu, ready)) break;
-            tc::fence_after_sync();
-            const int64_t row = (int64_t)(t / a.n_blocks) * kLinBM + row_in_tile;
-            const int n0 = (t % a.n_blocks) * kLinBN;
-            const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + acc * kLinBN;
-            for (int c = 0; c < kLinBN / 16; ++c) {
-                const int n = n0 + 16 * c;
-                if (n >= a.N) break;   // uniform over the warp
-                float v[16];
-                tc::tmem_ld16(tbase + 16 * c, v);
-                tc::tmem_ld_wait();
-                if (row < a.M) epi_store16<VEC>(v, row, n, a);
+        int buf = 0;
+        uint32_t buf_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
+            int mb, nb;
+            tile_coords(t, a, mb, nb);
+            float acc[kLinEpiCols];
+#pragma unroll
+            for (int j = 0; j < kLinEpiCols; ++j) acc[j] = 0.0f;
+            for (int c = 0; c < chunks; ++c) {
+                // warp-uniform outcome: tcgen05.ld below needs the whole warp
+                const bool ready = tc::mbar_wait(cfull0 + 8 * buf, buf_phase, abort, kLinWaitNs);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + buf * kLinBN + col0;
+                const int n_left = a.N - nb * kLinBN - col0;   // columns of this warp below N
+#pragma unroll
+                for (int g = 0; g < kLinEpiCols / 32; ++g) {
+                    if (32 * g < n_left) {   // uniform over the warp
+                        float v[32];
+                        tc::tmem_ld32(tbase + 32 * g, v);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) acc[32 * g + i] += v[i];
+                    }
+                }
+                tc::fence_before_sync();
+                tc::mbar_arrive(cempty0 + 8 * buf);
+                if (++buf == kLinBuffers) {
+                    buf = 0;
+                    buf_phase ^= 1;
+                }
             }
-            tc::fence_before_sync();
-            tc::mbar_arrive(acce0 + 8 * acc);
-            if (++acc == kLinAccums) {
-                acc = 0;
-                acc_phase ^= 1;
+            if (!ok) break;
+            const int64_t row = (int64_t)mb * kLinBM + row_in_tile;
+            const int n0 = nb * kLinBN + col0;
+            if (row < a.M) {
+#pragma unroll
+                for (int g = 0; g < kLinEpiCols / 16; ++g) {
+                    if (n0 + 16 * g < a.N) {
+                        float v[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) v[i] = acc[16 * g + i];
+                        epi_store16<VEC>(v, row, n0 + 16 * g, a);
+                    }
+                }
             }
         }
     }
@@ -311,6 +385,37 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
         tc::tmem_dealloc(tmem, kLinTmemCols);
     }
     if (threadIdx.x == 0 && *abort && a.err) atomicOr(a.err, GBX_LINEAR_TIMEOUT);
+}
+
+// General path (K not a multiple of 4, or operands off 16-byte alignment):
+// one thread per output on the CUDA cores, the same three product terms
+// with fp32 FMAs, the same epilogue.
+__global__ void __launch_bounds__(256)
+linear_general_kernel(const float* __restrict__ xh, const float* __restrict__ xl, const float* __restrict__ wh,
+                      const float* __restrict__ wl, const LinearArgs a)
+{
+    const int64_t total = a.M * a.N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / a.N;
+        const int n = (int)(i - m * a.N);
+        const float* xr = xh + m * a.K;
+        const float* wr = wh + (int64_t)n * a.K;
+        float acc = 0.0f;
+        for (int k = 0; k < a.K; ++k) {
+            acc = fmaf(xr[k], wr[k], acc);
+            if (wl) acc = fmaf(xr[k], wl[(int64_t)n * a.K + k], acc);
+            if (xl) acc = fmaf(xl[m * a.K + k], wr[k], acc);
+        }
+        const float o = epi_value(acc, n, m, a);
+        if (a.y_lo) {
+            float h, l;
+            split_value(o, h, l);
+            a.y[i] = h;
+            a.y_lo[i] = l;
+        } else {
+            a.y[i] = o;
+        }
+    }
 }
 
 // ------------------------------------------------------------------ split
@@ -451,9 +556,6 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     if (M == 0) return GBX_OK;
     if (!x_hi || !w_hi || !y) return set_error(GBX_EINVAL, "gbx_linear: null pointer");
     if (act != GBX_ACT_NONE && act != GBX_ACT_GELU) return set_error(GBX_EINVAL, "gbx_linear: act=%d", act);
-    if (K % 4 != 0) return set_error(GBX_EINVAL, "gbx_linear: K=%d is not a multiple of 4", K);
-    if (!aligned16(x_hi) || !aligned16(w_hi) || (x_lo && !aligned16(x_lo)) || (w_lo && !aligned16(w_lo)))
-        return set_error(GBX_EINVAL, "gbx_linear: x and w must be 16-byte aligned");
     if (y_lo == y || (const float*)y == x_hi || (const float*)y == w_hi || (x_lo && (const float*)y == x_lo) ||
         (w_lo && (const float*)y == w_lo))
         return set_error(GBX_EINVAL, "gbx_linear: y aliases an operand");
@@ -471,6 +573,7 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     a.M = M;
     a.N = N;
     a.K = K;
+    a.m_blocks = (int)m_blocks;
     a.n_blocks = (int)n_blocks;
     a.tiles = (int)(m_blocks * n_blocks);
     a.act = act;
@@ -479,6 +582,14 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     const bool vec = N % 4 == 0 && aligned16(y) && (!y_lo || aligned16(y_lo)) && (!resid || aligned16(resid)) &&
                      (!bias || aligned16(bias));
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const bool tma_ok = K % 4 == 0 && aligned16(x_hi) && aligned16(w_hi) && (!x_lo || aligned16(x_lo)) &&
+                        (!w_lo || aligned16(w_lo));
+    if (!tma_ok) {
+        const int grid = persistent_grid(linear_general_kernel, 256, 0, (M * N + 255) / 256, 8);
+        if (grid < 1) return GBX_ECUDA;
+        linear_general_kernel<<<grid, 256, 0, s>>>(x_hi, x_lo, w_hi, w_lo, a);
+        return check_launch("gbx_linear");
+    }
     if (linear_bk() == 32) {
         a.k_blocks = (K + 31) / 32;
         return vec ? launch_linear<32, true>(x_hi, x_lo, w_hi, w_lo, a, s)

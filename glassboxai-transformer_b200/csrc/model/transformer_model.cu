@@ -7,32 +7,33 @@
 //
 //   gbx_embed                              h = wte[ids] + wpe[pos]          (:805-815)
 //   for each layer l:
-//     gbx_layernorm / gbx_residual_layernorm
-//                                          ln = LN1(h)   (l = 0)
-//                                          h += down + b_down(l-1); ln = LN1(h)   (l > 0: the
-//                                          residual of :874-878 fused with the LN of :868)
-//     cuBLAS                               qkv = ln . Wqkv^T + b_qkv       (:830-832)
+//     gbx_layernorm, gbx_split_tf32        ln = LN1(h), as a tf32 pair     (:827-828)
+//     gbx_linear                           qkv = ln . Wqkv^T + b_qkv       (:830-832)
 //     cuBLAS (per sequence, batched over heads)
 //                                          raw[h] = Q_h . K_h^T            (:834-837, without
 //                                                                          the scale and mask)
 //     gbx_attn_softmax_rows                P = softmax(mask(raw / sqrt(hd)))  (:220-229, :839-842)
 //     cuBLAS (per sequence, batched over heads)
 //                                          attn_h = P_h . V_h              (:844-846)
-//     cuBLAS                               proj = attn . Wproj^T           (:848-850, bias below)
-//     gbx_residual_layernorm               h += proj + b_proj; ln = LN2(h) (:850-852 fused with :868)
-//     cuBLAS                               up = ln . Wup^T                 (:870-872, bias below)
-//     gbx_bias_gelu                        up = GELU(up + b_up)            (:272, 276-277)
-//     cuBLAS                               down = up . Wdown^T             (:874-876, bias and
-//                                                                          residual deferred)
-//   gbx_residual_layernorm on each sequence's last row
-//                                          last = LN_f(h + down + b_down)  (:890-896)
+//     gbx_split_tf32, gbx_linear           h += attn . Wproj^T + b_proj    (:848-852, the
+//                                                                          residual in the epilogue)
+//     gbx_layernorm, gbx_split_tf32        ln = LN2(h)                     (:866-868)
+//     gbx_linear                           up = GELU(ln . Wup^T + b_up), as a tf32 pair
+//                                                                          (:870-872)
+//     gbx_linear                           h += up . Wdown^T + b_down      (:874-878)
+//   gbx_layernorm on each sequence's last row
+//                                          last = LN_f(h)                  (:890-896)
 //   gbx_logits                             logits = last . wte^T           (:898-900)
 //   (nextToken) gbx_select_tokens          argmax / temperature sampling   (:994-1028)
 //
-// The GEMMs are fp32 cuBLAS (CUBLAS_COMPUTE_32F, no TF32), the reference's
-// precision; their outputs differ from the reference's sequential GEMV sums
-// in summation order only.  Activation buffers grow to the largest call
-// (like allocateBuffers, :770-787) and are reused.
+// The weight contractions run on the tcgen05 tensor cores (gbx_linear) with
+// every operand as a tf32 pair: each product within ~2^-21 of fp32's, fp32
+// sums, so they differ from the reference's sequential GEMV sums by rounding
+// of the same order as a change of summation order.  Weights are split once
+// at load; a weight read from an f16 or bf16 tensor is exact in tf32 and
+// needs no low part.  The per-head attention products are fp32 cuBLAS
+// (CUBLAS_COMPUTE_32F, no TF32).  Activation buffers grow to the largest
+// call (like allocateBuffers, :770-787) and are reused.
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -46,20 +47,6 @@
 namespace gbx {
 
 namespace {
-
-// dst[r * ld + c] = src[c] for r < rows, c < cols (QKV bias seeds the GEMM
-// accumulator, as the reference seeds its sum with the bias, :195-197).
-__global__ void broadcast_rows_kernel(float* __restrict__ dst, int64_t ld, const float* __restrict__ src,
-                                      int64_t rows, int cols)
-{
-    const int64_t total = rows * cols;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / cols;
-        const int c = (int)(i - r * cols);
-        dst[r * ld + c] = src[c];
-    }
-}
 
 struct DevBuf {
     float* p = nullptr;
@@ -91,8 +78,8 @@ struct TransformerModel::Impl {
     cublasHandle_t blas = nullptr;
     cudaStream_t stream = nullptr;
     int device = -1;
-    // activations
-    DevBuf h, ln, qkv, scores, attn, proj, up, down, last_h, last_x, last_y, logits;
+    // activations (ln, attn and up hold the hi half of a tf32 pair, *_lo the low half)
+    DevBuf h, ln, ln_lo, qkv, scores, attn, attn_lo, up, up_lo, last_h, last_y, logits;
     int32_t* ids = nullptr;
     size_t ids_n = 0;
     int32_t* err = nullptr;
@@ -106,14 +93,27 @@ struct TransformerModel::Impl {
             *down_b;
     };
     std::vector<Layer> layers;
+    // tf32 pairs of the four weight matrices per layer: hi is the loader's
+    // fp32 tensor itself when that is exact in tf32 (decoded from f16 or
+    // bf16; lo NULL), else a split copy owned here
+    struct Pair {
+        const float* hi = nullptr;
+        const float* lo = nullptr;
+    };
+    struct LayerW {
+        Pair qkv, proj, up, down;
+    };
+    std::vector<LayerW> wpairs;
+    std::vector<float*> owned;
     const float *lnf_g = nullptr, *lnf_b = nullptr;
     const void *wte = nullptr, *wpe = nullptr;
     int wte_dt = 0, wpe_dt = 0;
 
     ~Impl()
     {
-        for (DevBuf* b : {&h, &ln, &qkv, &scores, &attn, &proj, &up, &down, &last_h, &last_x, &last_y, &logits})
+        for (DevBuf* b : {&h, &ln, &ln_lo, &qkv, &scores, &attn, &attn_lo, &up, &up_lo, &last_h, &last_y, &logits})
             b->release();
+        for (float* p : owned) cudaFree(p);
         if (ids) cudaFree(ids);
         if (err) cudaFree(err);
         if (sel_ids) cudaFree(sel_ids);
@@ -197,6 +197,37 @@ bool TransformerModel::loadModel(const std::string& ggufPath)
             !(L.down_b = get(pre + "ffn_down.bias", d)))
             return false;
     }
+    // tf32 pairs of the weight matrices
+    auto pair = [&](const std::string& name, const float* w, int64_t n, Impl::Pair* out) -> bool {
+        const GGUFTensor* t = loader_.findTensor({name});
+        if (t->dtype == GBX_DT_F16 || t->dtype == GBX_DT_BF16) {
+            out->hi = w;   // at most 11 significant bits: exact in tf32
+            out->lo = nullptr;
+            return true;
+        }
+        float *hi = nullptr, *lo = nullptr;
+        if (cudaMalloc(&hi, n * sizeof(float)) != cudaSuccess) return fail("cudaMalloc of weight pairs failed");
+        m.owned.push_back(hi);
+        if (cudaMalloc(&lo, n * sizeof(float)) != cudaSuccess) return fail("cudaMalloc of weight pairs failed");
+        m.owned.push_back(lo);
+        if (gbx_split_tf32(w, hi, lo, n, reinterpret_cast<gbx_stream_t>(m.stream)) != GBX_OK)
+            return fail(std::string("weight split: ") + gbx_last_error());
+        out->hi = hi;
+        out->lo = lo;
+        return true;
+    };
+    m.wpairs.resize(numLayers_);
+    for (int l = 0; l < numLayers_; ++l) {
+        const std::string pre = "blk." + std::to_string(l) + ".";
+        const Impl::Layer& L = m.layers[l];
+        Impl::LayerW& W = m.wpairs[l];
+        if (!pair(pre + "attn_qkv.weight", L.qkv_w, 3 * d * d, &W.qkv) ||
+            !pair(pre + "attn_output.weight", L.proj_w, d * d, &W.proj) ||
+            !pair(pre + "ffn_up.weight", L.up_w, F * d, &W.up) || !pair(pre + "ffn_down.weight", L.down_w, d * F, &W.down))
+            return false;
+    }
+    if (cudaStreamSynchronize(m.stream) != cudaSuccess) return fail("weight split failed");
+
     const GGUFTensor* g = loader_.findTensor({"output_norm.weight", "ln_f.weight"});
     const GGUFTensor* b = loader_.findTensor({"output_norm.bias", "ln_f.bias"});
     if (!g || !b) return fail("missing output_norm / ln_f");
@@ -208,10 +239,10 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
 {
     Impl& m = *impl_;
     const int64_t d = embedDim_, F = ffnDim_, B = tokens / seq;
-    const bool ok = m.h.ensure(tokens * d) && m.ln.ensure(tokens * d) && m.qkv.ensure(tokens * 3 * d) &&
-                    m.scores.ensure((size_t)numHeads_ * seq * seq) && m.attn.ensure(tokens * d) &&
-                    m.proj.ensure(tokens * d) && m.up.ensure(tokens * F) && m.down.ensure(tokens * d) &&
-                    m.last_h.ensure(B * d) && m.last_x.ensure(B * d) && m.last_y.ensure(B * d) &&
+    const bool ok = m.h.ensure(tokens * d) && m.ln.ensure(tokens * d) && m.ln_lo.ensure(tokens * d) &&
+                    m.qkv.ensure(tokens * 3 * d) && m.scores.ensure((size_t)numHeads_ * seq * seq) &&
+                    m.attn.ensure(tokens * d) && m.attn_lo.ensure(tokens * d) && m.up.ensure(tokens * F) &&
+                    m.up_lo.ensure(tokens * F) && m.last_h.ensure(B * d) && m.last_y.ensure(B * d) &&
                     m.logits.ensure((size_t)B * vocab_);
     if (!ok) return fail("cudaMalloc of activation buffers failed");
     if ((size_t)tokens > m.ids_n) {
@@ -317,11 +348,10 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
     auto blas = [&](cublasStatus_t s) {
         if (s != CUBLAS_STATUS_SUCCESS) blas_ok = false;
     };
-    // row-major Y[M, Nout] (ld ldy) = X[M, K] (ld ldx) . W[Nout, K]^T (ld K)
-    auto linear = [&](const float* X, int64_t ldx, const float* W, float* Y, int64_t ldy, int64_t M, int Nout, int K,
-                      float beta) {
-        blas(cublasSgemm(m.blas, CUBLAS_OP_T, CUBLAS_OP_N, Nout, (int)M, K, &one, W, K, X, (int)ldx, &beta, Y,
-                         (int)ldy));
+    // y[M, Nout] = act(x . W^T + bias) + resid on the tensor cores, x and W as tf32 pairs
+    auto linear = [&](const float* xh, const float* xl, const Impl::Pair& W, const float* bias, const float* resid,
+                      float* y, float* y_lo, int64_t M, int Nout, int K, int act) {
+        check(gbx_linear(xh, xl, W.hi, W.lo, bias, resid, y, y_lo, M, Nout, K, act, m.err, gs));
     };
 
     if (cudaMemcpyAsync(m.ids, tokenIDs.data(), N * sizeof(int32_t), cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -332,19 +362,10 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
     const float scale = sqrtf((float)hd);   // transformer.cu:836
     for (int l = 0; l < numLayers_ && rc == GBX_OK && blas_ok; ++l) {
         const Impl::Layer& L = m.layers[l];
-        if (l == 0)
-            check(gbx_layernorm(m.h.p, m.ln.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
-        else
-            check(gbx_residual_layernorm(m.down.p, m.h.p, m.layers[l - 1].down_b, m.h.p, m.ln.p, L.ln1_g, L.ln1_b, N,
-                                         d, 1e-5f, gs));
-        // qkv = b_qkv + ln . Wqkv^T
-        {
-            const int64_t total = N * 3 * d;
-            const int grid = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-            broadcast_rows_kernel<<<grid, 256, 0, st>>>(m.qkv.p, 3 * d, L.qkv_b, N, 3 * d);
-            if (cudaGetLastError() != cudaSuccess) check(GBX_ECUDA);
-        }
-        linear(m.ln.p, d, L.qkv_w, m.qkv.p, 3 * d, N, 3 * d, d, 1.0f);
+        const Impl::LayerW& W = m.wpairs[l];
+        check(gbx_layernorm(m.h.p, m.ln.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
+        check(gbx_split_tf32(m.ln.p, m.ln.p, m.ln_lo.p, N * d, gs));
+        linear(m.ln.p, m.ln_lo.p, W.qkv, L.qkv_b, nullptr, m.qkv.p, nullptr, N, 3 * d, d, GBX_ACT_NONE);
         for (int b = 0; b < batch; ++b) {
             const float* q = m.qkv.p + (int64_t)b * S * 3 * d;
             const float* k = q + d;
@@ -357,28 +378,21 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
             blas(cublasSgemmStridedBatched(m.blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, S, S, &one, v, 3 * d, hd, m.scores.p,
                                            S, (int64_t)S * S, &zero, m.attn.p + (int64_t)b * S * d, d, hd, H));
         }
-        linear(m.attn.p, d, L.proj_w, m.proj.p, d, N, d, d, 0.0f);
-        check(gbx_residual_layernorm(m.proj.p, m.h.p, L.proj_b, m.h.p, m.ln.p, L.ln2_g, L.ln2_b, N, d, 1e-5f, gs));
-        linear(m.ln.p, d, L.up_w, m.up.p, F, N, F, d, 0.0f);
-        check(gbx_bias_gelu(m.up.p, m.up.p, L.up_b, N, F, gs));
-        linear(m.up.p, F, L.down_w, m.down.p, d, N, d, F, 0.0f);
+        check(gbx_split_tf32(m.attn.p, m.attn.p, m.attn_lo.p, N * d, gs));
+        linear(m.attn.p, m.attn_lo.p, W.proj, L.proj_b, m.h.p, m.h.p, nullptr, N, d, d, GBX_ACT_NONE);
+        check(gbx_layernorm(m.h.p, m.ln.p, L.ln2_g, L.ln2_b, N, d, 1e-5f, gs));
+        check(gbx_split_tf32(m.ln.p, m.ln.p, m.ln_lo.p, N * d, gs));
+        linear(m.ln.p, m.ln_lo.p, W.up, L.up_b, nullptr, m.up.p, m.up_lo.p, N, F, d, GBX_ACT_GELU);
+        linear(m.up.p, m.up_lo.p, W.down, L.down_b, m.h.p, m.h.p, nullptr, N, d, F, GBX_ACT_NONE);
     }
     if (rc == GBX_OK && blas_ok) {
-        // each sequence's last row: h + (down + b_down), then ln_f
+        // each sequence's last row of h, then ln_f
         const size_t pitch = (size_t)S * d * sizeof(float);
         const size_t row = (size_t)d * sizeof(float);
         if (cudaMemcpy2DAsync(m.last_h.p, row, m.h.p + (int64_t)(S - 1) * d, pitch, row, batch,
                               cudaMemcpyDeviceToDevice, st) != cudaSuccess)
             check(GBX_ECUDA);
-        if (numLayers_ > 0) {
-            if (cudaMemcpy2DAsync(m.last_x.p, row, m.down.p + (int64_t)(S - 1) * d, pitch, row, batch,
-                                  cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-                check(GBX_ECUDA);
-            check(gbx_residual_layernorm(m.last_x.p, m.last_h.p, m.layers[numLayers_ - 1].down_b, nullptr, m.last_y.p,
-                                         m.lnf_g, m.lnf_b, batch, d, 1e-5f, gs));
-        } else {
-            check(gbx_layernorm(m.last_h.p, m.last_y.p, m.lnf_g, m.lnf_b, batch, d, 1e-5f, gs));
-        }
+        check(gbx_layernorm(m.last_h.p, m.last_y.p, m.lnf_g, m.lnf_b, batch, d, 1e-5f, gs));
         check(gbx_logits(m.last_y.p, batch, m.wte, m.wte_dt, m.logits.p, V, d, gs));
     }
     int32_t err_host = 0;
@@ -388,6 +402,7 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
     if (cudaStreamSynchronize(st) != cudaSuccess && rc == GBX_OK) rc = GBX_ECUDA;
     if (!blas_ok) return fail("cuBLAS call failed");
     if (rc != GBX_OK) return fail(std::string(gbx_status_string(rc)) + ": " + gbx_last_error());
+    if (err_host & GBX_LINEAR_TIMEOUT) return fail("a tensor-core contraction timed out (its output is incomplete)");
     if (err_host) return fail("embedding reported out-of-range ids or positions");
     return true;
 }

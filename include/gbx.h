@@ -231,8 +231,10 @@ int gbx_split_tf32(const float* x, float* hi, float* lo, int64_t n, gbx_stream_t
  *                receive its tf32 pair (gbx_split_tf32 of it), ready to be
  *                the x operand of the next gbx_linear
  *   err_flag     device int32 (may be NULL): GBX_LINEAR_TIMEOUT
- * K must be a multiple of 4 and x_hi, x_lo, w_hi, w_lo 16-byte aligned
- * (the TMA row and base rules); M < 2^31.  y must not overlap x or w.
+ * The tensor-core path needs K a multiple of 4 and x_hi, x_lo, w_hi, w_lo
+ * 16-byte aligned (the TMA row and base rules); other shapes run a general
+ * CUDA-core kernel with the same three product terms.  M < 2^31.  y must
+ * not overlap x or w.
  */
 int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo, const float* bias,
                const float* resid, float* y, float* y_lo, int64_t M, int N, int K, int act, int* err_flag,

@@ -41,10 +41,14 @@
 //   - nextToken (new) is one step of generate without the tokenizer: the
 //     argmax / temperature sampling of transformer.cu:994-1028 runs on the
 //     device (gbx_select_tokens), so the logits never cross to the host.
-//   - The contractions around the hot path (QKV, scores, P.V, projections,
-//     FFN up/down) run as fp32 cuBLAS GEMMs; the hot path itself (embed,
-//     LayerNorm, residual + LayerNorm, score epilogue + softmax,
-//     bias + GELU, logits) runs on the sm_100a kernels behind gbx.h.
+//   - The weight contractions (QKV, projection, FFN up/down) run on the
+//     tcgen05 tensor cores (gbx_linear) with fp32 operands carried as tf32
+//     pairs, their bias, GELU and residual fused into the epilogue; the
+//     per-head score and P.V products are fp32 cuBLAS GEMMs.  The hot path
+//     itself (embed, LayerNorm, score epilogue + softmax, logits) runs on the
+//     sm_100a kernels behind gbx.h.  Loading keeps a tf32 pair of every f32
+//     weight matrix on the device (two extra fp32 copies); f16 / bf16
+//     weights need none.
 #pragma once
 
 #include <cstdint>

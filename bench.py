@@ -696,6 +696,109 @@ def run_linear(args, shape, G, g, f32):
                       "speedup_vs_sgemm": sg / us}), flush=True)
 
 
+def bench_gguf(shape, workload):
+    """A GGUF file of random-init GPT-2 weights of the workload's shape (the
+    reference's tensor names, every tensor in the workload's table dtype;
+    matrices and tables ~N(0, 0.02), LayerNorm gains 1 + N(0, 0.1)), written
+    once under the temp directory."""
+    import tempfile
+    import numpy as np
+    path = os.path.join(tempfile.gettempdir(), f"gbx_bench_{workload}.gguf")
+    if os.path.exists(path):
+        return path
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from gguf_writer import gpt2_kv, raw_of, write_gguf
+    rng = np.random.default_rng(0)
+    gt = shape.table_dtype
+    d, ff = shape.d, shape.ff
+    items = []
+
+    def add(name, arr):
+        items.append((name, list(arr.shape), gt, raw_of(arr, gt)))
+
+    n = lambda *s: 0.02 * rng.standard_normal(s, dtype=np.float32)              # noqa: E731
+    gain = lambda k: 1 + 0.1 * rng.standard_normal(k, dtype=np.float32)         # noqa: E731
+    add("token_embd.weight", n(shape.vocab, d))
+    add("position_embd.weight", n(shape.n_ctx, d))
+    for l in range(shape.layers):
+        p = f"blk.{l}."
+        for name, arr in (("attn_norm.weight", gain(d)), ("attn_norm.bias", n(d)), ("attn_qkv.weight", n(3 * d, d)),
+                          ("attn_qkv.bias", n(3 * d)), ("attn_output.weight", n(d, d)), ("attn_output.bias", n(d)),
+                          ("ffn_norm.weight", gain(d)), ("ffn_norm.bias", n(d)), ("ffn_up.weight", n(ff, d)),
+                          ("ffn_up.bias", n(ff)), ("ffn_down.weight", n(d, ff)), ("ffn_down.bias", n(d))):
+            add(p + name, arr)
+    add("output_norm.weight", gain(d))
+    add("output_norm.bias", n(d))
+    tmp = path + f".{os.getpid()}.tmp"
+    write_gguf(tmp, gpt2_kv(d=d, layers=shape.layers, heads=shape.heads, ff=ff, ctx=shape.n_ctx), items)
+    os.replace(tmp, path)
+    return path
+
+
+def forward_flops(shape, tokens, seq):
+    """Multiply-adds x 2 of one forward: the four weight contractions per
+    layer and the per-head score and P.V products, plus the logits row of
+    each sequence."""
+    d, ff, L = shape.d, shape.ff, shape.layers
+    weights = 2.0 * tokens * (3 * d * d + d * d + 2 * d * ff) * L
+    attn = 2.0 * 2 * (tokens // seq) * seq * seq * d * L
+    return weights + attn + 2.0 * (tokens // seq) * d * shape.vocab
+
+
+def run_model_forward(args, shape, desc, impl):
+    """The drop-in TransformerModel::forward end to end through its C ABI
+    (libgbx_model.so: token ids from host memory in, last-row logits to host
+    memory out), wall-clock per call on a random-init GGUF of the workload's
+    model: the batch (forwardBatch) and one sequence.  With impl reference,
+    the reference's own TransformerModel::forward (its transformer.cu,
+    compiled unmodified) on one sequence, on the same GPU."""
+    import numpy as np
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    path = bench_gguf(shape, args.workload)
+    ids = np.random.default_rng(1).integers(0, shape.vocab, shape.batch * shape.seq).astype(np.int32)
+    one = ids[:shape.seq].copy()
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    out = {"mode": "model-forward", "impl": impl, "workload": args.workload, "description": desc,
+           "weights": {0: "f32", 1: "f16", 30: "bf16"}[shape.table_dtype],
+           "data": "synthetic (random-init weights in a GGUF file, seeded token ids)", "warmup": args.warmup,
+           "steps": args.steps}
+    if impl == "reference":
+        import oracle
+        if not oracle.ref_available():
+            out["unavailable"] = "the reference build (oracle/_ref) is missing"
+        else:
+            m = oracle.RefModel(path)
+            s1 = timed(lambda: m.forward(one), max(1, min(args.steps, 3)), 1)
+            m.close()
+            out.update({"sequence_tokens": shape.seq, "single_sequence_ms": s1 * 1e3,
+                        "single_sequence_tokens_per_s": shape.seq / s1,
+                        "single_sequence_tflops": forward_flops(shape, shape.seq, shape.seq) / s1 / 1e12})
+    else:
+        gm = importlib.import_module("glassboxai-transformer_b200.model")
+        m = gm.Model(path)
+        sb = timed(lambda: m.forward(ids, batch=shape.batch), args.steps, args.warmup)
+        s1 = timed(lambda: m.forward(one), args.steps, args.warmup)
+        N = shape.batch * shape.seq
+        out.update({"tokens_per_forward": N, "batch": shape.batch, "seq_len": shape.seq, "forward_ms": sb * 1e3,
+                    "tokens_per_s": N / sb, "tflops": forward_flops(shape, N, shape.seq) / sb / 1e12,
+                    "single_sequence_ms": s1 * 1e3, "single_sequence_tokens_per_s": shape.seq / s1,
+                    "single_sequence_tflops": forward_flops(shape, shape.seq, shape.seq) / s1 / 1e12,
+                    "h2d_bytes_per_forward": 4 * N, "d2h_bytes_per_forward": 4 * shape.batch * shape.vocab})
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -711,6 +814,8 @@ def main():
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--graph", action="store_true",
                     help="capture one step in a CUDA graph and replay it (launch-bound workloads)")
+    ap.add_argument("--model-forward", action="store_true",
+                    help="time the drop-in TransformerModel forward end to end on a random-init GGUF of the workload")
     ap.add_argument("--pdl", action="store_true",
                     help="launch the row kernels with programmatic dependent launch (gbx_set_pdl)")
     args = ap.parse_args()
@@ -721,7 +826,9 @@ def main():
     shape_kw, desc, chain_kw, scaling = WORKLOADS[args.workload]
     chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
     shape = chain_mod.ChainShape(**shape_kw)
-    if args.kernel:
+    if args.model_forward:
+        run_model_forward(args, shape, desc, args.impl)
+    elif args.kernel:
         run_kernel(args, shape)
     elif args.impl == "reference":
         run_reference(args, shape, desc)

@@ -47,6 +47,7 @@ SIGNATURES = {
     "gbx_dequant": [_vp, _int, _vp, _i64, _vp],
     "gbx_embed": [_vp, _vp, _int, _vp, _int, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, _vp],
     "gbx_layernorm": [_vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
+    "gbx_layernorm_pair": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
     "gbx_residual_layernorm": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
     "gbx_bias_gelu": [_vp, _vp, _vp, _i64, _int, _vp],
     "gbx_softmax_rows": [_vp, _vp, _i64, _int, _vp],
@@ -129,6 +130,11 @@ def embed(ids, wte, wte_dtype, wpe, wpe_dtype, out, *, n_tok, d, vocab, n_ctx, s
 
 def layernorm(x, y, gamma, beta, *, rows, d, eps=1e-5, stream=None):
     _check(lib().gbx_layernorm(_p(x), _p(y), _p(gamma), _p(beta), rows, d, eps, _stream(stream)))
+
+
+def layernorm_pair(x, y_hi, y_lo, gamma, beta, *, rows, d, eps=1e-5, stream=None):
+    """LayerNorm with the output as a tf32 pair (the x operand of linear)."""
+    _check(lib().gbx_layernorm_pair(_p(x), _p(y_hi), _p(y_lo), _p(gamma), _p(beta), rows, d, eps, _stream(stream)))
 
 
 def residual_layernorm(x, r, h_out, y, gamma, beta, *, rows, d, eps=1e-5, xbias=None, stream=None):

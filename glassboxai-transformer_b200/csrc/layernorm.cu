@@ -13,6 +13,7 @@
 // and differs from it only in the order of the two sums (shuffle tree here,
 // shared-memory tree there).
 #include "rows.cuh"
+#include "tf32.cuh"
 
 namespace gbx {
 
@@ -21,9 +22,11 @@ __device__ __forceinline__ float4 f4add(float4 a, float4 b)
     return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
 
+// y_lo non-null: y and y_lo receive the tf32 pair of the output (tf32.cuh)
+// instead of the fp32 output, for gbx_linear.
 template <int TPR, int V4, bool RESID>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads)
-ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out, float* y,
+ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out, float* y, float* y_lo,
               const float* __restrict__ gamma, const float* __restrict__ beta, int64_t rows, int d, float eps)
 {
     grid_dependency_wait();   // see launch_row_kernel
@@ -90,7 +93,14 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
                 o.y = fmaf((v[k].y - mean) * inv, g.y, b.y);
                 o.z = fmaf((v[k].z - mean) * inv, g.z, b.z);
                 o.w = fmaf((v[k].w - mean) * inv, g.w, b.w);
-                st_stream(y + off + 4 * c, o);
+                if (y_lo) {
+                    float4 hi, lo;
+                    split4(o, hi, lo);
+                    st_stream(y + off + 4 * c, hi);
+                    st_stream(y_lo + off + 4 * c, lo);
+                } else {
+                    st_stream(y + off + 4 * c, o);
+                }
             }
         }
     }
@@ -103,7 +113,7 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
 template <bool RESID>
 __global__ void __launch_bounds__(kGeneralCTA)
 ln_general_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out,
-                  float* y, const float* __restrict__ gamma, const float* __restrict__ beta,
+                  float* y, float* y_lo, const float* __restrict__ gamma, const float* __restrict__ beta,
                   int64_t rows, int d, float eps)
 {
     __shared__ float red[2][kGeneralCTA / 32];
@@ -135,33 +145,41 @@ ln_general_kernel(const float* x, const float* r, const float* __restrict__ xbia
         for (int i = threadIdx.x; i < d; i += kGeneralCTA) {
             const float g = gamma ? gamma[i] : 1.0f;
             const float b = beta ? beta[i] : 0.0f;
-            y[off + i] = fmaf((hval(i) - mean) * inv, g, b);
+            const float o = fmaf((hval(i) - mean) * inv, g, b);
+            if (y_lo) {
+                float hi, lo;
+                split_value(o, hi, lo);
+                y[off + i] = hi;
+                y_lo[off + i] = lo;
+            } else {
+                y[off + i] = o;
+            }
         }
         __syncthreads();   // pass-0 writes of the next row vs this row's reads
     }
 }
 
 template <int TPR, int V4, bool RESID>
-static int launch_ln_vec(const float* x, const float* r, const float* xbias, float* h_out, float* y,
+static int launch_ln_vec(const float* x, const float* r, const float* xbias, float* h_out, float* y, float* y_lo,
                          const float* g, const float* b, int64_t rows, int d, float eps, cudaStream_t stream)
 {
     const int64_t grid = row_grid<TPR>(rows);
     if (grid < 0) return GBX_ERANGE;
     launch_row_kernel(ln_vec_kernel<TPR, V4, RESID>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads), 0, stream, x,
-                      r, xbias, h_out, y, g, b, rows, d, eps);
+                      r, xbias, h_out, y, y_lo, g, b, rows, d, eps);
     return GBX_OK;
 }
 
 template <bool RESID>
 static int launch_ln(const char* what, const float* x, const float* r, const float* xbias, float* h_out, float* y,
-                     const float* g, const float* b, int64_t rows, int d, float eps, cudaStream_t stream)
+                     float* y_lo, const float* g, const float* b, int64_t rows, int d, float eps, cudaStream_t stream)
 {
     RowShape shape;
     const bool vec = d % 4 == 0 && row_shape(d / 4, &shape) && aligned16(x) && aligned16(y) &&
-                     (!RESID || aligned16(r)) && (!h_out || aligned16(h_out)) && (!xbias || aligned16(xbias)) &&
-                     (!g || aligned16(g)) && (!b || aligned16(b));
+                     (!y_lo || aligned16(y_lo)) && (!RESID || aligned16(r)) && (!h_out || aligned16(h_out)) &&
+                     (!xbias || aligned16(xbias)) && (!g || aligned16(g)) && (!b || aligned16(b));
     if (vec) {
-#define GBX_LN_CALL(T, V) launch_ln_vec<T, V, RESID>(x, r, xbias, h_out, y, g, b, rows, d, eps, stream)
+#define GBX_LN_CALL(T, V) launch_ln_vec<T, V, RESID>(x, r, xbias, h_out, y, y_lo, g, b, rows, d, eps, stream)
         const int rc = GBX_ROW_DISPATCH(shape, GBX_LN_CALL, GBX_ERANGE);
 #undef GBX_LN_CALL
         if (rc != GBX_OK) return set_error(rc, "%s: rows=%lld d=%d out of range", what, (long long)rows, d);
@@ -169,7 +187,7 @@ static int launch_ln(const char* what, const float* x, const float* r, const flo
         auto k = ln_general_kernel<RESID>;
         const int grid = persistent_grid(k, kGeneralCTA, 0, rows, 4);
         if (grid < 1) return GBX_ECUDA;
-        k<<<grid, kGeneralCTA, 0, stream>>>(x, r, xbias, h_out, y, g, b, rows, d, eps);
+        k<<<grid, kGeneralCTA, 0, stream>>>(x, r, xbias, h_out, y, y_lo, g, b, rows, d, eps);
     }
     return check_launch(what);
 }
@@ -184,8 +202,19 @@ extern "C" int gbx_layernorm(const float* x, float* y, const float* gamma, const
     if (rows < 0 || d <= 0) return set_error(GBX_EINVAL, "gbx_layernorm: rows=%lld d=%d", (long long)rows, d);
     if (rows == 0) return GBX_OK;
     if (!x || !y) return set_error(GBX_EINVAL, "gbx_layernorm: null pointer");
-    return launch_ln<false>("gbx_layernorm", x, nullptr, nullptr, nullptr, y, gamma, beta, rows, d, eps,
+    return launch_ln<false>("gbx_layernorm", x, nullptr, nullptr, nullptr, y, nullptr, gamma, beta, rows, d, eps,
                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gbx_layernorm_pair(const float* x, float* y_hi, float* y_lo, const float* gamma, const float* beta,
+                                  int64_t rows, int d, float eps, gbx_stream_t stream)
+{
+    if (rows < 0 || d <= 0) return set_error(GBX_EINVAL, "gbx_layernorm_pair: rows=%lld d=%d", (long long)rows, d);
+    if (rows == 0) return GBX_OK;
+    if (!x || !y_hi || !y_lo) return set_error(GBX_EINVAL, "gbx_layernorm_pair: null pointer");
+    if (y_lo == x || y_lo == y_hi) return set_error(GBX_EINVAL, "gbx_layernorm_pair: y_lo must not alias x or y_hi");
+    return launch_ln<false>("gbx_layernorm_pair", x, nullptr, nullptr, nullptr, y_hi, y_lo, gamma, beta, rows, d,
+                            eps, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gbx_residual_layernorm(const float* x, const float* r, const float* xbias, float* h_out,
@@ -197,6 +226,6 @@ extern "C" int gbx_residual_layernorm(const float* x, const float* r, const floa
     if (rows == 0) return GBX_OK;
     if (!x || !r || !y) return set_error(GBX_EINVAL, "gbx_residual_layernorm: null pointer");
     if (h_out && h_out == y) return set_error(GBX_EINVAL, "gbx_residual_layernorm: h_out and y must differ");
-    return launch_ln<true>("gbx_residual_layernorm", x, r, xbias, h_out, y, gamma, beta, rows, d, eps,
+    return launch_ln<true>("gbx_residual_layernorm", x, r, xbias, h_out, y, nullptr, gamma, beta, rows, d, eps,
                            reinterpret_cast<cudaStream_t>(stream));
 }

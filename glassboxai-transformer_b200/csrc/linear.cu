@@ -44,6 +44,7 @@
 #include "gbx_common.cuh"
 #include "gelu.cuh"
 #include "tcgen05.cuh"
+#include "tf32.cuh"
 
 namespace gbx {
 
@@ -61,18 +62,24 @@ constexpr int kLinTmemCols = kLinBuffers * kLinBN;
 constexpr int kLinChunkK = GBX_LINEAR_CHUNK_K;   // K elements summed in TMEM before each fp32 promotion
 constexpr uint64_t kLinWaitNs = 1000000000ull;
 
-template <int BK>
+// Shared-memory ring and barrier layout.  PAIR: a cluster of two CTAs runs
+// one M 256 x N 256 MMA (cta_group::2); each CTA holds its 128 x rows and
+// half (128) of the w rows, so a stage is 4 tiles of 128 rows.
+template <int BK, bool PAIR>
 struct LinCfg {
     static constexpr int row_bytes = BK * 4;             // 64 or 128: the swizzle width
-    static constexpr int a_bytes = kLinBM * row_bytes;   // one x tile
-    static constexpr int b_bytes = kLinBN * row_bytes;   // one w tile
+    static constexpr int a_rows = kLinBM;                 // x rows in this CTA
+    static constexpr int b_rows = PAIR ? kLinBN / 2 : kLinBN;   // w rows in this CTA
+    static constexpr int a_bytes = a_rows * row_bytes;   // one x tile
+    static constexpr int b_bytes = b_rows * row_bytes;   // one w tile
     static constexpr int stage_bytes = 2 * a_bytes + 2 * b_bytes;
-    static constexpr int stages = (196 * 1024) / stage_bytes;   // BK 16: 4, BK 32: 2
+    static constexpr int stages = (196 * 1024) / stage_bytes;   // BK 16: 4 (6 paired), BK 32: 2 (3 paired)
     static constexpr int ksteps = BK / 8;                       // tf32 MMA K = 8 (32 bytes)
     static constexpr int chunk_blocks = kLinChunkK / BK;          // K blocks per chunk
-    static_assert(kLinChunkK % 32 == 0, "a chunk is whole K blocks");
+    static constexpr int tile_rows = PAIR ? 2 * kLinBM : kLinBM;  // output rows per tile
     static constexpr int nbars = 2 * stages + 2 * kLinBuffers + 1;
     static constexpr size_t smem = (size_t)stages * stage_bytes + 1024 + 8 * nbars + 16;
+    static_assert(kLinChunkK % 32 == 0, "a chunk is whole K blocks");
     static_assert(BK == 16 || BK == 32, "swizzle width");
     static_assert(stages >= 2, "pipeline depth");
     static_assert(a_bytes % 1024 == 0 && b_bytes % 1024 == 0, "tiles stay aligned to the swizzle repeat");
@@ -105,13 +112,6 @@ __device__ __forceinline__ void tile_coords(int t, const LinearArgs& a, int& mb,
 {
     mb = t / a.n_blocks;
     nb = t - mb * a.n_blocks;
-}
-
-__device__ __forceinline__ void split_value(float x, float& hi, float& lo)
-{
-    hi = tc::to_tf32(x);
-    if (isinf(hi) && !isinf(x)) hi = __uint_as_float(__float_as_uint(x) & 0xffffe000u);   // rounding overflowed
-    lo = isfinite(hi) ? tc::to_tf32(x - hi) : 0.0f;
 }
 
 __device__ __forceinline__ float epi_value(float acc, int n, int64_t row, const LinearArgs& a)
@@ -174,13 +174,13 @@ __device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, i
     }
 }
 
-template <int BK, bool VEC>
+template <int BK, bool VEC, bool PAIR>
 __global__ void __launch_bounds__(kLinThreads, 1)
 linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constant__ CUtensorMap map_xl,
                      const __grid_constant__ CUtensorMap map_wh, const __grid_constant__ CUtensorMap map_wl,
                      const LinearArgs a)
 {
-    using C = LinCfg<BK>;
+    using C = LinCfg<BK, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::stages * C::stage_bytes);
@@ -196,6 +196,13 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int chunks = (a.k_blocks + C::chunk_blocks - 1) / C::chunk_blocks;   // per tile
+    // PAIR: the barriers that count both CTAs (full, chunk_empty, drain) live
+    // in the leader, rank 0; empty and chunk_full exist in both (the MMA
+    // commit multicasts to the two)
+    const uint32_t rank = PAIR ? tc::cluster_rank() : 0;
+    const bool leader = rank == 0;
+    const int unit = PAIR ? (int)tc::cluster_id_x() : (int)blockIdx.x;        // tile walker
+    const int units = PAIR ? (int)tc::cluster_count_x() : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::stages; ++s) {
@@ -204,7 +211,7 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
         }
         for (int b = 0; b < kLinBuffers; ++b) {
             tc::mbar_init(cfull0 + 8 * b, 1);
-            tc::mbar_init(cempty0 + 8 * b, kLinEpiThreads);
+            tc::mbar_init(cempty0 + 8 * b, (PAIR ? 2 : 1) * kLinEpiWarps);   // one arrival per epilogue warp
         }
         tc::mbar_init(drain, 1);
         *abort = 0;
@@ -215,37 +222,54 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
         if (a.has_wlo) tc::tma_prefetch(&map_wl);
     }
     if (warp == 1) {
-        tc::tmem_alloc(tc::smem_u32(tmem_slot), kLinTmemCols);
-        tc::tmem_relinquish();
+        if constexpr (PAIR) {
+            tc::tmem_alloc_pair(tc::smem_u32(tmem_slot), kLinTmemCols);
+            tc::tmem_relinquish_pair();
+        } else {
+            tc::tmem_alloc(tc::smem_u32(tmem_slot), kLinTmemCols);
+            tc::tmem_relinquish();
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
+    if constexpr (PAIR) tc::cluster_sync();   // both CTAs' barriers and TMEM exist before any cross-CTA signal
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------------------------------------------- producer
-            const uint32_t bytes = (uint32_t)(C::a_bytes * (1 + a.has_xlo) + C::b_bytes * (1 + a.has_wlo));
+            const uint32_t cta_bytes = (uint32_t)(C::a_bytes * (1 + a.has_xlo) + C::b_bytes * (1 + a.has_wlo));
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued = 0;    // bit s: stage s has had a load issued
             uint32_t lastpar = 0;   // bit s: parity of the phase of its last load
-            for (int t = blockIdx.x; t < a.tiles && !*abort; t += gridDim.x) {
+            for (int t = unit; t < a.tiles && !*abort; t += units) {
                 int mb, nb;
                 tile_coords(t, a, mb, nb);
-                const int y_x = mb * kLinBM;
-                const int y_w = nb * kLinBN;
+                const int n_left = a.N - nb * kLinBN;
+                const int n_mma = n_left >= kLinBN ? kLinBN : (n_left + 15) & ~15;
+                const int y_x = mb * C::tile_rows + (int)rank * kLinBM;
+                const int y_w = nb * kLinBN + (PAIR ? (int)rank * (n_mma / 2) : 0);
                 for (int kb = 0; kb < a.k_blocks; ++kb) {
                     if (!tc::mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kLinWaitNs)) break;
                     const uint32_t full = full0 + 8 * stage;
                     const uint32_t base = smem0 + stage * C::stage_bytes;
-                    tc::mbar_arrive_expect_tx(full, bytes);
                     const int x = kb * BK;
-                    tc::tma_load_2d(base, &map_xh, full, x, y_x);
-                    if (a.has_xlo) tc::tma_load_2d(base + C::a_bytes, &map_xl, full, x, y_x);
-                    tc::tma_load_2d(base + 2 * C::a_bytes, &map_wh, full, x, y_w);
-                    if (a.has_wlo) tc::tma_load_2d(base + 2 * C::a_bytes + C::b_bytes, &map_wl, full, x, y_w);
+                    if constexpr (PAIR) {
+                        if (leader) tc::mbar_arrive_expect_tx(full, 2 * cta_bytes);   // both CTAs' tiles
+                        const uint32_t fl = tc::mapa(full, 0);
+                        tc::tma_load_2d_pair(base, &map_xh, fl, x, y_x);
+                        if (a.has_xlo) tc::tma_load_2d_pair(base + C::a_bytes, &map_xl, fl, x, y_x);
+                        tc::tma_load_2d_pair(base + 2 * C::a_bytes, &map_wh, fl, x, y_w);
+                        if (a.has_wlo) tc::tma_load_2d_pair(base + 2 * C::a_bytes + C::b_bytes, &map_wl, fl, x, y_w);
+                    } else {
+                        tc::mbar_arrive_expect_tx(full, cta_bytes);
+                        tc::tma_load_2d(base, &map_xh, full, x, y_x);
+                        if (a.has_xlo) tc::tma_load_2d(base + C::a_bytes, &map_xl, full, x, y_x);
+                        tc::tma_load_2d(base + 2 * C::a_bytes, &map_wh, full, x, y_w);
+                        if (a.has_wlo) tc::tma_load_2d(base + 2 * C::a_bytes + C::b_bytes, &map_wl, full, x, y_w);
+                    }
                     issued |= 1u << stage;
                     lastpar = (lastpar & ~(1u << stage)) | (phase << stage);
                     if (++stage == C::stages) {
@@ -254,25 +278,29 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                     }
                 }
             }
-            // every load issued has landed before the CTA may exit
-            for (int s = 0; s < C::stages; ++s)
-                if (issued & (1u << s)) tc::mbar_wait(full0 + 8 * s, (lastpar >> s) & 1, nullptr, kLinWaitNs);
+            // Every load issued has landed before the CTA may exit.  PAIR: the
+            // leader's full barriers count both CTAs' loads; the follower's
+            // last loads are consumed by the leader's MMAs before the final
+            // cluster barrier (or, after an abort, had a wait limit's time to land).
+            if (leader)
+                for (int s = 0; s < C::stages; ++s)
+                    if (issued & (1u << s)) tc::mbar_wait(full0 + 8 * s, (lastpar >> s) & 1, nullptr, kLinWaitNs);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && leader) {
             // ---------------------------------------------------- MMA issuer
             int stage = 0;
             uint32_t phase = 0;
             int buf = 0;
             uint32_t buf_phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
+            for (int t = unit; t < a.tiles && ok; t += units) {
                 // the last column tile runs only as wide as N needs (a multiple of 16)
                 int mb, nb;
                 tile_coords(t, a, mb, nb);
                 const int n_left = a.N - nb * kLinBN;
                 const int n_mma = n_left >= kLinBN ? kLinBN : (n_left + 15) & ~15;
-                const uint32_t idesc = tc::idesc_tf32(kLinBM, n_mma);
+                const uint32_t idesc = tc::idesc_tf32(C::tile_rows, n_mma);
                 for (int c = 0; c < chunks && ok; ++c) {
                     if (!tc::mbar_wait(cempty0 + 8 * buf, buf_phase ^ 1, abort, kLinWaitNs)) {
                         ok = false;
@@ -294,22 +322,43 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                             const uint32_t off = ks * 32;
                             const uint64_t xh = tc::smem_desc(base + off, C::row_bytes);
                             const uint64_t wh = tc::smem_desc(base + 2 * C::a_bytes + off, C::row_bytes);
-                            tc::mma_tf32(d, xh, wh, idesc, (kb != kb0) | (ks != 0));
-                            if (a.has_wlo)
-                                tc::mma_tf32(d, xh,
-                                             tc::smem_desc(base + 2 * C::a_bytes + C::b_bytes + off, C::row_bytes),
-                                             idesc, 1);
-                            if (a.has_xlo)
-                                tc::mma_tf32(d, tc::smem_desc(base + C::a_bytes + off, C::row_bytes), wh, idesc, 1);
+                            const uint32_t acc0 = (kb != kb0) | (ks != 0);
+                            if constexpr (PAIR) {
+                                tc::mma_tf32_pair(d, xh, wh, idesc, acc0);
+                                if (a.has_wlo)
+                                    tc::mma_tf32_pair(
+                                        d, xh, tc::smem_desc(base + 2 * C::a_bytes + C::b_bytes + off, C::row_bytes),
+                                        idesc, 1);
+                                if (a.has_xlo)
+                                    tc::mma_tf32_pair(d, tc::smem_desc(base + C::a_bytes + off, C::row_bytes), wh,
+                                                      idesc, 1);
+                            } else {
+                                tc::mma_tf32(d, xh, wh, idesc, acc0);
+                                if (a.has_wlo)
+                                    tc::mma_tf32(d, xh,
+                                                 tc::smem_desc(base + 2 * C::a_bytes + C::b_bytes + off, C::row_bytes),
+                                                 idesc, 1);
+                                if (a.has_xlo)
+                                    tc::mma_tf32(d, tc::smem_desc(base + C::a_bytes + off, C::row_bytes), wh, idesc,
+                                                 1);
+                            }
                         }
-                        tc::mma_commit(empty0 + 8 * stage);   // the stage is free once these MMAs are done
+                        // the stage is free (in both CTAs) once these MMAs are done
+                        if constexpr (PAIR)
+                            tc::mma_commit_pair_multicast(empty0 + 8 * stage, 3);
+                        else
+                            tc::mma_commit(empty0 + 8 * stage);
                         if (++stage == C::stages) {
                             stage = 0;
                             phase ^= 1;
                         }
                     }
                     if (!ok) break;
-                    tc::mma_commit(cfull0 + 8 * buf);   // chunk complete
+                    // chunk complete (in both CTAs' TMEM)
+                    if constexpr (PAIR)
+                        tc::mma_commit_pair_multicast(cfull0 + 8 * buf, 3);
+                    else
+                        tc::mma_commit(cfull0 + 8 * buf);
                     if (++buf == kLinBuffers) {
                         buf = 0;
                         buf_phase ^= 1;
@@ -317,18 +366,21 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                 }
             }
             // every MMA issued has completed before TMEM is freed
-            tc::mma_commit(drain);
+            if constexpr (PAIR)
+                tc::mma_commit_pair(drain);
+            else
+                tc::mma_commit(drain);
             tc::mbar_wait(drain, 0, nullptr, kLinWaitNs);
         }
     } else {
         // -------------------------------------------------------- epilogue
         const int quarter = warp & 3;   // the TMEM lanes this warp may read
         const int col0 = ((warp - 2) >> 2) * kLinEpiCols;
-        const int row_in_tile = 32 * quarter + lane;
+        const int row_in_tile = (int)rank * kLinBM + 32 * quarter + lane;
         int buf = 0;
         uint32_t buf_phase = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < a.tiles && ok; t += gridDim.x) {
+        for (int t = unit; t < a.tiles && ok; t += units) {
             int mb, nb;
             tile_coords(t, a, mb, nb);
             float acc[kLinEpiCols];
@@ -355,14 +407,20 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                     }
                 }
                 tc::fence_before_sync();
-                tc::mbar_arrive(cempty0 + 8 * buf);
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (PAIR)
+                        tc::mbar_arrive_cluster(tc::mapa(cempty0 + 8 * buf, 0));
+                    else
+                        tc::mbar_arrive(cempty0 + 8 * buf);
+                }
                 if (++buf == kLinBuffers) {
                     buf = 0;
                     buf_phase ^= 1;
                 }
             }
             if (!ok) break;
-            const int64_t row = (int64_t)mb * kLinBM + row_in_tile;
+            const int64_t row = (int64_t)mb * C::tile_rows + row_in_tile;
             const int n0 = nb * kLinBN + col0;
             if (row < a.M) {
 #pragma unroll
@@ -379,10 +437,14 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
     }
 
     __syncthreads();   // every role has left its loop (all waits are bounded)
+    if constexpr (PAIR) tc::cluster_sync();   // the leader's MMAs, which read both CTAs, are drained
     if (warp == 1) {
         __syncwarp();
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, kLinTmemCols);
+        if constexpr (PAIR)
+            tc::tmem_dealloc_pair(tmem, kLinTmemCols);
+        else
+            tc::tmem_dealloc(tmem, kLinTmemCols);
     }
     if (threadIdx.x == 0 && *abort && a.err) atomicOr(a.err, GBX_LINEAR_TIMEOUT);
 }
@@ -480,36 +542,64 @@ static int make_map(CUtensorMap* m, const float* base, int64_t rows, int K, int 
     return GBX_OK;
 }
 
-template <int BK, bool VEC>
-static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
-                         const LinearArgs& a, cudaStream_t s)
+template <int BK, bool VEC, bool PAIR>
+static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo, LinearArgs a,
+                         cudaStream_t s)
 {
-    using C = LinCfg<BK>;
+    using C = LinCfg<BK, PAIR>;
     DeviceInfo di;
     if (device_info(&di) != GBX_OK) return GBX_ECUDA;
     if ((size_t)di.max_smem_optin < C::smem)
         return set_error(GBX_ERANGE, "gbx_linear: needs %zu bytes of shared memory per CTA", C::smem);
+    const int64_t m_blocks = (a.M + C::tile_rows - 1) / C::tile_rows;
+    if (m_blocks * a.n_blocks > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: too many tiles");
+    a.m_blocks = (int)m_blocks;
+    a.tiles = (int)(m_blocks * a.n_blocks);
+    a.k_blocks = (a.K + BK - 1) / BK;
     CUtensorMap mxh, mxl, mwh, mwl;
     int rc;
-    if ((rc = make_map(&mxh, x_hi, a.M, a.K, kLinBM, BK)) != GBX_OK) return rc;
-    if ((rc = make_map(&mwh, w_hi, a.N, a.K, kLinBN, BK)) != GBX_OK) return rc;
+    if ((rc = make_map(&mxh, x_hi, a.M, a.K, C::a_rows, BK)) != GBX_OK) return rc;
+    if ((rc = make_map(&mwh, w_hi, a.N, a.K, C::b_rows, BK)) != GBX_OK) return rc;
     if (a.has_xlo) {
-        if ((rc = make_map(&mxl, x_lo, a.M, a.K, kLinBM, BK)) != GBX_OK) return rc;
+        if ((rc = make_map(&mxl, x_lo, a.M, a.K, C::a_rows, BK)) != GBX_OK) return rc;
     } else {
         mxl = mxh;   // never loaded
     }
     if (a.has_wlo) {
-        if ((rc = make_map(&mwl, w_lo, a.N, a.K, kLinBN, BK)) != GBX_OK) return rc;
+        if ((rc = make_map(&mwl, w_lo, a.N, a.K, C::b_rows, BK)) != GBX_OK) return rc;
     } else {
         mwl = mwh;
     }
-    auto k = linear_tf32x3_kernel<BK, VEC>;
+    auto k = linear_tf32x3_kernel<BK, VEC, PAIR>;
     // per device, so set on every call (a host-side attribute write)
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::smem) != cudaSuccess)
         return set_error(GBX_ECUDA, "gbx_linear: shared-memory attribute refused");
-    const int grid = a.tiles < di.sm_count ? a.tiles : di.sm_count;
-    k<<<grid, kLinThreads, C::smem, s>>>(mxh, mxl, mwh, mwl, a);
-    return check_launch("gbx_linear");
+    if constexpr (!PAIR) {
+        const int grid = a.tiles < di.sm_count ? a.tiles : di.sm_count;
+        k<<<grid, kLinThreads, C::smem, s>>>(mxh, mxl, mwh, mwl, a);
+        return check_launch("gbx_linear");
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.blockDim = dim3(kLinThreads);
+        cfg.dynamicSmemBytes = C::smem;
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cfg.gridDim = dim3(2 * (unsigned)(di.sm_count / 2));
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess || clusters < 1)
+            return set_error(GBX_ECUDA, "gbx_linear: no resident CTA pair fits");
+        if (clusters > a.tiles) clusters = a.tiles;
+        cfg.gridDim = dim3(2 * (unsigned)clusters);
+        if (cudaLaunchKernelEx(&cfg, k, mxh, mxl, mwh, mwl, a) != cudaSuccess)
+            return set_error(GBX_ECUDA, "gbx_linear: cluster launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return check_launch("gbx_linear");
+    }
 }
 
 }  // namespace gbx
@@ -536,15 +626,28 @@ extern "C" int gbx_split_tf32(const float* x, float* hi, float* lo, int64_t n, g
     return check_launch("gbx_split_tf32");
 }
 
-// Tile K width: 16 (64-byte rows, 4 pipeline stages) unless GBX_LINEAR_BK=32
-// (128-byte rows, 2 stages) is set in the environment, read once.
+// Tile K width: 16 (64-byte rows, 4 pipeline stages; 6 in CTA pairs)
+// unless GBX_LINEAR_BK=32 (128-byte rows) is set in the environment.  CTA
+// pairs (M 256 tiles over two SMs) for M >= kLinPairMinRows unless
+// GBX_LINEAR_PAIR=0; GBX_LINEAR_PAIR=1 forces them.  Read once.
+constexpr int64_t kLinPairMinRows = 1024;
+
+static int env_int(const char* name, int dflt)
+{
+    const char* e = getenv(name);
+    return (e && *e) ? atoi(e) : dflt;
+}
+
 static int linear_bk()
 {
-    static int bk = [] {
-        const char* e = getenv("GBX_LINEAR_BK");
-        return (e && atoi(e) == 32) ? 32 : 16;
-    }();
+    static int bk = env_int("GBX_LINEAR_BK", 16) == 32 ? 32 : 16;
     return bk;
+}
+
+static int linear_pair_mode()   // -1 auto, 0 never, 1 always
+{
+    static int mode = env_int("GBX_LINEAR_PAIR", -1);
+    return mode;
 }
 
 extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
@@ -560,9 +663,7 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
         (w_lo && (const float*)y == w_lo))
         return set_error(GBX_EINVAL, "gbx_linear: y aliases an operand");
     if (M > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: M=%lld", (long long)M);
-    const int64_t m_blocks = (M + kLinBM - 1) / kLinBM;
     const int64_t n_blocks = ((int64_t)N + kLinBN - 1) / kLinBN;
-    if (m_blocks * n_blocks > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: too many tiles");
 
     LinearArgs a;
     a.bias = bias;
@@ -573,9 +674,7 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     a.M = M;
     a.N = N;
     a.K = K;
-    a.m_blocks = (int)m_blocks;
     a.n_blocks = (int)n_blocks;
-    a.tiles = (int)(m_blocks * n_blocks);
     a.act = act;
     a.has_xlo = x_lo != nullptr;
     a.has_wlo = w_lo != nullptr;
@@ -585,17 +684,20 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     const bool tma_ok = K % 4 == 0 && aligned16(x_hi) && aligned16(w_hi) && (!x_lo || aligned16(x_lo)) &&
                         (!w_lo || aligned16(w_lo));
     if (!tma_ok) {
+        a.m_blocks = a.tiles = a.k_blocks = 0;   // unused by the general kernel
         const int grid = persistent_grid(linear_general_kernel, 256, 0, (M * N + 255) / 256, 8);
         if (grid < 1) return GBX_ECUDA;
         linear_general_kernel<<<grid, 256, 0, s>>>(x_hi, x_lo, w_hi, w_lo, a);
         return check_launch("gbx_linear");
     }
+    const int pm = linear_pair_mode();
+    const bool pair = pm == 1 || (pm != 0 && M >= kLinPairMinRows);
+#define GBX_LIN(BKV, VECV, PAIRV) launch_linear<BKV, VECV, PAIRV>(x_hi, x_lo, w_hi, w_lo, a, s)
     if (linear_bk() == 32) {
-        a.k_blocks = (K + 31) / 32;
-        return vec ? launch_linear<32, true>(x_hi, x_lo, w_hi, w_lo, a, s)
-                   : launch_linear<32, false>(x_hi, x_lo, w_hi, w_lo, a, s);
+        if (pair) return vec ? GBX_LIN(32, true, true) : GBX_LIN(32, false, true);
+        return vec ? GBX_LIN(32, true, false) : GBX_LIN(32, false, false);
     }
-    a.k_blocks = (K + 15) / 16;
-    return vec ? launch_linear<16, true>(x_hi, x_lo, w_hi, w_lo, a, s)
-               : launch_linear<16, false>(x_hi, x_lo, w_hi, w_lo, a, s);
+    if (pair) return vec ? GBX_LIN(16, true, true) : GBX_LIN(16, false, true);
+    return vec ? GBX_LIN(16, true, false) : GBX_LIN(16, false, false);
+#undef GBX_LIN
 }

@@ -7,7 +7,7 @@
 //
 //   gbx_embed                              h = wte[ids] + wpe[pos]          (:805-815)
 //   for each layer l:
-//     gbx_layernorm, gbx_split_tf32        ln = LN1(h), as a tf32 pair     (:827-828)
+//     gbx_layernorm_pair                   ln = LN1(h), as a tf32 pair     (:827-828)
 //     gbx_linear                           qkv = ln . Wqkv^T + b_qkv       (:830-832)
 //     cuBLAS (per sequence, batched over heads)
 //                                          raw[h] = Q_h . K_h^T            (:834-837, without
@@ -17,7 +17,7 @@
 //                                          attn_h = P_h . V_h              (:844-846)
 //     gbx_split_tf32, gbx_linear           h += attn . Wproj^T + b_proj    (:848-852, the
 //                                                                          residual in the epilogue)
-//     gbx_layernorm, gbx_split_tf32        ln = LN2(h)                     (:866-868)
+//     gbx_layernorm_pair                   ln = LN2(h), as a tf32 pair     (:866-868)
 //     gbx_linear                           up = GELU(ln . Wup^T + b_up), as a tf32 pair
 //                                                                          (:870-872)
 //     gbx_linear                           h += up . Wdown^T + b_down      (:874-878)
@@ -363,8 +363,7 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
     for (int l = 0; l < numLayers_ && rc == GBX_OK && blas_ok; ++l) {
         const Impl::Layer& L = m.layers[l];
         const Impl::LayerW& W = m.wpairs[l];
-        check(gbx_layernorm(m.h.p, m.ln.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
-        check(gbx_split_tf32(m.ln.p, m.ln.p, m.ln_lo.p, N * d, gs));
+        check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
         linear(m.ln.p, m.ln_lo.p, W.qkv, L.qkv_b, nullptr, m.qkv.p, nullptr, N, 3 * d, d, GBX_ACT_NONE);
         for (int b = 0; b < batch; ++b) {
             const float* q = m.qkv.p + (int64_t)b * S * 3 * d;
@@ -380,8 +379,7 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
         }
         check(gbx_split_tf32(m.attn.p, m.attn.p, m.attn_lo.p, N * d, gs));
         linear(m.attn.p, m.attn_lo.p, W.proj, L.proj_b, m.h.p, m.h.p, nullptr, N, d, d, GBX_ACT_NONE);
-        check(gbx_layernorm(m.h.p, m.ln.p, L.ln2_g, L.ln2_b, N, d, 1e-5f, gs));
-        check(gbx_split_tf32(m.ln.p, m.ln.p, m.ln_lo.p, N * d, gs));
+        check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln2_g, L.ln2_b, N, d, 1e-5f, gs));
         linear(m.ln.p, m.ln_lo.p, W.up, L.up_b, nullptr, m.up.p, m.up_lo.p, N, F, d, GBX_ACT_GELU);
         linear(m.up.p, m.up_lo.p, W.down, L.down_b, m.h.p, m.h.p, nullptr, N, d, F, GBX_ACT_NONE);
     }

@@ -109,6 +109,15 @@ int gbx_layernorm(const float* x, float* y, const float* gamma, const float* bet
                   int d, float eps, gbx_stream_t stream);
 
 /*
+ * gbx_layernorm with the output as the tf32 pair gbx_linear reads as its x
+ * operand: y_hi, y_lo are exactly gbx_split_tf32 of gbx_layernorm's y, in
+ * one pass (no fp32 copy of y).  No counterpart in the reference: it feeds
+ * the QKV and FFN-up contractions.  y_hi may alias x; y_lo may not.
+ */
+int gbx_layernorm_pair(const float* x, float* y_hi, float* y_lo, const float* gamma, const float* beta,
+                       int64_t rows, int d, float eps, gbx_stream_t stream);
+
+/*
  * Fused residual add + LayerNorm.  Replaces the residual epilogue of
  * projectionKernel / ffnDownKernel (transformer.cu:262, :292:
  * out = residual + (bias + sum)) followed by the next layerNormKernel:

@@ -126,6 +126,33 @@ def test_split_tf32_pairs(gbx, cuda):
         assert np.all(l[~fin] == 0)
 
 
+@pytest.mark.parametrize("rows,d,off", [(300, 1600, 0), (33, 768, 0), (17, 70, 0), (40, 64, 1)])
+def test_layernorm_pair_is_split_of_layernorm(gbx, cuda, rows, d, off):
+    """gbx_layernorm_pair gives, bit for bit, gbx_split_tf32 of gbx_layernorm
+    (vector rows, a row length with a remainder, and misaligned rows on the
+    general kernel)."""
+    import torch
+    rng = np.random.default_rng(rows + d)
+    x = rng.standard_normal(rows * d).astype(np.float32) * 3 + 0.5
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(d)).astype(np.float32)
+
+    def dev(a, extra=0):
+        t = torch.zeros(a.size + off, dtype=torch.float32, device="cuda")[off:]
+        t.copy_(torch.from_numpy(a))
+        return t
+    xd, gd, bd = dev(x), torch.from_numpy(g).cuda(), torch.from_numpy(b).cuda()
+    y = dev(np.zeros_like(x))
+    gbx.layernorm(xd, y, gd, bd, rows=rows, d=d)
+    yh, yl = dev(np.zeros_like(x)), dev(np.zeros_like(x))
+    gbx.split_tf32(y, yh, yl, n=x.size)
+    ph, pl = dev(np.zeros_like(x)), dev(np.zeros_like(x))
+    gbx.layernorm_pair(xd, ph, pl, gd, bd, rows=rows, d=d)
+    torch.cuda.synchronize()
+    assert torch.equal(ph.view(torch.int32), yh.view(torch.int32))
+    assert torch.equal(pl.view(torch.int32), yl.view(torch.int32))
+
+
 SHAPES = [
     # (M, N, K)
     (1, 8, 4),
@@ -136,6 +163,7 @@ SHAPES = [
     (257, 2304, 768),       # GPT-2 small QKV
     (96, 1600, 1600),       # GPT-2 XL proj (N = 6.25 tiles)
     (64, 768, 3072),        # GPT-2 small down (K = 3072)
+    (1100, 1600, 1600),     # CTA pairs (M >= 1024): M 256 tiles, the last one 76 rows
 ]
 
 
@@ -336,16 +364,14 @@ def test_linear_rejects_bad_arguments(gbx, cuda):
         gbx.linear(x, None, w, None, y, M=8, N=8, K=8, y_lo=y)
 
 
-def test_linear_kblock_32(cuda):
-    """The 128-byte-row variant (GBX_LINEAR_BK=32, two stages) on a few
-    shapes, in a fresh process (the setting is read once)."""
-    code = r"""
+_SUBPROCESS_CASES = r"""
 import importlib, sys
 import numpy as np, torch
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
 gbx = importlib.import_module("glassboxai-transformer_b200")
 import test_linear_gpu as t
-for M, N, K in ((129, 257, 52), (300, 1600, 1600), (64, 768, 3072)):
+for M, N, K, act, res in ((1, 8, 4, 0, 0), (37, 100, 20, 1, 0), (129, 257, 52, 0, 1), (300, 1600, 1600, 0, 1),
+                          (257, 2304, 768, 0, 0), (64, 768, 3072, 1, 0), (520, 6400, 1600, 1, 0)):
     rng = np.random.default_rng(M + N + K)
     x = rng.standard_normal((M, K)).astype(np.float32)
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
@@ -354,15 +380,36 @@ for M, N, K in ((129, 257, 52), (300, 1600, 1600), (64, 768, 3072)):
     xd, wd, bd, rd = (torch.from_numpy(a).cuda() for a in (x, w, b, r))
     xh, xl = t._split(gbx, torch, xd)
     wh, wl = t._split(gbx, torch, wd)
-    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    gbx.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=bd, resid=rd)
+    full, y = t._guarded(torch, M, N)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.linear(xh, xl, wh, wl, y, M=M, N=N, K=K, bias=bd, resid=rd if res else None, act=act, err_flag=err)
     torch.cuda.synchronize()
-    want, tol = t._expected(x, w, b, r, 0)
-    t._assert_within(y.cpu().numpy(), want, tol, f"BK=32 {M}x{N}x{K}")
+    assert int(err.item()) == 0
+    want, tol = t._expected(x, w, b, r if res else None, act)
+    t._assert_within(y.cpu().numpy(), want, tol, f"{M}x{N}x{K} act={act} resid={res}")
+    t._check_guards(full)
 print("ok")
 """
+
+
+def _run_cases(env_extra):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, GBX_LINEAR_BK="32")
-    out = subprocess.run([sys.executable, "-c", code, root, os.path.join(root, "tests")], env=env,
+    env = dict(os.environ, **env_extra)
+    out = subprocess.run([sys.executable, "-c", _SUBPROCESS_CASES, root, os.path.join(root, "tests")], env=env,
                          capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stdout + out.stderr
+
+
+def test_linear_cta_pairs_every_shape(cuda):
+    """The CTA-pair kernel (two SMs per M 256 tile, cta_group::2) forced on
+    for every shape, M = 1 included: tails in M (a whole second CTA of
+    out-of-range rows), N and K, and each epilogue."""
+    _run_cases({"GBX_LINEAR_PAIR": "1"})
+
+
+def test_linear_cta_pairs_kblock_32(cuda):
+    _run_cases({"GBX_LINEAR_PAIR": "1", "GBX_LINEAR_BK": "32"})
+
+
+def test_linear_single_cta_kblock_32(cuda):
+    _run_cases({"GBX_LINEAR_PAIR": "0", "GBX_LINEAR_BK": "32"})

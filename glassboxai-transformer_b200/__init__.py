@@ -21,7 +21,7 @@ LIB_PATH = os.path.join(HERE, "libgbx.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "gbx.h")
 
 DT_F32, DT_F16, DT_BF16 = 0, 1, 30
-EMBED_BAD_ID, EMBED_BAD_POS = 1, 2
+EMBED_BAD_ID, EMBED_BAD_POS, EMBED_TIMEOUT = 1, 2, 4
 
 STATUS = {0: "GBX_OK", 1: "GBX_EINVAL", 2: "GBX_EDTYPE", 3: "GBX_ERANGE", 4: "GBX_ECUDA",
           5: "GBX_EIO", 6: "GBX_ENOTFOUND", 7: "GBX_ENOMEM"}

@@ -1,5 +1,6 @@
 // tcgen05.cuh -- inline-PTX wrappers for the sm_100a tensor-core pipeline of
-// linear.cu: mbarriers with time-bounded waits, 2-D TMA tile loads (no
+// linear.cu: mbarriers with time-bounded waits, 2-D TMA tile loads and
+// untiled bulk copies (the latter also for embed.cu's staged gather; no
 // cluster multicast: every load targets this CTA's own shared memory), TMEM
 // allocation, tcgen05.mma (kind::tf32, one CTA), tcgen05.commit and
 // tcgen05.ld, and the shared-memory / instruction descriptors the MMA reads.
@@ -106,6 +107,23 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
             "r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
         : "memory");
+}
+
+// Adds `bytes` to the transaction count of the current phase of `bar`
+// without arriving (for copies issued by a thread before its arrive).
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Untiled bulk copy of `bytes` contiguous bytes from global memory into this
+// CTA's shared memory at dst (no cluster multicast); completion is signalled
+// on bar as transaction bytes.  src, dst and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 
 // ---------------------------------------------------------------- TMEM

@@ -49,8 +49,11 @@ enum {
 
 enum { GBX_DT_F32 = 0, GBX_DT_F16 = 1, GBX_DT_BF16 = 30 };
 
-/* Bits set in *err_flag by gbx_embed (device int32, OR-ed in). */
-enum { GBX_EMBED_BAD_ID = 1, GBX_EMBED_BAD_POS = 2 };
+/* Bits set in *err_flag by gbx_embed (device int32, OR-ed in).
+ * GBX_EMBED_TIMEOUT: a staged copy of table rows did not complete within one
+ * second; the rows it fed are left unwritten (the kernel returns without
+ * faulting). */
+enum { GBX_EMBED_BAD_ID = 1, GBX_EMBED_BAD_POS = 2, GBX_EMBED_TIMEOUT = 4 };
 
 /* Library version, major*10000 + minor*100 + patch. */
 int gbx_version(void);

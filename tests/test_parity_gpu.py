@@ -109,6 +109,57 @@ def test_embed_bit_exact(gbx, orc, cuda, wdt, pdt, d):
     _check_guards(full)
 
 
+@pytest.mark.parametrize("wdt,pdt", [(0, 0), (1, 1), (30, 30), (1, 0), (30, 1), (0, 30)])
+@pytest.mark.parametrize("d,n_tok", [(1600, 703), (768, 1367), (4096, 261)])
+def test_embed_staged_path_bit_exact(gbx, orc, cuda, wdt, pdt, d, n_tok):
+    """Launches of at least 2^20 elements whose table rows are a multiple of
+    16 bytes run the shared-memory staged kernel; the token counts leave a
+    ragged last CTA for every tokens-per-CTA the widths give."""
+    import torch
+    rng = np.random.default_rng(d + 7 * wdt + pdt)
+    V, C, S = 301, 1024, 512
+    assert n_tok * d >= 1 << 20
+    wte = _table(rng, V, d, wdt, 0.02)
+    wpe = _table(rng, C, d, pdt, 0.01)
+    ids = rng.integers(0, V, n_tok).astype(np.int32)
+    if wdt != 0:
+        for j, p in enumerate([0x8000, 0x7C01, 0xFC00, 0x0001, 0x83FF, 0xFFC1]):
+            wte[ids[j], (37 * j) % d] = p
+    if pdt != 0:
+        wpe[3, 5] = 0x8000
+    full, out = _guarded((n_tok, d), torch)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.embed(_t(ids, torch), _t(wte, torch), wdt, _t(wpe, torch), pdt, out, n_tok=n_tok, d=d, vocab=V,
+              n_ctx=C, seq=S, pos_off=3, err_flag=err)
+    ref, bad = orc.embed(ids, wte, wdt, wpe, pdt, d, V, C, seq=S, pos_off=3)
+    assert bad == 0 and int(err.item()) == 0
+    assert_bits_equal(out.cpu().numpy(), ref, f"staged embed {wdt}/{pdt} d={d}")
+    _check_guards(full)
+
+
+def test_embed_staged_path_out_of_range(gbx, orc, cuda):
+    """Out-of-range ids and positions (through pos_ids) on the staged kernel:
+    zero rows, both error bits, every other row exact."""
+    import torch
+    rng = np.random.default_rng(13)
+    V, C, d, n = 400, 900, 1600, 701
+    wte = _table(rng, V, d, 30, 0.02)
+    wpe = _table(rng, C, d, 30, 0.02)
+    ids = rng.integers(0, V, n).astype(np.int32)
+    pos = rng.integers(0, C, n).astype(np.int32)
+    ids[[0, 7, 300, 700]] = [V, -1, 1 << 30, V + 5]
+    pos[[1, 7, 301, 699]] = [C, -2, C + 100, -(1 << 30)]
+    full, out = _guarded((n, d), torch)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.embed(_t(ids, torch), _t(wte, torch), 30, _t(wpe, torch), 30, out, n_tok=n, d=d, vocab=V, n_ctx=C,
+              pos_ids=_t(pos, torch), err_flag=err)
+    ref, bad = orc.embed(ids, wte, 30, wpe, 30, d, V, C, pos_ids=pos)
+    assert bad == 7
+    assert int(err.item()) == (gbx.EMBED_BAD_ID | gbx.EMBED_BAD_POS)
+    assert_bits_equal(out.cpu().numpy(), ref, "staged embed with rejected rows")
+    _check_guards(full)
+
+
 def test_embed_f32_specials_canonical_nan(gbx, orc, cuda):
     import torch
     rng = np.random.default_rng(9)

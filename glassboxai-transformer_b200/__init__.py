@@ -52,6 +52,10 @@ SIGNATURES = {
     "gbx_bias_gelu": [_vp, _vp, _vp, _i64, _int, _vp],
     "gbx_softmax_rows": [_vp, _vp, _i64, _int, _vp],
     "gbx_attn_softmax_rows": [_vp, _vp, _i64, _int, _int, _int, _f, _int, _vp],
+    "gbx_attn_softmax_rows_pair": [_vp, _vp, _vp, _i64, _int, _int, _int, _f, _int, _vp],
+    "gbx_attn_scores": [_vp, _vp, _vp, _vp, _i64, _vp, _int, _int, _int, _int, _int, _vp, _vp],
+    "gbx_transpose_heads": [_vp, _i64, _vp, _int, _int, _int, _int, _vp],
+    "gbx_attn_values": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, _vp],
     "gbx_logits": [_vp, _i64, _vp, _int, _vp, _int, _int, _vp],
     "gbx_select_tokens": [_vp, _i64, _int, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
     "gbx_split_tf32": [_vp, _vp, _vp, _i64, _vp],
@@ -179,3 +183,27 @@ def linear(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, bias=None, resid=None, y_lo=No
     """y = act(x . w^T + bias) + resid on the tensor cores (tf32 pairs, see gbx.h)."""
     _check(lib().gbx_linear(_p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(resid), _p(y), _p(y_lo), M, N, K,
                             act, _p(err_flag), _stream(stream)))
+
+
+def attn_softmax_rows_pair(scores, probs_hi, probs_lo, *, rows, L, S, scale, q_off=0, causal=True, stream=None):
+    """attn_softmax_rows with the probabilities as a tf32 pair (attn_values' P operand)."""
+    _check(lib().gbx_attn_softmax_rows_pair(_p(scores), _p(probs_hi), _p(probs_lo), rows, L, S, q_off, scale,
+                                            1 if causal else 0, _stream(stream)))
+
+
+def attn_scores(q_hi, q_lo, k_hi, k_lo, dots, *, ld, B, S, H, hd, causal=True, err_flag=None, stream=None):
+    """dots[(b*H+h)*S*S + p*S + s] = q[b, p, head h] . k[b, s, head h] on the tensor cores."""
+    _check(lib().gbx_attn_scores(_p(q_hi), _p(q_lo), _p(k_hi), _p(k_lo), ld, _p(dots), B, S, H, hd,
+                                 1 if causal else 0, _p(err_flag), _stream(stream)))
+
+
+def transpose_heads(v, vt, *, ld, B, S, H, hd, stream=None):
+    """vt[((b*H+h)*hd + i)*S + s] = v[(b*S + s)*ld + h*hd + i]."""
+    _check(lib().gbx_transpose_heads(_p(v), ld, _p(vt), B, S, H, hd, _stream(stream)))
+
+
+def attn_values(p_hi, p_lo, vt_hi, vt_lo, out, *, ld_out, B, S, H, hd, out_lo=None, causal=True, err_flag=None,
+                stream=None):
+    """out[(b*S+p)*ld_out + h*hd + i] = sum_s P[b, h, p, s] vt[b, h, i, s] on the tensor cores."""
+    _check(lib().gbx_attn_values(_p(p_hi), _p(p_lo), _p(vt_hi), _p(vt_lo), _p(out), _p(out_lo), ld_out, B, S, H, hd,
+                                 1 if causal else 0, _p(err_flag), _stream(stream)))

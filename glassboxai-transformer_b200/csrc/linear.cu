@@ -101,6 +101,28 @@ struct LinearArgs {
     int act;
     int has_xlo;
     int has_wlo;
+    // Heads mode (the per-head attention products): tile t belongs to head
+    // z = t / tiles_per_z, z = b * H + h, and every operand is a 4-D box
+    // (k, row, head, sequence) of its tensor map; y of head z starts at
+    // b * syb + h * syh with rows ldy apart.  Plain mode: H 1, ldy N.
+    int H;
+    int tiles_per_z;
+    int64_t ldy;
+    int64_t syh;
+    int64_t syb;
+    int causal_tiles;   // tiles whose columns all exceed every row + q_off are not computed
+    int causal_k;       // a tile sums only k < (its last row + 1) + q_off
+    int q_off;
+    int x_head_major;   // 1: x's map orders its dimensions (k, head, row, sequence)
+    int w_head_major;
+    int w_box_rows;     // w rows per TMA box: the tile's, or fewer when N is narrow
+};
+
+struct TileInfo {
+    int mb, nb;    // row tile, column tile (within the head)
+    int h, b;      // head, sequence (0 in plain mode)
+    int kb_end;    // K blocks summed
+    bool live;     // false: the tile is skipped by every role
 };
 
 // Tile t -> (row tile, column tile): consecutive tiles sweep the column
@@ -108,10 +130,29 @@ struct LinearArgs {
 // from HBM once) and the weight matrix, which L2 largely holds.  (Grouping
 // 8-32 row tiles per column tile measured no faster on B200: the kernel is
 // bound by shared-memory traffic, not by L2 misses.)
-__device__ __forceinline__ void tile_coords(int t, const LinearArgs& a, int& mb, int& nb)
+template <int BK, bool PAIR, bool HEADS>
+__device__ __forceinline__ TileInfo tile_info(int t, const LinearArgs& a)
 {
-    mb = t / a.n_blocks;
-    nb = t - mb * a.n_blocks;
+    TileInfo ti;
+    int r = t;
+    ti.h = ti.b = 0;
+    if constexpr (HEADS) {
+        const int z = t / a.tiles_per_z;
+        r = t - z * a.tiles_per_z;
+        ti.b = z / a.H;
+        ti.h = z - ti.b * a.H;
+    }
+    ti.mb = r / a.n_blocks;
+    ti.nb = r - ti.mb * a.n_blocks;
+    ti.live = true;
+    ti.kb_end = a.k_blocks;
+    if constexpr (HEADS) {
+        // columns (keys) below rows_end are visible to some row of the tile
+        const int64_t rows_end = (int64_t)(ti.mb + 1) * LinCfg<BK, PAIR>::tile_rows + a.q_off;
+        if (a.causal_tiles && (int64_t)ti.nb * kLinBN >= rows_end) ti.live = false;
+        if (a.causal_k && rows_end < a.K) ti.kb_end = (int)((rows_end + BK - 1) / BK);
+    }
+    return ti;
 }
 
 __device__ __forceinline__ float epi_value(float acc, int n, int64_t row, const LinearArgs& a)
@@ -124,8 +165,10 @@ __device__ __forceinline__ float epi_value(float acc, int n, int64_t row, const 
 }
 
 // 16 accumulator columns of one output row: columns n .. n+15 (n < N).
+// yoff: the row's offset in y (row * N in plain mode); the residual is
+// always read at row * N + n.
 template <bool VEC>
-__device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, int n, const LinearArgs& a)
+__device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, int64_t yoff, int n, const LinearArgs& a)
 {
     const int64_t off = row * a.N;
     if (VEC) {
@@ -151,10 +194,10 @@ __device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, i
                 split_value(o.y, h.y, l.y);
                 split_value(o.z, h.z, l.z);
                 split_value(o.w, h.w, l.w);
-                *reinterpret_cast<float4*>(a.y + off + n + j) = h;
-                *reinterpret_cast<float4*>(a.y_lo + off + n + j) = l;
+                *reinterpret_cast<float4*>(a.y + yoff + n + j) = h;
+                *reinterpret_cast<float4*>(a.y_lo + yoff + n + j) = l;
             } else {
-                *reinterpret_cast<float4*>(a.y + off + n + j) = o;
+                *reinterpret_cast<float4*>(a.y + yoff + n + j) = o;
             }
         }
     } else {
@@ -165,16 +208,16 @@ __device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, i
             if (a.y_lo) {
                 float h, l;
                 split_value(o, h, l);
-                a.y[off + n + j] = h;
-                a.y_lo[off + n + j] = l;
+                a.y[yoff + n + j] = h;
+                a.y_lo[yoff + n + j] = l;
             } else {
-                a.y[off + n + j] = o;
+                a.y[yoff + n + j] = o;
             }
         }
     }
 }
 
-template <int BK, bool VEC, bool PAIR>
+template <int BK, bool VEC, bool PAIR, bool HEADS>
 __global__ void __launch_bounds__(kLinThreads, 1)
 linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constant__ CUtensorMap map_xl,
                      const __grid_constant__ CUtensorMap map_wh, const __grid_constant__ CUtensorMap map_wl,
@@ -195,7 +238,6 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int chunks = (a.k_blocks + C::chunk_blocks - 1) / C::chunk_blocks;   // per tile
     // PAIR: the barriers that count both CTAs (full, chunk_empty, drain) live
     // in the leader, rank 0; empty and chunk_full exist in both (the MMA
     // commit multicasts to the two)
@@ -239,24 +281,42 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
     if (warp == 0) {
         if (lane == 0) {
             // ---------------------------------------------------- producer
-            const uint32_t cta_bytes = (uint32_t)(C::a_bytes * (1 + a.has_xlo) + C::b_bytes * (1 + a.has_wlo));
+            const uint32_t cta_bytes =
+                (uint32_t)(C::a_bytes * (1 + a.has_xlo) + a.w_box_rows * C::row_bytes * (1 + a.has_wlo));
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued = 0;    // bit s: stage s has had a load issued
             uint32_t lastpar = 0;   // bit s: parity of the phase of its last load
             for (int t = unit; t < a.tiles && !*abort; t += units) {
-                int mb, nb;
-                tile_coords(t, a, mb, nb);
-                const int n_left = a.N - nb * kLinBN;
+                const TileInfo ti = tile_info<BK, PAIR, HEADS>(t, a);
+                if (!ti.live) continue;
+                const int n_left = a.N - ti.nb * kLinBN;
                 const int n_mma = n_left >= kLinBN ? kLinBN : (n_left + 15) & ~15;
-                const int y_x = mb * C::tile_rows + (int)rank * kLinBM;
-                const int y_w = nb * kLinBN + (PAIR ? (int)rank * (n_mma / 2) : 0);
-                for (int kb = 0; kb < a.k_blocks; ++kb) {
+                const int y_x = ti.mb * C::tile_rows + (int)rank * kLinBM;
+                const int y_w = ti.nb * kLinBN + (PAIR ? (int)rank * (n_mma / 2) : 0);
+                // 4-D boxes: (k, row, head, sequence), or (k, head, row, sequence)
+                const int x1 = a.x_head_major ? ti.h : y_x, x2 = a.x_head_major ? y_x : ti.h;
+                const int w1 = a.w_head_major ? ti.h : y_w, w2 = a.w_head_major ? y_w : ti.h;
+                for (int kb = 0; kb < ti.kb_end; ++kb) {
                     if (!tc::mbar_wait(empty0 + 8 * stage, phase ^ 1, abort, kLinWaitNs)) break;
                     const uint32_t full = full0 + 8 * stage;
                     const uint32_t base = smem0 + stage * C::stage_bytes;
                     const int x = kb * BK;
-                    if constexpr (PAIR) {
+                    if constexpr (PAIR && HEADS) {
+                        if (leader) tc::mbar_arrive_expect_tx(full, 2 * cta_bytes);
+                        const uint32_t fl = tc::mapa(full, 0);
+                        tc::tma_load_4d_pair(base, &map_xh, fl, x, x1, x2, ti.b);
+                        if (a.has_xlo) tc::tma_load_4d_pair(base + C::a_bytes, &map_xl, fl, x, x1, x2, ti.b);
+                        tc::tma_load_4d_pair(base + 2 * C::a_bytes, &map_wh, fl, x, w1, w2, ti.b);
+                        if (a.has_wlo)
+                            tc::tma_load_4d_pair(base + 2 * C::a_bytes + C::b_bytes, &map_wl, fl, x, w1, w2, ti.b);
+                    } else if constexpr (HEADS) {
+                        tc::mbar_arrive_expect_tx(full, cta_bytes);
+                        tc::tma_load_4d(base, &map_xh, full, x, x1, x2, ti.b);
+                        if (a.has_xlo) tc::tma_load_4d(base + C::a_bytes, &map_xl, full, x, x1, x2, ti.b);
+                        tc::tma_load_4d(base + 2 * C::a_bytes, &map_wh, full, x, w1, w2, ti.b);
+                        if (a.has_wlo) tc::tma_load_4d(base + 2 * C::a_bytes + C::b_bytes, &map_wl, full, x, w1, w2, ti.b);
+                    } else if constexpr (PAIR) {
                         if (leader) tc::mbar_arrive_expect_tx(full, 2 * cta_bytes);   // both CTAs' tiles
                         const uint32_t fl = tc::mapa(full, 0);
                         tc::tma_load_2d_pair(base, &map_xh, fl, x, y_x);
@@ -296,11 +356,12 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
             bool ok = true;
             for (int t = unit; t < a.tiles && ok; t += units) {
                 // the last column tile runs only as wide as N needs (a multiple of 16)
-                int mb, nb;
-                tile_coords(t, a, mb, nb);
-                const int n_left = a.N - nb * kLinBN;
+                const TileInfo ti = tile_info<BK, PAIR, HEADS>(t, a);
+                if (!ti.live) continue;
+                const int n_left = a.N - ti.nb * kLinBN;
                 const int n_mma = n_left >= kLinBN ? kLinBN : (n_left + 15) & ~15;
                 const uint32_t idesc = tc::idesc_tf32(C::tile_rows, n_mma);
+                const int chunks = (ti.kb_end + C::chunk_blocks - 1) / C::chunk_blocks;
                 for (int c = 0; c < chunks && ok; ++c) {
                     if (!tc::mbar_wait(cempty0 + 8 * buf, buf_phase ^ 1, abort, kLinWaitNs)) {
                         ok = false;
@@ -309,7 +370,7 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                     tc::fence_after_sync();
                     const uint32_t d = tmem + buf * kLinBN;
                     const int kb0 = c * C::chunk_blocks;
-                    const int kb1 = kb0 + C::chunk_blocks < a.k_blocks ? kb0 + C::chunk_blocks : a.k_blocks;
+                    const int kb1 = kb0 + C::chunk_blocks < ti.kb_end ? kb0 + C::chunk_blocks : ti.kb_end;
                     for (int kb = kb0; kb < kb1; ++kb) {
                         if (!tc::mbar_wait(full0 + 8 * stage, phase, abort, kLinWaitNs)) {
                             ok = false;
@@ -381,8 +442,10 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
         uint32_t buf_phase = 0;
         bool ok = true;
         for (int t = unit; t < a.tiles && ok; t += units) {
-            int mb, nb;
-            tile_coords(t, a, mb, nb);
+            const TileInfo ti = tile_info<BK, PAIR, HEADS>(t, a);
+            if (!ti.live) continue;
+            const int mb = ti.mb, nb = ti.nb;
+            const int chunks = (ti.kb_end + C::chunk_blocks - 1) / C::chunk_blocks;
             float acc[kLinEpiCols];
 #pragma unroll
             for (int j = 0; j < kLinEpiCols; ++j) acc[j] = 0.0f;
@@ -422,6 +485,8 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
             if (!ok) break;
             const int64_t row = (int64_t)mb * C::tile_rows + row_in_tile;
             const int n0 = nb * kLinBN + col0;
+            int64_t yoff = row * a.ldy;
+            if constexpr (HEADS) yoff += ti.b * a.syb + ti.h * a.syh;
             if (row < a.M) {
 #pragma unroll
                 for (int g = 0; g < kLinEpiCols / 16; ++g) {
@@ -429,7 +494,7 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                         float v[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) v[i] = acc[16 * g + i];
-                        epi_store16<VEC>(v, row, n0 + 16 * g, a);
+                        epi_store16<VEC>(v, row, yoff, n0 + 16 * g, a);
                     }
                 }
             }
@@ -477,6 +542,78 @@ linear_general_kernel(const float* __restrict__ xh, const float* __restrict__ xl
         } else {
             a.y[i] = o;
         }
+    }
+}
+
+// An operand of the heads mode: element (sequence b, head h, row r, k) at
+// base[b * sb + h * sh + r * ld + k], in elements.  head_major orders the
+// tensor map's dimensions (k, head, row, sequence) instead of (k, row, head,
+// sequence), so that the strides increase with the dimension (the Q and K
+// column blocks of a [tokens, 3d] QKV buffer: sh = hd < ld).
+struct HeadsOperand {
+    const float* hi;
+    const float* lo;
+    int64_t ld, sh, sb;
+    int rows;
+    bool head_major;
+};
+
+// General path of the heads mode (operands the tensor maps cannot describe):
+// one thread per output, the same three product terms, the same causal
+// limits at element granularity (outputs past the diagonal are not written).
+__global__ void __launch_bounds__(256)
+linear_heads_general_kernel(const HeadsOperand x, const HeadsOperand w, const LinearArgs a, int B)
+{
+    const int64_t per_z = a.M * (int64_t)a.N;
+    const int64_t total = per_z * a.H * B;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t z = i / per_z;
+        const int64_t r = i - z * per_z;
+        const int64_t m = r / a.N;
+        const int n = (int)(r - m * a.N);
+        const int64_t b = z / a.H, h = z - b * a.H;
+        if (a.causal_tiles && n > m + a.q_off) continue;
+        const int64_t kend = a.causal_k ? (m + a.q_off + 1 < a.K ? m + a.q_off + 1 : a.K) : a.K;
+        const int64_t xo = b * x.sb + h * x.sh + m * x.ld, wo = b * w.sb + h * w.sh + (int64_t)n * w.ld;
+        float acc = 0.0f;
+        for (int64_t k = 0; k < kend; ++k) {
+            acc = fmaf(x.hi[xo + k], w.hi[wo + k], acc);
+            if (w.lo) acc = fmaf(x.hi[xo + k], w.lo[wo + k], acc);
+            if (x.lo) acc = fmaf(x.lo[xo + k], w.hi[wo + k], acc);
+        }
+        const int64_t yo = b * a.syb + h * a.syh + m * a.ldy + n;
+        if (a.y_lo) {
+            float hv, lv;
+            split_value(acc, hv, lv);
+            a.y[yo] = hv;
+            a.y_lo[yo] = lv;
+        } else {
+            a.y[yo] = acc;
+        }
+    }
+}
+
+// vt[((b * H + h) * hd + i) * S + s] = v[(b * S + s) * ld + h * hd + i]:
+// the V block of each head transposed so that the attention output's
+// contraction index (the key position) is contiguous, as the tensor maps
+// read it.  32 x 32 tiles through shared memory; coalesced on both sides.
+__global__ void __launch_bounds__(256)
+transpose_heads_kernel(const float* __restrict__ v, int64_t ld, float* __restrict__ vt, int S, int H, int hd)
+{
+    __shared__ float tile[32][33];
+    const int z = blockIdx.z;
+    const int b = z / H, h = z - b * H;
+    const int s0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
+    const float* src = v + (int64_t)b * S * ld + (int64_t)h * hd;
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int sp = s0 + r, i = i0 + threadIdx.x;
+        if (sp < S && i < hd) tile[r][threadIdx.x] = src[(int64_t)sp * ld + i];
+    }
+    __syncthreads();
+    float* dst = vt + (int64_t)z * hd * S;
+    for (int r = threadIdx.y; r < 32; r += 8) {
+        const int i = i0 + r, sp = s0 + threadIdx.x;
+        if (i < hd && sp < S) dst[(int64_t)i * S + sp] = tile[threadIdx.x][r];
     }
 }
 
@@ -542,9 +679,50 @@ static int make_map(CUtensorMap* m, const float* base, int64_t rows, int K, int 
     return GBX_OK;
 }
 
-template <int BK, bool VEC, bool PAIR>
+// One plane (hi or lo) of a heads-mode operand as a 4-D map, boxes of
+// BK x box_rows (one head, one sequence) with the BK-wide swizzle.
+static int make_map4(CUtensorMap* m, const float* base, const HeadsOperand& op, int K, int H, int B, int box_rows,
+                     int BK)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return set_error(GBX_ECUDA, "gbx_attn: cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t e = sizeof(float);
+    cuuint64_t dims[4], strides[3];
+    cuuint32_t box[4];
+    dims[0] = (cuuint64_t)K;
+    dims[3] = (cuuint64_t)B;
+    strides[2] = (cuuint64_t)op.sb * e;
+    box[0] = (cuuint32_t)BK;
+    box[3] = 1;
+    if (op.head_major) {
+        dims[1] = (cuuint64_t)H;
+        dims[2] = (cuuint64_t)op.rows;
+        strides[0] = (cuuint64_t)op.sh * e;
+        strides[1] = (cuuint64_t)op.ld * e;
+        box[1] = 1;
+        box[2] = (cuuint32_t)box_rows;
+    } else {
+        dims[1] = (cuuint64_t)op.rows;
+        dims[2] = (cuuint64_t)H;
+        strides[0] = (cuuint64_t)op.ld * e;
+        strides[1] = (cuuint64_t)op.sh * e;
+        box[1] = (cuuint32_t)box_rows;
+        box[2] = 1;
+    }
+    if (B == 1) strides[2] = strides[1] * dims[2];   // unused; any valid stride
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GBX_EINVAL, "gbx_attn: tensor map rejected (CUresult %d)", (int)r);
+    return GBX_OK;
+}
+
+// hx / hw: the heads-mode operands (HEADS only; B sequences of a.H heads).
+template <int BK, bool VEC, bool PAIR, bool HEADS>
 static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo, LinearArgs a,
-                         cudaStream_t s)
+                         cudaStream_t s, const HeadsOperand* hx = nullptr, const HeadsOperand* hw = nullptr, int B = 1)
 {
     using C = LinCfg<BK, PAIR>;
     DeviceInfo di;
@@ -552,25 +730,42 @@ static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi
     if ((size_t)di.max_smem_optin < C::smem)
         return set_error(GBX_ERANGE, "gbx_linear: needs %zu bytes of shared memory per CTA", C::smem);
     const int64_t m_blocks = (a.M + C::tile_rows - 1) / C::tile_rows;
-    if (m_blocks * a.n_blocks > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: too many tiles");
+    const int64_t zs = HEADS ? (int64_t)a.H * B : 1;
+    if (m_blocks * a.n_blocks * zs > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: too many tiles");
     a.m_blocks = (int)m_blocks;
-    a.tiles = (int)(m_blocks * a.n_blocks);
+    a.tiles_per_z = (int)(m_blocks * a.n_blocks);
+    a.tiles = (int)(m_blocks * a.n_blocks * zs);
     a.k_blocks = (a.K + BK - 1) / BK;
+    a.w_box_rows = C::b_rows;
+    if (HEADS && a.n_blocks == 1) {   // a narrow N (a head's width): load only the rows the MMA reads
+        const int n16 = (a.N + 15) & ~15;
+        const int rows = PAIR ? n16 / 2 : n16;
+        if (rows < a.w_box_rows) a.w_box_rows = rows;
+    }
     CUtensorMap mxh, mxl, mwh, mwl;
     int rc;
-    if ((rc = make_map(&mxh, x_hi, a.M, a.K, C::a_rows, BK)) != GBX_OK) return rc;
-    if ((rc = make_map(&mwh, w_hi, a.N, a.K, C::b_rows, BK)) != GBX_OK) return rc;
-    if (a.has_xlo) {
-        if ((rc = make_map(&mxl, x_lo, a.M, a.K, C::a_rows, BK)) != GBX_OK) return rc;
-    } else {
-        mxl = mxh;   // never loaded
-    }
-    if (a.has_wlo) {
-        if ((rc = make_map(&mwl, w_lo, a.N, a.K, C::b_rows, BK)) != GBX_OK) return rc;
-    } else {
+    if constexpr (HEADS) {
+        if ((rc = make_map4(&mxh, hx->hi, *hx, a.K, a.H, B, C::a_rows, BK)) != GBX_OK) return rc;
+        if ((rc = make_map4(&mwh, hw->hi, *hw, a.K, a.H, B, a.w_box_rows, BK)) != GBX_OK) return rc;
+        mxl = mxh;
         mwl = mwh;
+        if (a.has_xlo && (rc = make_map4(&mxl, hx->lo, *hx, a.K, a.H, B, C::a_rows, BK)) != GBX_OK) return rc;
+        if (a.has_wlo && (rc = make_map4(&mwl, hw->lo, *hw, a.K, a.H, B, a.w_box_rows, BK)) != GBX_OK) return rc;
+    } else {
+        if ((rc = make_map(&mxh, x_hi, a.M, a.K, C::a_rows, BK)) != GBX_OK) return rc;
+        if ((rc = make_map(&mwh, w_hi, a.N, a.K, C::b_rows, BK)) != GBX_OK) return rc;
+        if (a.has_xlo) {
+            if ((rc = make_map(&mxl, x_lo, a.M, a.K, C::a_rows, BK)) != GBX_OK) return rc;
+        } else {
+            mxl = mxh;   // never loaded
+        }
+        if (a.has_wlo) {
+            if ((rc = make_map(&mwl, w_lo, a.N, a.K, C::b_rows, BK)) != GBX_OK) return rc;
+        } else {
+            mwl = mwh;
+        }
     }
-    auto k = linear_tf32x3_kernel<BK, VEC, PAIR>;
+    auto k = linear_tf32x3_kernel<BK, VEC, PAIR, HEADS>;
     // per device, so set on every call (a host-side attribute write)
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::smem) != cudaSuccess)
         return set_error(GBX_ECUDA, "gbx_linear: shared-memory attribute refused");
@@ -678,13 +873,18 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     a.act = act;
     a.has_xlo = x_lo != nullptr;
     a.has_wlo = w_lo != nullptr;
+    a.H = 1;
+    a.ldy = N;
+    a.syh = a.syb = 0;
+    a.causal_tiles = a.causal_k = a.q_off = 0;
+    a.x_head_major = a.w_head_major = 0;
     const bool vec = N % 4 == 0 && aligned16(y) && (!y_lo || aligned16(y_lo)) && (!resid || aligned16(resid)) &&
                      (!bias || aligned16(bias));
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const bool tma_ok = K % 4 == 0 && aligned16(x_hi) && aligned16(w_hi) && (!x_lo || aligned16(x_lo)) &&
                         (!w_lo || aligned16(w_lo));
     if (!tma_ok) {
-        a.m_blocks = a.tiles = a.k_blocks = 0;   // unused by the general kernel
+        a.m_blocks = a.tiles = a.k_blocks = a.tiles_per_z = a.w_box_rows = 0;   // unused by the general kernel
         const int grid = persistent_grid(linear_general_kernel, 256, 0, (M * N + 255) / 256, 8);
         if (grid < 1) return GBX_ECUDA;
         linear_general_kernel<<<grid, 256, 0, s>>>(x_hi, x_lo, w_hi, w_lo, a);
@@ -692,7 +892,7 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     }
     const int pm = linear_pair_mode();
     const bool pair = pm == 1 || (pm != 0 && M >= kLinPairMinRows);
-#define GBX_LIN(BKV, VECV, PAIRV) launch_linear<BKV, VECV, PAIRV>(x_hi, x_lo, w_hi, w_lo, a, s)
+#define GBX_LIN(BKV, VECV, PAIRV) launch_linear<BKV, VECV, PAIRV, false>(x_hi, x_lo, w_hi, w_lo, a, s)
     if (linear_bk() == 32) {
         if (pair) return vec ? GBX_LIN(32, true, true) : GBX_LIN(32, false, true);
         return vec ? GBX_LIN(32, true, false) : GBX_LIN(32, false, false);
@@ -700,4 +900,106 @@ extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_h
     if (pair) return vec ? GBX_LIN(16, true, true) : GBX_LIN(16, false, true);
     return vec ? GBX_LIN(16, true, false) : GBX_LIN(16, false, false);
 #undef GBX_LIN
+}
+
+// ------------------------------------------------------------------ attention
+// y[z] = x[z] . w[z]^T for every head z = b * H + h of B sequences, on the
+// heads mode of the tensor-core kernel (or its general path).
+static int heads_gemm(const char* what, const HeadsOperand& x, const HeadsOperand& w, float* y, float* y_lo,
+                      int64_t ldy, int64_t syh, int64_t syb, int B, int H, int M, int N, int K, int causal_tiles,
+                      int causal_k, int* err_flag, cudaStream_t s)
+{
+    LinearArgs a;
+    a.bias = nullptr;
+    a.resid = nullptr;
+    a.y = y;
+    a.y_lo = y_lo;
+    a.err = err_flag;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.n_blocks = (N + kLinBN - 1) / kLinBN;
+    a.act = GBX_ACT_NONE;
+    a.has_xlo = x.lo != nullptr;
+    a.has_wlo = w.lo != nullptr;
+    a.H = H;
+    a.ldy = ldy;
+    a.syh = syh;
+    a.syb = syb;
+    a.causal_tiles = causal_tiles;
+    a.causal_k = causal_k;
+    a.q_off = 0;
+    a.x_head_major = x.head_major;
+    a.w_head_major = w.head_major;
+    auto al16 = [](const void* p) { return p == nullptr || aligned16(p); };
+    auto st4 = [](const HeadsOperand& o) { return o.ld % 4 == 0 && o.sh % 4 == 0 && o.sb % 4 == 0; };
+    const bool tma_ok = K % 4 == 0 && st4(x) && st4(w) && al16(x.hi) && al16(x.lo) && al16(w.hi) && al16(w.lo);
+    const bool vec = N % 4 == 0 && ldy % 4 == 0 && syh % 4 == 0 && syb % 4 == 0 && al16(y) && al16(y_lo);
+    if (!tma_ok) {
+        a.m_blocks = a.tiles = a.k_blocks = a.tiles_per_z = a.w_box_rows = 0;
+        const int64_t total = (int64_t)B * H * M * N;
+        const int grid = persistent_grid(linear_heads_general_kernel, 256, 0, (total + 255) / 256, 8);
+        if (grid < 1) return GBX_ECUDA;
+        linear_heads_general_kernel<<<grid, 256, 0, s>>>(x, w, a, B);
+        return check_launch(what);
+    }
+    const int pm = linear_pair_mode();
+    const bool pair = pm == 1 || (pm != 0 && M >= kLinPairMinRows);
+#define GBX_HEADS(VECV, PAIRV) launch_linear<16, VECV, PAIRV, true>(x.hi, x.lo, w.hi, w.lo, a, s, &x, &w, B)
+    if (pair) return vec ? GBX_HEADS(true, true) : GBX_HEADS(false, true);
+    return vec ? GBX_HEADS(true, false) : GBX_HEADS(false, false);
+#undef GBX_HEADS
+}
+
+static int heads_dims(const char* what, int B, int S, int H, int hd)
+{
+    if (B <= 0 || S <= 0 || H <= 0 || hd <= 0) return set_error(GBX_EINVAL, "%s: B=%d S=%d H=%d hd=%d", what, B, S, H, hd);
+    if ((int64_t)B * H * S * S > ((int64_t)1 << 40) || (int64_t)B * H > 65535)
+        return set_error(GBX_ERANGE, "%s: B=%d H=%d S=%d too large", what, B, H, S);
+    return GBX_OK;
+}
+
+extern "C" int gbx_attn_scores(const float* q_hi, const float* q_lo, const float* k_hi, const float* k_lo, int64_t ld,
+                               float* dots, int B, int S, int H, int hd, int causal, int* err_flag,
+                               gbx_stream_t stream)
+{
+    if (int rc = heads_dims("gbx_attn_scores", B, S, H, hd)) return rc;
+    if (ld < (int64_t)H * hd) return set_error(GBX_EINVAL, "gbx_attn_scores: ld=%lld < H*hd", (long long)ld);
+    if (!q_hi || !k_hi || !dots) return set_error(GBX_EINVAL, "gbx_attn_scores: null pointer");
+    if ((const float*)dots == q_hi || (const float*)dots == k_hi || (q_lo && (const float*)dots == q_lo) ||
+        (k_lo && (const float*)dots == k_lo))
+        return set_error(GBX_EINVAL, "gbx_attn_scores: dots aliases an operand");
+    const HeadsOperand x{q_hi, q_lo, ld, hd, (int64_t)S * ld, S, true};
+    const HeadsOperand w{k_hi, k_lo, ld, hd, (int64_t)S * ld, S, true};
+    return heads_gemm("gbx_attn_scores", x, w, dots, nullptr, S, (int64_t)S * S, (int64_t)H * S * S, B, H, S, S, hd,
+                      causal ? 1 : 0, 0, err_flag, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gbx_attn_values(const float* p_hi, const float* p_lo, const float* vt_hi, const float* vt_lo,
+                               float* out, float* out_lo, int64_t ld_out, int B, int S, int H, int hd, int causal,
+                               int* err_flag, gbx_stream_t stream)
+{
+    if (int rc = heads_dims("gbx_attn_values", B, S, H, hd)) return rc;
+    if (ld_out < (int64_t)H * hd) return set_error(GBX_EINVAL, "gbx_attn_values: ld_out=%lld < H*hd", (long long)ld_out);
+    if (!p_hi || !vt_hi || !out) return set_error(GBX_EINVAL, "gbx_attn_values: null pointer");
+    if (out_lo == out || (const float*)out == p_hi || (const float*)out == vt_hi || (p_lo && (const float*)out == p_lo) ||
+        (vt_lo && (const float*)out == vt_lo))
+        return set_error(GBX_EINVAL, "gbx_attn_values: out aliases an operand");
+    const HeadsOperand x{p_hi, p_lo, S, (int64_t)S * S, (int64_t)H * S * S, S, false};
+    const HeadsOperand w{vt_hi, vt_lo, S, (int64_t)hd * S, (int64_t)H * hd * S, hd, false};
+    return heads_gemm("gbx_attn_values", x, w, out, out_lo, ld_out, hd, (int64_t)S * ld_out, B, H, S, hd, S, 0,
+                      causal ? 1 : 0, err_flag, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gbx_transpose_heads(const float* v, int64_t ld, float* vt, int B, int S, int H, int hd,
+                                   gbx_stream_t stream)
+{
+    if (int rc = heads_dims("gbx_transpose_heads", B, S, H, hd)) return rc;
+    if (ld < (int64_t)H * hd) return set_error(GBX_EINVAL, "gbx_transpose_heads: ld=%lld < H*hd", (long long)ld);
+    if (!v || !vt) return set_error(GBX_EINVAL, "gbx_transpose_heads: null pointer");
+    if ((const float*)vt == v) return set_error(GBX_EINVAL, "gbx_transpose_heads: vt aliases v");
+    const dim3 grid((unsigned)((S + 31) / 32), (unsigned)((hd + 31) / 32), (unsigned)(B * H));
+    if (grid.y > 65535) return set_error(GBX_ERANGE, "gbx_transpose_heads: hd=%d", hd);
+    transpose_heads_kernel<<<grid, dim3(32, 8), 0, reinterpret_cast<cudaStream_t>(stream)>>>(v, ld, vt, S, H, hd);
+    return check_launch("gbx_transpose_heads");
 }

@@ -8,14 +8,16 @@
 //   gbx_embed                              h = wte[ids] + wpe[pos]          (:805-815)
 //   for each layer l:
 //     gbx_layernorm_pair                   ln = LN1(h), as a tf32 pair     (:827-828)
-//     gbx_linear                           qkv = ln . Wqkv^T + b_qkv       (:830-832)
-//     cuBLAS (per sequence, batched over heads)
-//                                          raw[h] = Q_h . K_h^T            (:834-837, without
+//     gbx_linear                           qkv = ln . Wqkv^T + b_qkv, as a tf32 pair (:830-832)
+//     per group of sequences, every head in one launch each:
+//       gbx_attn_scores                    raw[b][h] = Q_bh . K_bh^T, causal tiles only
+//                                                                          (:834-837, without
 //                                                                          the scale and mask)
-//     gbx_attn_softmax_rows                P = softmax(mask(raw / sqrt(hd)))  (:220-229, :839-842)
-//     cuBLAS (per sequence, batched over heads)
-//                                          attn_h = P_h . V_h              (:844-846)
-//     gbx_split_tf32, gbx_linear           h += attn . Wproj^T + b_proj    (:848-852, the
+//       gbx_attn_softmax_rows_pair         P = softmax(mask(raw / sqrt(hd))), as a tf32 pair
+//                                                                          (:220-229, :839-842)
+//       gbx_transpose_heads (hi, lo)       Vt[b][h] = V_bh^T
+//       gbx_attn_values                    attn_bh = P_bh . V_bh, as a tf32 pair (:844-846)
+//     gbx_linear                           h += attn . Wproj^T + b_proj    (:848-852, the
 //                                                                          residual in the epilogue)
 //     gbx_layernorm_pair                   ln = LN2(h), as a tf32 pair     (:866-868)
 //     gbx_linear                           up = GELU(ln . Wup^T + b_up), as a tf32 pair
@@ -26,20 +28,21 @@
 //   gbx_logits                             logits = last . wte^T           (:898-900)
 //   (nextToken) gbx_select_tokens          argmax / temperature sampling   (:994-1028)
 //
-// The weight contractions run on the tcgen05 tensor cores (gbx_linear) with
-// every operand as a tf32 pair: each product within ~2^-21 of fp32's, fp32
-// sums, so they differ from the reference's sequential GEMV sums by rounding
-// of the same order as a change of summation order.  Weights are split once
-// at load; a weight read from an f16 or bf16 tensor is exact in tf32 and
-// needs no low part.  The per-head attention products are fp32 cuBLAS
-// (CUBLAS_COMPUTE_32F, no TF32).  Activation buffers grow to the largest
-// call (like allocateBuffers, :770-787) and are reused.
+// Every contraction, the weight products (gbx_linear) and the per-head
+// attention products (gbx_attn_scores, gbx_attn_values), runs on the tcgen05
+// tensor cores with every operand as a tf32 pair: each product within
+// ~2^-21 of fp32's, fp32 sums, so they differ from the reference's
+// sequential GEMV sums by rounding of the same order as a change of
+// summation order.  Weights are split once at load; a weight read from an
+// f16 or bf16 tensor is exact in tf32 and needs no low part.  Activation
+// buffers grow to the largest call (like allocateBuffers, :770-787) and are
+// reused; the attention scores of at most kScoreGroupFloats floats are held
+// at a time (sequences are taken in groups that fit).
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <random>
 
-#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include "gbx_model.hpp"
@@ -47,6 +50,10 @@
 namespace gbx {
 
 namespace {
+
+// attention scores held at once: 2^28 floats (1 GiB), and as much again for
+// the low half of the probabilities
+constexpr int64_t kScoreGroupFloats = (int64_t)1 << 28;
 
 struct DevBuf {
     float* p = nullptr;
@@ -75,11 +82,12 @@ struct DevBuf {
 }  // namespace
 
 struct TransformerModel::Impl {
-    cublasHandle_t blas = nullptr;
     cudaStream_t stream = nullptr;
     int device = -1;
-    // activations (ln, attn and up hold the hi half of a tf32 pair, *_lo the low half)
-    DevBuf h, ln, ln_lo, qkv, scores, attn, attn_lo, up, up_lo, last_h, last_y, logits;
+    // activations (ln, qkv, scores (as probabilities), vt, attn and up hold
+    // the hi half of a tf32 pair, *_lo the low half)
+    DevBuf h, ln, ln_lo, qkv, qkv_lo, scores, probs_lo, vt, vt_lo, attn, attn_lo, up, up_lo, last_h, last_y, logits;
+    int score_group = 1;   // sequences per attention launch
     int32_t* ids = nullptr;
     size_t ids_n = 0;
     int32_t* err = nullptr;
@@ -111,7 +119,8 @@ struct TransformerModel::Impl {
 
     ~Impl()
     {
-        for (DevBuf* b : {&h, &ln, &ln_lo, &qkv, &scores, &attn, &attn_lo, &up, &up_lo, &last_h, &last_y, &logits})
+        for (DevBuf* b : {&h, &ln, &ln_lo, &qkv, &qkv_lo, &scores, &probs_lo, &vt, &vt_lo, &attn, &attn_lo, &up, &up_lo,
+                          &last_h, &last_y, &logits})
             b->release();
         for (float* p : owned) cudaFree(p);
         if (ids) cudaFree(ids);
@@ -119,7 +128,6 @@ struct TransformerModel::Impl {
         if (sel_ids) cudaFree(sel_ids);
         if (sel_logit) cudaFree(sel_logit);
         if (sel_u) cudaFree(sel_u);
-        if (blas) cublasDestroy(blas);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -145,9 +153,6 @@ bool TransformerModel::loadModel(const std::string& ggufPath)
     Impl& m = *impl_;
     if (cudaGetDevice(&m.device) != cudaSuccess) return fail("no CUDA device");
     if (cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
-    if (cublasCreate(&m.blas) != CUBLAS_STATUS_SUCCESS) return fail("cublasCreate failed");
-    cublasSetStream(m.blas, m.stream);
-    cublasSetMathMode(m.blas, CUBLAS_DEFAULT_MATH);   // fp32 SGEMM; TF32 is never enabled
     if (cudaMalloc(&m.err, sizeof(int32_t)) != cudaSuccess || cudaMalloc(&m.sel_ids, 2 * sizeof(int32_t)) != cudaSuccess ||
         cudaMalloc(&m.sel_logit, sizeof(float)) != cudaSuccess || cudaMalloc(&m.sel_u, sizeof(double)) != cudaSuccess)
         return fail("cudaMalloc");
@@ -239,8 +244,14 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
 {
     Impl& m = *impl_;
     const int64_t d = embedDim_, F = ffnDim_, B = tokens / seq;
+    const int64_t per_seq = (int64_t)numHeads_ * seq * seq;
+    int64_t G = kScoreGroupFloats / per_seq;
+    G = G < 1 ? 1 : (G > B ? B : G);
+    m.score_group = (int)G;
     const bool ok = m.h.ensure(tokens * d) && m.ln.ensure(tokens * d) && m.ln_lo.ensure(tokens * d) &&
-                    m.qkv.ensure(tokens * 3 * d) && m.scores.ensure((size_t)numHeads_ * seq * seq) &&
+                    m.qkv.ensure(tokens * 3 * d) && m.qkv_lo.ensure(tokens * 3 * d) &&
+                    m.scores.ensure((size_t)(G * per_seq)) && m.probs_lo.ensure((size_t)(G * per_seq)) &&
+                    m.vt.ensure((size_t)(G * seq * d)) && m.vt_lo.ensure((size_t)(G * seq * d)) &&
                     m.attn.ensure(tokens * d) && m.attn_lo.ensure(tokens * d) && m.up.ensure(tokens * F) &&
                     m.up_lo.ensure(tokens * F) && m.last_h.ensure(B * d) && m.last_y.ensure(B * d) &&
                     m.logits.ensure((size_t)B * vocab_);
@@ -323,7 +334,7 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
 {
     Impl& m = *impl_;
     err_.clear();
-    if (!loader_.isLoaded() || !m.blas) return fail("model not loaded");
+    if (!loader_.isLoaded() || !m.stream) return fail("model not loaded");
     if (batch <= 0 || tokenIDs.empty() || tokenIDs.size() % (size_t)batch)
         return fail("forward: need batch > 0 sequences of equal, non-zero length");
     const int64_t N = (int64_t)tokenIDs.size();
@@ -337,16 +348,11 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
     if (!ensureBuffers(N, S)) return false;
 
     const int d = embedDim_, H = numHeads_, hd = headDim_, F = ffnDim_, V = vocab_;
-    const float one = 1.0f, zero = 0.0f;
     cudaStream_t st = m.stream;
     gbx_stream_t gs = reinterpret_cast<gbx_stream_t>(st);
     int rc = GBX_OK;
-    bool blas_ok = true;
     auto check = [&](int r) {
         if (rc == GBX_OK && r != GBX_OK) rc = r;
-    };
-    auto blas = [&](cublasStatus_t s) {
-        if (s != CUBLAS_STATUS_SUCCESS) blas_ok = false;
     };
     // y[M, Nout] = act(x . W^T + bias) + resid on the tensor cores, x and W as tf32 pairs
     auto linear = [&](const float* xh, const float* xl, const Impl::Pair& W, const float* bias, const float* resid,
@@ -360,30 +366,31 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
     check(gbx_embed(m.ids, m.wte, m.wte_dt, m.wpe, m.wpe_dt, nullptr, m.h.p, N, S, 0, d, V, nCtx_, m.err, gs));
 
     const float scale = sqrtf((float)hd);   // transformer.cu:836
-    for (int l = 0; l < numLayers_ && rc == GBX_OK && blas_ok; ++l) {
+    for (int l = 0; l < numLayers_ && rc == GBX_OK; ++l) {
         const Impl::Layer& L = m.layers[l];
         const Impl::LayerW& W = m.wpairs[l];
         check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
-        linear(m.ln.p, m.ln_lo.p, W.qkv, L.qkv_b, nullptr, m.qkv.p, nullptr, N, 3 * d, d, GBX_ACT_NONE);
-        for (int b = 0; b < batch; ++b) {
-            const float* q = m.qkv.p + (int64_t)b * S * 3 * d;
-            const float* k = q + d;
-            const float* v = q + 2 * d;
-            // raw[h][p][s] = sum_i Q[p, h*hd+i] K[s, h*hd+i]
-            blas(cublasSgemmStridedBatched(m.blas, CUBLAS_OP_T, CUBLAS_OP_N, S, S, hd, &one, k, 3 * d, hd, q, 3 * d,
-                                           hd, &zero, m.scores.p, S, (int64_t)S * S, H));
-            check(gbx_attn_softmax_rows(m.scores.p, m.scores.p, (int64_t)H * S, S, S, 0, scale, 1, gs));
-            // attn[p, h*hd+i] = sum_s P[h][p][s] V[s, h*hd+i]
-            blas(cublasSgemmStridedBatched(m.blas, CUBLAS_OP_N, CUBLAS_OP_N, hd, S, S, &one, v, 3 * d, hd, m.scores.p,
-                                           S, (int64_t)S * S, &zero, m.attn.p + (int64_t)b * S * d, d, hd, H));
+        linear(m.ln.p, m.ln_lo.p, W.qkv, L.qkv_b, nullptr, m.qkv.p, m.qkv_lo.p, N, 3 * d, d, GBX_ACT_NONE);
+        for (int b0 = 0; b0 < batch; b0 += m.score_group) {
+            const int g = batch - b0 < m.score_group ? batch - b0 : m.score_group;
+            const float* qh = m.qkv.p + (int64_t)b0 * S * 3 * d;
+            const float* ql = m.qkv_lo.p + (int64_t)b0 * S * 3 * d;
+            // raw[b][h][p][s] = sum_i Q[b, p, h*hd+i] K[b, s, h*hd+i] (s <= p)
+            check(gbx_attn_scores(qh, ql, qh + d, ql + d, 3 * d, m.scores.p, g, S, H, hd, 1, m.err, gs));
+            check(gbx_attn_softmax_rows_pair(m.scores.p, m.scores.p, m.probs_lo.p, (int64_t)g * H * S, S, S, 0, scale,
+                                             1, gs));
+            check(gbx_transpose_heads(qh + 2 * d, 3 * d, m.vt.p, g, S, H, hd, gs));
+            check(gbx_transpose_heads(ql + 2 * d, 3 * d, m.vt_lo.p, g, S, H, hd, gs));
+            // attn[b, p, h*hd+i] = sum_s P[b][h][p][s] V[b, s, h*hd+i]
+            check(gbx_attn_values(m.scores.p, m.probs_lo.p, m.vt.p, m.vt_lo.p, m.attn.p + (int64_t)b0 * S * d,
+                                  m.attn_lo.p + (int64_t)b0 * S * d, d, g, S, H, hd, 1, m.err, gs));
         }
-        check(gbx_split_tf32(m.attn.p, m.attn.p, m.attn_lo.p, N * d, gs));
         linear(m.attn.p, m.attn_lo.p, W.proj, L.proj_b, m.h.p, m.h.p, nullptr, N, d, d, GBX_ACT_NONE);
         check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln2_g, L.ln2_b, N, d, 1e-5f, gs));
         linear(m.ln.p, m.ln_lo.p, W.up, L.up_b, nullptr, m.up.p, m.up_lo.p, N, F, d, GBX_ACT_GELU);
         linear(m.up.p, m.up_lo.p, W.down, L.down_b, m.h.p, m.h.p, nullptr, N, d, F, GBX_ACT_NONE);
     }
-    if (rc == GBX_OK && blas_ok) {
+    if (rc == GBX_OK) {
         // each sequence's last row of h, then ln_f
         const size_t pitch = (size_t)S * d * sizeof(float);
         const size_t row = (size_t)d * sizeof(float);
@@ -394,11 +401,9 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
         check(gbx_logits(m.last_y.p, batch, m.wte, m.wte_dt, m.logits.p, V, d, gs));
     }
     int32_t err_host = 0;
-    if (rc == GBX_OK && blas_ok &&
-        cudaMemcpyAsync(&err_host, m.err, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    if (rc == GBX_OK && cudaMemcpyAsync(&err_host, m.err, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
         rc = GBX_ECUDA;
     if (cudaStreamSynchronize(st) != cudaSuccess && rc == GBX_OK) rc = GBX_ECUDA;
-    if (!blas_ok) return fail("cuBLAS call failed");
     if (rc != GBX_OK) return fail(std::string(gbx_status_string(rc)) + ": " + gbx_last_error());
     if (err_host & GBX_LINEAR_TIMEOUT) return fail("a tensor-core contraction timed out (its output is incomplete)");
     if (err_host) return fail("embedding reported out-of-range ids or positions");

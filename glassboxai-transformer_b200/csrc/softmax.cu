@@ -23,6 +23,7 @@
 // Because max is exact and expf is the same CUDA function, every e is
 // bit-identical to the reference's; only the order of the sum differs.
 #include "rows.cuh"
+#include "tf32.cuh"
 
 namespace gbx {
 
@@ -44,9 +45,11 @@ struct ScoreEpilogue {
 };
 
 // POW2: scale is a power of two, so raw / scale == raw * (1/scale) exactly.
-template <int TPR, int V4, bool ATTN, bool POW2>
+// PAIR_OUT: out and out_lo receive the tf32 pair of each probability
+// (tf32.cuh), the operand form of the attention-output contraction.
+template <int TPR, int V4, bool ATTN, bool POW2, bool PAIR_OUT>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads)
-softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep)
+softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep)
 {
     grid_dependency_wait();   // see launch_row_kernel
     allow_dependents();
@@ -120,18 +123,27 @@ softmax_vec_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilog
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
             const int c = k * TPR + lane;
-            if (c < n4)
-                st_stream(out + off + 4 * c, make_float4(div_by(v[k].x, s, r), div_by(v[k].y, s, r),
-                                                         div_by(v[k].z, s, r), div_by(v[k].w, s, r)));
+            if (c < n4) {
+                const float4 q = make_float4(div_by(v[k].x, s, r), div_by(v[k].y, s, r), div_by(v[k].z, s, r),
+                                             div_by(v[k].w, s, r));
+                if constexpr (PAIR_OUT) {
+                    float4 hi, lo;
+                    split4(q, hi, lo);
+                    st_stream(out + off + 4 * c, hi);
+                    st_stream(out_lo + off + 4 * c, lo);
+                } else {
+                    st_stream(out + off + 4 * c, q);
+                }
+            }
         }
     }
 }
 
 // General path (any L, any alignment, rows longer than the register path):
 // one CTA per row, the reference's three passes with shuffle reductions.
-template <bool ATTN>
+template <bool ATTN, bool PAIR_OUT>
 __global__ void __launch_bounds__(kGeneralCTA)
-softmax_general_kernel(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep)
+softmax_general_kernel(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep)
 {
     __shared__ float red[2][kGeneralCTA / 32];
     const float rscale = ATTN ? 1.0f / ep.scale : 1.0f;
@@ -154,7 +166,17 @@ softmax_general_kernel(const float* in, float* out, int64_t rows, int L, ScoreEp
         }
         s = block_sum(s, red[1]);
         const float r = 1.0f / s;
-        for (int i = threadIdx.x; i < L; i += kGeneralCTA) orow[i] = div_by(orow[i], s, r);
+        for (int i = threadIdx.x; i < L; i += kGeneralCTA) {
+            const float q = div_by(orow[i], s, r);
+            if constexpr (PAIR_OUT) {
+                float hv, lv;
+                split_value(q, hv, lv);
+                orow[i] = hv;
+                out_lo[row * L + i] = lv;
+            } else {
+                orow[i] = q;
+            }
+        }
         __syncthreads();
     }
 }
@@ -165,37 +187,38 @@ static bool is_pow2(float x)
     return x > 0.0f && frexpf(x, &e) == 0.5f;
 }
 
-template <int TPR, int V4, bool ATTN>
-static int launch_softmax_vec(const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep,
+template <int TPR, int V4, bool ATTN, bool PAIR_OUT>
+static int launch_softmax_vec(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep,
                               cudaStream_t stream)
 {
     const int64_t grid = row_grid<TPR>(rows);
     if (grid < 0) return GBX_ERANGE;
     if (ATTN && is_pow2(ep.scale))
-        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, true>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads), 0,
-                          stream, in, out, rows, L, ep);
+        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, true, PAIR_OUT>, dim3((unsigned)grid),
+                          dim3(RowCTA<TPR>::threads), 0, stream, in, out, out_lo, rows, L, ep);
     else
-        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, false>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads),
-                          0, stream, in, out, rows, L, ep);
+        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, false, PAIR_OUT>, dim3((unsigned)grid),
+                          dim3(RowCTA<TPR>::threads), 0, stream, in, out, out_lo, rows, L, ep);
     return GBX_OK;
 }
 
-template <bool ATTN>
-static int launch_softmax(const char* what, const float* in, float* out, int64_t rows, int L, ScoreEpilogue ep,
-                          cudaStream_t s)
+template <bool ATTN, bool PAIR_OUT>
+static int launch_softmax(const char* what, const float* in, float* out, float* out_lo, int64_t rows, int L,
+                          ScoreEpilogue ep, cudaStream_t s)
 {
     RowShape shape;
     int rc;
     // the vector path numbers rows in 32 bits for the causal position
-    if (L % 4 == 0 && aligned16(in) && aligned16(out) && row_shape(L / 4, &shape) && rows <= 0xffffffffLL) {
-#define GBX_SM_CALL(T, V) launch_softmax_vec<T, V, ATTN>(in, out, rows, L, ep, s)
+    if (L % 4 == 0 && aligned16(in) && aligned16(out) && (!PAIR_OUT || aligned16(out_lo)) &&
+        row_shape(L / 4, &shape) && rows <= 0xffffffffLL) {
+#define GBX_SM_CALL(T, V) launch_softmax_vec<T, V, ATTN, PAIR_OUT>(in, out, out_lo, rows, L, ep, s)
         rc = GBX_ROW_DISPATCH(shape, GBX_SM_CALL, GBX_ERANGE);
 #undef GBX_SM_CALL
         if (rc != GBX_OK) return set_error(rc, "%s: rows=%lld L=%d out of range", what, (long long)rows, L);
     } else {
-        const int grid = persistent_grid(softmax_general_kernel<ATTN>, kGeneralCTA, 0, rows, 4);
+        const int grid = persistent_grid(softmax_general_kernel<ATTN, PAIR_OUT>, kGeneralCTA, 0, rows, 4);
         if (grid < 1) return GBX_ECUDA;
-        softmax_general_kernel<ATTN><<<grid, kGeneralCTA, 0, s>>>(in, out, rows, L, ep);
+        softmax_general_kernel<ATTN, PAIR_OUT><<<grid, kGeneralCTA, 0, s>>>(in, out, out_lo, rows, L, ep);
     }
     return check_launch(what);
 }
@@ -210,7 +233,8 @@ extern "C" int gbx_softmax_rows(const float* in, float* out, int64_t rows, int L
     if (rows == 0) return GBX_OK;
     if (!in || !out) return set_error(GBX_EINVAL, "gbx_softmax_rows: null pointer");
     ScoreEpilogue ep{1, 0, 1.0f, false, make_fastdiv(1)};
-    return launch_softmax<false>("gbx_softmax_rows", in, out, rows, L, ep, reinterpret_cast<cudaStream_t>(stream));
+    return launch_softmax<false, false>("gbx_softmax_rows", in, out, nullptr, rows, L, ep,
+                                        reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t rows, int L, int S, int q_off,
@@ -225,6 +249,24 @@ extern "C" int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t 
     if (rows == 0) return GBX_OK;
     if (!scores || !probs) return set_error(GBX_EINVAL, "gbx_attn_softmax_rows: null pointer");
     ScoreEpilogue ep{S, q_off, scale, causal != 0, make_fastdiv((uint32_t)S)};
-    return launch_softmax<true>("gbx_attn_softmax_rows", scores, probs, rows, L, ep,
-                                reinterpret_cast<cudaStream_t>(stream));
+    return launch_softmax<true, false>("gbx_attn_softmax_rows", scores, probs, nullptr, rows, L, ep,
+                                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gbx_attn_softmax_rows_pair(const float* scores, float* probs_hi, float* probs_lo, int64_t rows, int L,
+                                          int S, int q_off, float scale, int causal, gbx_stream_t stream)
+{
+    if (rows < 0 || L <= 0 || S <= 0 || q_off < 0)
+        return set_error(GBX_EINVAL, "gbx_attn_softmax_rows_pair: rows=%lld L=%d S=%d q_off=%d", (long long)rows, L, S,
+                         q_off);
+    if (!(scale >= 1.17549435e-38f) || scale == INFINITY)
+        return set_error(GBX_EINVAL, "gbx_attn_softmax_rows_pair: scale=%g must be a normal positive float",
+                         (double)scale);
+    if (rows == 0) return GBX_OK;
+    if (!scores || !probs_hi || !probs_lo) return set_error(GBX_EINVAL, "gbx_attn_softmax_rows_pair: null pointer");
+    if ((const float*)probs_lo == scores || probs_lo == probs_hi)
+        return set_error(GBX_EINVAL, "gbx_attn_softmax_rows_pair: probs_lo aliases scores or probs_hi");
+    ScoreEpilogue ep{S, q_off, scale, causal != 0, make_fastdiv((uint32_t)S)};
+    return launch_softmax<true, true>("gbx_attn_softmax_rows_pair", scores, probs_hi, probs_lo, rows, L, ep,
+                                      reinterpret_cast<cudaStream_t>(stream));
 }

@@ -172,6 +172,16 @@ int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t rows, int L
                           float scale, int causal, gbx_stream_t stream);
 
 /*
+ * gbx_attn_softmax_rows with the probabilities written as the tf32 pair
+ * gbx_attn_values reads: probs_hi, probs_lo are exactly gbx_split_tf32 of
+ * gbx_attn_softmax_rows' output, in one pass.  No counterpart in the
+ * reference: it feeds the attention-output contraction.  probs_hi may alias
+ * scores; probs_lo may alias neither.
+ */
+int gbx_attn_softmax_rows_pair(const float* scores, float* probs_hi, float* probs_lo, int64_t rows, int L, int S,
+                               int q_off, float scale, int causal, gbx_stream_t stream);
+
+/*
  * Tied-weight logits, replacing computeLogitsKernel (transformer.cu:296-307,
  * launched at :898-900 on the final-LayerNorm row):
  *   logits[r*vocab + v] = sum_j h[r*d + j] * dec(wte[v*d + j])
@@ -251,6 +261,49 @@ int gbx_split_tf32(const float* x, float* hi, float* lo, int64_t n, gbx_stream_t
 int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo, const float* bias,
                const float* resid, float* y, float* y_lo, int64_t M, int N, int K, int act, int* err_flag,
                gbx_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * The per-head attention products on the tcgen05 tensor cores, for B
+ * sequences of S tokens, H heads of width hd, every operand a tf32 pair (the
+ * *_lo planes may be NULL: one product term less).  Head z = b*H + h.
+ * ------------------------------------------------------------------------ */
+
+/*
+ * Raw attention dot products, replacing the sums of attentionScoresKernel
+ * (transformer.cu:213-232) for every head of every sequence in one launch:
+ *   dots[(z*S + p)*S + s] = sum_i q[(b*S + p)*ld + h*hd + i] * k[(b*S + s)*ld + h*hd + i]
+ * q and k are row-major with row stride ld (>= H*hd; the Q and K column
+ * blocks of the [tokens, 3*d] QKV output: ld = 3*d).  causal != 0: only
+ * s <= p is required, and tiles of the [S, S] matrix lying wholly past the
+ * diagonal are neither computed nor written (gbx_attn_softmax_rows reads
+ * no entry past the diagonal).  The scale and the -1e9f mask are applied by
+ * the softmax.  dots must not overlap the operands.  err_flag: as
+ * gbx_linear (GBX_LINEAR_TIMEOUT).
+ */
+int gbx_attn_scores(const float* q_hi, const float* q_lo, const float* k_hi, const float* k_lo, int64_t ld,
+                    float* dots, int B, int S, int H, int hd, int causal, int* err_flag, gbx_stream_t stream);
+
+/*
+ * V of each head transposed for gbx_attn_values (no counterpart in the
+ * reference; one plane, call it for hi and for lo):
+ *   vt[((b*H + h)*hd + i)*S + s] = v[(b*S + s)*ld + h*hd + i]
+ */
+int gbx_transpose_heads(const float* v, int64_t ld, float* vt, int B, int S, int H, int hd, gbx_stream_t stream);
+
+/*
+ * Attention output, replacing attentionOutputKernel (transformer.cu:234-249)
+ * for every head of every sequence in one launch:
+ *   out[(b*S + p)*ld_out + h*hd + i] = sum_s P[(z*S + p)*S + s] * vt[(z*hd + i)*S + s]
+ * P: the probabilities [B*H*S, S] as a tf32 pair (gbx_attn_softmax_rows_pair);
+ * vt: gbx_transpose_heads of V.  causal != 0: P is zero past the diagonal
+ * (as the causal softmax writes it) and the sum stops there.  out_lo NULL:
+ * out receives the fp32 result; otherwise out and out_lo its tf32 pair,
+ * the x operand of the output projection.  out must not overlap the
+ * operands.  err_flag: as gbx_linear.
+ */
+int gbx_attn_values(const float* p_hi, const float* p_lo, const float* vt_hi, const float* vt_lo, float* out,
+                    float* out_lo, int64_t ld_out, int B, int S, int H, int hd, int causal, int* err_flag,
+                    gbx_stream_t stream);
 
 #ifdef __cplusplus
 }

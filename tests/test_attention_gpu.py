@@ -1,0 +1,236 @@
+"""Parity of the per-head attention products on the tensor cores
+(gbx_attn_scores, gbx_transpose_heads, gbx_attn_softmax_rows_pair,
+gbx_attn_values), called through the C ABI.
+
+Reference semantics: attentionScoresKernel (transformer.cu:213-232) forms
+dot[h][p][s] = sum_i Q[p, h*hd+i] K[s, h*hd+i] for every key s <= p;
+attentionOutputKernel (:234-249) forms out[p, h*hd+i] = sum_s P[h][p][s]
+V[s, h*hd+i]; both in fp32.  Here every operand is a tf32 pair and the
+check is against the exact value (float64 of the same fp32 inputs) with
+gbx_linear's worst-case bound for its arithmetic (tests/test_linear_gpu.py):
+  |y - exact| <= (48 2^-23 + ceil(K/128) 2^-24 + 2^-20) sum_k |x w|
+                 + 4 eps_32 |exact| + 1e-6
+and, for the CUDA-core path (operands the tensor maps cannot describe),
+(3 K 2^-24 1.01 + 2^-20) sum_k |x w| in its place.  A wrong head, tile,
+sequence offset or K range gives errors of order |x w|.  Outputs sit
+between NaN-canary guards that must survive.
+"""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CANARY = np.uint32(0x7FBADBAD)
+
+
+def _split(gbx, torch, a):
+    hi = torch.empty_like(a)
+    lo = torch.empty_like(a)
+    gbx.split_tf32(a, hi, lo, n=a.numel())
+    return hi, lo
+
+
+def _guarded(torch, n):
+    """A flat device buffer of n floats with 64 canary words either side."""
+    full = torch.empty(n + 128, dtype=torch.float32, device="cuda")
+    full.view(torch.int32).fill_(int(CANARY.view(np.int32)))
+    return full, full[64:64 + n]
+
+
+def _check_guards(full):
+    h = full.cpu().numpy().view(np.uint32)
+    assert np.all(h[:64] == CANARY) and np.all(h[-64:] == CANARY), "write outside the output"
+
+
+def _tol(exact, mag, K, general):
+    if general:
+        b = (3 * K * 2.0 ** -24 * 1.01 + 2.0 ** -20) * mag
+    else:
+        b = (48 * 2.0 ** -23 + -(-K // 128) * 2.0 ** -24 + 2.0 ** -20) * mag
+    return b + 4 * np.finfo(np.float32).eps * np.abs(exact) + 1e-6
+
+
+def _assert_within(got, want, tol, what, mask=None):
+    got = got.astype(np.float64)
+    if mask is not None:   # entries outside the mask are unspecified (canaries where no tile wrote)
+        got = np.where(mask, got, want)
+    err = np.abs(got - want)
+    bad = ~(err <= tol)
+    if bad.any():
+        i = np.unravel_index(int(np.argmax(np.where(bad, err - tol, -np.inf))), err.shape)
+        raise AssertionError(f"{what}: {int(bad.sum())} of {err.size} outside the bound; worst at {i}: "
+                             f"{got[i]!r} vs {want[i]!r} (|d| {err[i]:.3g} > {tol[i]:.3g})")
+
+
+def _heads(a, B, S, H, hd):
+    """[B*S, H*hd] -> [B, H, S, hd] float64."""
+    return a.astype(np.float64).reshape(B, S, H, hd).transpose(0, 2, 1, 3)
+
+
+# (B, S, H, hd): S 1024 runs CTA pairs, S 17 an N tail and a general-path P.V,
+# hd 12 a K block mostly out of range, hd 6 the general path for both products
+SHAPES = [(2, 64, 3, 64), (1, 1024, 2, 64), (2, 200, 2, 64), (3, 17, 2, 64), (1, 36, 2, 12), (2, 40, 2, 6)]
+
+
+def _qkv(torch, B, S, H, hd, seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    return torch.randn((B * S, 3 * H * hd), generator=g, device="cuda")
+
+
+def run_scores(gbx, torch, B, S, H, hd, causal):
+    d = H * hd
+    qkv = _qkv(torch, B, S, H, hd, B * 1000 + S + hd)
+    hi, lo = _split(gbx, torch, qkv)
+    full, dots = _guarded(torch, B * H * S * S)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.attn_scores(hi, lo, hi[:, d:], lo[:, d:], dots, ld=3 * d, B=B, S=S, H=H, hd=hd, causal=causal, err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    x = qkv.cpu().numpy()
+    q, k = _heads(x[:, :d], B, S, H, hd), _heads(x[:, d:2 * d], B, S, H, hd)
+    exact = q @ k.transpose(0, 1, 3, 2)
+    mag = np.abs(q) @ np.abs(k).transpose(0, 1, 3, 2)
+    got = dots.cpu().numpy().reshape(B, H, S, S)
+    mask = np.tril(np.ones((S, S), bool))[None, None] if causal else None
+    _assert_within(got, exact, _tol(exact, mag, hd, hd % 4 != 0), f"scores B{B} S{S} H{H} hd{hd} causal={causal}",
+                   mask)
+    _check_guards(full)
+
+
+def run_values(gbx, torch, B, S, H, hd, causal, pair_out):
+    d = H * hd
+    qkv = _qkv(torch, B, S, H, hd, 7 * S + hd + B)
+    hi, lo = _split(gbx, torch, qkv)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(S + hd)
+    scores = 2.0 * torch.randn((B * H * S, S), generator=g, device="cuda")
+    p_ref = torch.empty_like(scores)
+    gbx.attn_softmax_rows(scores, p_ref, rows=B * H * S, L=S, S=S, scale=8.0, causal=causal)
+    p_hi = torch.empty_like(scores)
+    p_lo = torch.empty_like(scores)
+    gbx.attn_softmax_rows_pair(scores, p_hi, p_lo, rows=B * H * S, L=S, S=S, scale=8.0, causal=causal)
+    vt_hi = torch.empty(B * H * hd * S, dtype=torch.float32, device="cuda")
+    vt_lo = torch.empty_like(vt_hi)
+    gbx.transpose_heads(hi[:, 2 * d:], vt_hi, ld=3 * d, B=B, S=S, H=H, hd=hd)
+    gbx.transpose_heads(lo[:, 2 * d:], vt_lo, ld=3 * d, B=B, S=S, H=H, hd=hd)
+    full, out = _guarded(torch, B * S * d)
+    full_lo, out_lo = _guarded(torch, B * S * d)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.attn_values(p_hi, p_lo, vt_hi, vt_lo, out, ld_out=d, B=B, S=S, H=H, hd=hd, out_lo=out_lo if pair_out else None,
+                    causal=causal, err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    P = p_ref.cpu().numpy().astype(np.float64).reshape(B, H, S, S)
+    v = _heads(qkv.cpu().numpy()[:, 2 * d:], B, S, H, hd)
+    exact = (P @ v).transpose(0, 2, 1, 3).reshape(B * S, d)
+    mag = (np.abs(P) @ np.abs(v)).transpose(0, 2, 1, 3).reshape(B * S, d)
+    got = out.cpu().numpy().astype(np.float64).reshape(B * S, d)
+    if pair_out:
+        got = got + out_lo.cpu().numpy().astype(np.float64).reshape(B * S, d)
+        _check_guards(full_lo)
+    _assert_within(got, exact, _tol(exact, mag, S, S % 4 != 0),
+                   f"values B{B} S{S} H{H} hd{hd} causal={causal} pair={pair_out}")
+    _check_guards(full)
+
+
+@pytest.mark.parametrize("B,S,H,hd", SHAPES)
+@pytest.mark.parametrize("causal", [True, False])
+def test_attn_scores(gbx, cuda, B, S, H, hd, causal):
+    import torch
+    run_scores(gbx, torch, B, S, H, hd, causal)
+
+
+@pytest.mark.parametrize("B,S,H,hd", SHAPES)
+@pytest.mark.parametrize("causal,pair_out", [(True, True), (True, False), (False, False)])
+def test_attn_values(gbx, cuda, B, S, H, hd, causal, pair_out):
+    import torch
+    run_values(gbx, torch, B, S, H, hd, causal, pair_out)
+
+
+@pytest.mark.parametrize("B,S,H,hd", [(2, 17, 3, 64), (1, 1024, 2, 64), (2, 40, 2, 6)])
+def test_transpose_heads_exact(gbx, cuda, B, S, H, hd):
+    import torch
+    d = H * hd
+    qkv = _qkv(torch, B, S, H, hd, 3)
+    full, vt = _guarded(torch, B * H * hd * S)
+    gbx.transpose_heads(qkv[:, 2 * d:], vt, ld=3 * d, B=B, S=S, H=H, hd=hd)
+    want = qkv.cpu().numpy()[:, 2 * d:].reshape(B, S, H, hd).transpose(0, 2, 3, 1).reshape(-1)
+    assert np.array_equal(vt.cpu().numpy(), want)
+    _check_guards(full)
+
+
+@pytest.mark.parametrize("S,scale", [(64, 8.0), (1024, 8.0), (17, 8.0), (128, float(np.sqrt(np.float32(100.0))))])
+def test_attn_softmax_pair_is_split_of_softmax(gbx, cuda, S, scale):
+    import torch
+    rows = 3 * S
+    g = torch.Generator(device="cuda")
+    g.manual_seed(S)
+    scores = 3.0 * torch.randn((rows, S), generator=g, device="cuda")
+    p = torch.empty_like(scores)
+    gbx.attn_softmax_rows(scores, p, rows=rows, L=S, S=S, scale=scale)
+    want_hi, want_lo = _split(gbx, torch, p)
+    hi = torch.empty_like(scores)
+    lo = torch.empty_like(scores)
+    gbx.attn_softmax_rows_pair(scores, hi, lo, rows=rows, L=S, S=S, scale=scale)
+    assert torch.equal(hi.view(torch.int32), want_hi.view(torch.int32))
+    assert torch.equal(lo.view(torch.int32), want_lo.view(torch.int32))
+    # in place (hi over the scores)
+    s2 = scores.clone()
+    gbx.attn_softmax_rows_pair(s2, s2, lo, rows=rows, L=S, S=S, scale=scale)
+    assert torch.equal(s2.view(torch.int32), want_hi.view(torch.int32))
+    with pytest.raises(gbx.GbxError):
+        gbx.attn_softmax_rows_pair(scores, hi, hi, rows=rows, L=S, S=S, scale=scale)
+
+
+def test_attn_products_reject_bad_arguments(gbx, cuda):
+    import torch
+    x = torch.zeros(4096, dtype=torch.float32, device="cuda")
+    y = torch.zeros(4096, dtype=torch.float32, device="cuda")
+    for kw in (dict(B=0), dict(S=0), dict(H=0), dict(hd=0), dict(ld=3)):
+        args = dict(ld=8, B=1, S=4, H=2, hd=4)
+        args.update(kw)
+        with pytest.raises(gbx.GbxError):
+            gbx.attn_scores(x, None, x, None, y, **args)
+    with pytest.raises(gbx.GbxError):   # output aliases an operand
+        gbx.attn_scores(x, None, x, None, x, ld=8, B=1, S=4, H=2, hd=4)
+    with pytest.raises(gbx.GbxError):
+        gbx.attn_values(x, None, x, None, y, ld_out=8, B=1, S=4, H=2, hd=4, out_lo=y)
+    with pytest.raises(gbx.GbxError):
+        gbx.transpose_heads(x, x, ld=8, B=1, S=4, H=2, hd=4)
+
+
+_SUBPROCESS_CASES = r"""
+import importlib, sys
+import torch
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
+gbx = importlib.import_module("glassboxai-transformer_b200")
+import test_attention_gpu as t
+for B, S, H, hd in ((2, 64, 3, 64), (1, 300, 2, 64), (3, 17, 2, 64), (1, 36, 2, 12), (1, 1024, 1, 64)):
+    for causal in (True, False):
+        t.run_scores(gbx, torch, B, S, H, hd, causal)
+        t.run_values(gbx, torch, B, S, H, hd, causal, causal)
+print("ok")
+"""
+
+
+def _run_cases(env_extra):
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, **env_extra)
+    out = subprocess.run([sys.executable, "-c", _SUBPROCESS_CASES, root, os.path.join(root, "tests")], env=env,
+                         capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stdout + out.stderr
+
+
+def test_attn_products_cta_pairs_forced(cuda):
+    """The heads mode on CTA pairs for every shape (a 256-row pair tile over
+    fewer rows than a head holds)."""
+    _run_cases({"GBX_LINEAR_PAIR": "1"})
+
+
+def test_attn_products_single_cta_forced(cuda):
+    _run_cases({"GBX_LINEAR_PAIR": "0"})

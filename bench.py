@@ -597,6 +597,8 @@ def run_kernel(args, shape):
         nbytes = 4 * R + R * d * es + min(seq, shape.n_ctx) * d * es + 4 * R * d
     elif name.startswith("linear_"):
         return run_linear(args, shape, G, g, f32)
+    elif name in ATTN_KERNELS:
+        return run_attn(args, shape, G, g, f32)
     else:
         raise SystemExit(f"unknown kernel {name}")
     for _ in range(args.warmup):
@@ -694,6 +696,98 @@ def run_linear(args, shape, G, g, f32):
                       "frac_of_tf32_peak": terms * flop / (us * 1e-6) / 1e12 / peak, "tf32_peak": peak,
                       "peak_kind": kind, "cublas_sgemm_us": sg, "cublas_sgemm_tflops": flop / (sg * 1e-6) / 1e12,
                       "speedup_vs_sgemm": sg / us}), flush=True)
+
+
+ATTN_KERNELS = ["attn_scores", "attn_values", "attn_block"]
+
+
+def run_attn(args, shape, G, g, f32):
+    """The per-head attention products of the workload's layer on --rows
+    token rows (rows / seq causal sequences): gbx_attn_scores,
+    gbx_attn_values, or the whole block (scores, softmax with tf32-pair
+    output, V transposes, values), against cuBLAS fp32 batched GEMMs (TF32
+    off) with torch's masked softmax, each timed per launch with CUDA events."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    S, H, d = shape.seq, shape.heads, shape.d
+    hd = d // H
+    B = max(1, args.rows // S)
+    N = B * S
+    qkv = torch.randn((N, 3 * d), generator=g, **f32)
+    qh, ql = torch.empty_like(qkv), torch.empty_like(qkv)
+    G.split_tf32(qkv, qh, ql, n=qkv.numel())
+    dots = torch.empty((B * H * S, S), **f32)
+    p_lo = torch.empty_like(dots)
+    vt, vt_lo = torch.empty((B * H * hd * S,), **f32), torch.empty((B * H * hd * S,), **f32)
+    out, out_lo = torch.empty((N, d), **f32), torch.empty((N, d), **f32)
+    err = torch.zeros(1, dtype=torch.int32, device=qkv.device)
+    scale = math.sqrt(hd)
+    # probabilities for the values product alone
+    G.attn_scores(qh, ql, qh[:, d:], ql[:, d:], dots, ld=3 * d, B=B, S=S, H=H, hd=hd, err_flag=err)
+    G.attn_softmax_rows_pair(dots, dots, p_lo, rows=B * H * S, L=S, S=S, scale=scale)
+    G.transpose_heads(qh[:, 2 * d:], vt, ld=3 * d, B=B, S=S, H=H, hd=hd)
+    G.transpose_heads(ql[:, 2 * d:], vt_lo, ld=3 * d, B=B, S=S, H=H, hd=hd)
+    dots2 = torch.empty_like(dots)
+
+    def scores():
+        G.attn_scores(qh, ql, qh[:, d:], ql[:, d:], dots2, ld=3 * d, B=B, S=S, H=H, hd=hd, err_flag=err)
+
+    def values():
+        G.attn_values(dots, p_lo, vt, vt_lo, out, ld_out=d, B=B, S=S, H=H, hd=hd, out_lo=out_lo, err_flag=err)
+
+    def block():
+        G.attn_scores(qh, ql, qh[:, d:], ql[:, d:], dots2, ld=3 * d, B=B, S=S, H=H, hd=hd, err_flag=err)
+        G.attn_softmax_rows_pair(dots2, dots2, p_lo, rows=B * H * S, L=S, S=S, scale=scale)
+        G.transpose_heads(qh[:, 2 * d:], vt, ld=3 * d, B=B, S=S, H=H, hd=hd)
+        G.transpose_heads(ql[:, 2 * d:], vt_lo, ld=3 * d, B=B, S=S, H=H, hd=hd)
+        G.attn_values(dots2, p_lo, vt, vt_lo, out, ld_out=d, B=B, S=S, H=H, hd=hd, out_lo=out_lo, err_flag=err)
+
+    q4 = qkv[:, :d].reshape(B, S, H, hd).permute(0, 2, 1, 3).reshape(B * H, S, hd)
+    k4 = qkv[:, d:2 * d].reshape(B, S, H, hd).permute(0, 2, 1, 3).reshape(B * H, S, hd)
+    v4 = qkv[:, 2 * d:].reshape(B, S, H, hd).permute(0, 2, 1, 3).reshape(B * H, S, hd)
+    mask = torch.triu(torch.ones((S, S), dtype=torch.bool, device=qkv.device), 1)
+    sr = torch.empty((B * H, S, S), **f32)
+    pr = torch.empty((B * H, S, S), **f32)
+    orf = torch.empty((B * H, S, hd), **f32)
+
+    def ref_scores():
+        torch.bmm(q4, k4.transpose(1, 2), out=sr)
+
+    def ref_values():
+        torch.bmm(pr, v4, out=orf)
+
+    def ref_block():
+        torch.bmm(q4, k4.transpose(1, 2), out=sr)
+        sr.div_(scale).masked_fill_(mask, -1e9)
+        torch.softmax(sr, dim=-1, out=pr)
+        torch.bmm(pr, v4, out=orf)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, e in evs:
+            a.record()
+            fn()
+            e.record()
+        torch.cuda.synchronize()
+        return statistics.median([1000.0 * a.elapsed_time(e) for a, e in evs])
+
+    ours, ref = {"attn_scores": (scores, ref_scores), "attn_values": (values, ref_values),
+                 "attn_block": (block, ref_block)}[args.kernel]
+    us = timed(ours)
+    if int(err.item()) != 0:
+        raise SystemExit("an attention product reported a pipeline timeout")
+    rus = timed(ref)
+    per = 2.0 * B * H * S * S * hd   # one dense product, flops
+    flop = {"attn_scores": per, "attn_values": per, "attn_block": 2 * per}[args.kernel]
+    print(json.dumps({"kernel": args.kernel, "workload": args.workload, "sequences": B, "seq": S, "heads": H,
+                      "head_dim": hd, "causal": True, "median_us": us,
+                      "dense_equiv_tflops": flop / (us * 1e-6) / 1e12,
+                      "cublas_fp32_us": rus, "speedup_vs_cublas_fp32": rus / us,
+                      "cublas_path": "torch.bmm fp32 (TF32 off), dense; block: + scale, mask, torch.softmax"}),
+          flush=True)
 
 
 def bench_gguf(shape, workload):
@@ -809,7 +903,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--kernel", choices=["embed", "layernorm", "residual_layernorm", "softmax_rows", "attn_softmax_rows",
-                                         "bias_gelu"] + sorted(LINEAR_KERNELS),
+                                         "bias_gelu"] + sorted(LINEAR_KERNELS) + ATTN_KERNELS,
                     help="time one kernel alone on --rows rows of the workload's shape")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--graph", action="store_true",

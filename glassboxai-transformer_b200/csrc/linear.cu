@@ -61,6 +61,10 @@ constexpr int kLinTmemCols = kLinBuffers * kLinBN;
 #endif
 constexpr int kLinChunkK = GBX_LINEAR_CHUNK_K;   // K elements summed in TMEM before each fp32 promotion
 constexpr uint64_t kLinWaitNs = 1000000000ull;
+// Heads mode: per epilogue warp, a 32-row x 16-column staging block in
+// shared memory (after the barriers) for coalesced output stores.
+constexpr int kLinStageFloats = 32 * 16;
+constexpr size_t kLinEpiStageBytes = (size_t)kLinEpiWarps * kLinStageFloats * sizeof(float) + 16;
 
 // Shared-memory ring and barrier layout.  PAIR: a cluster of two CTAs runs
 // one M 256 x N 256 MMA (cta_group::2); each CTA holds its 128 x rows and
@@ -77,7 +81,7 @@ struct LinCfg {
     static constexpr int ksteps = BK / 8;                       // tf32 MMA K = 8 (32 bytes)
     static constexpr int chunk_blocks = kLinChunkK / BK;          // K blocks per chunk
     static constexpr int tile_rows = PAIR ? 2 * kLinBM : kLinBM;  // output rows per tile
-    static constexpr int nbars = 2 * stages + 2 * kLinBuffers + 1;
+    static constexpr int nbars = 2 * stages + 3 * kLinBuffers + 1;
     static constexpr size_t smem = (size_t)stages * stage_bytes + 1024 + 8 * nbars + 16;
     static_assert(kLinChunkK % 32 == 0, "a chunk is whole K blocks");
     static_assert(BK == 16 || BK == 32, "swizzle width");
@@ -217,6 +221,51 @@ __device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, i
     }
 }
 
+// Heads mode, VEC: output columns n .. n+15 of an epilogue warp's 32 rows
+// (this lane's row's values v[off .. off+15], off a constant after
+// unrolling), written through the warp's
+// 32 x 16 staging block `stg`.  Straight from the accumulator's thread-per-row
+// layout every warp store would touch 32 rows with 16 bytes each; staged, a
+// warp store writes 8 rows x 64 contiguous bytes.  The block is XOR-swizzled
+// by 16-byte chunk (chunk ^ ((row >> 1) & 3)), so both the row-wise writes
+// and the column-wise reads are free of bank conflicts.  r_rd: the first
+// output row this lane writes on the read side (8 rows apart after it),
+// out_rd its offset in y plus the lane's 4-column offset.  The heads mode has
+// no bias, residual or activation.  All 32 lanes call it.
+template <int LEN>
+__device__ __forceinline__ void heads_store16(float* stg, int lane, const float (&v)[LEN], int off, int n,
+                                              int64_t r_rd, int64_t out_rd, const LinearArgs& a)
+{
+    float* const wrow = stg + lane * 16;
+    const int wsw = (lane >> 1) & 3;
+    const int q = lane & 3;
+    // the read side's row 8 i + lane / 4 has swizzle (lane >> 3) & 3 for every i
+    const float* const rd = stg + (lane >> 2) * 16 + 4 * (q ^ ((lane >> 3) & 3));
+    const bool col_ok = n + 4 * q < a.N;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        if (part == 1 && !a.y_lo) break;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float4 o = make_float4(v[off + 4 * j], v[off + 4 * j + 1], v[off + 4 * j + 2], v[off + 4 * j + 3]);
+            if (a.y_lo) {
+                float4 h, l;
+                split4(o, h, l);
+                o = part ? l : h;
+            }
+            *reinterpret_cast<float4*>(wrow + 4 * (j ^ wsw)) = o;
+        }
+        __syncwarp();
+        float* const dst = (part ? a.y_lo : a.y) + out_rd + n;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 o = *reinterpret_cast<const float4*>(rd + 128 * i);
+            if (col_ok && r_rd + 8 * i < a.M) *reinterpret_cast<float4*>(dst + 8 * i * a.ldy) = o;
+        }
+        __syncwarp();
+    }
+}
+
 template <int BK, bool VEC, bool PAIR, bool HEADS>
 __global__ void __launch_bounds__(kLinThreads, 1)
 linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constant__ CUtensorMap map_xl,
@@ -229,18 +278,23 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::stages * C::stage_bytes);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::nbars);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // heads mode only (the host adds kLinEpiStageBytes to the launch's shared memory)
+    float* const epi_stage = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(tmem_slot + 2) + 15) & ~uintptr_t(15));
     const uint32_t full0 = tc::smem_u32(bars);                     // full[s]        = full0 + 8 s
     const uint32_t empty0 = full0 + 8 * C::stages;                 // empty[s]
     const uint32_t cfull0 = empty0 + 8 * C::stages;                // chunk_full[b]
     const uint32_t cempty0 = cfull0 + 8 * kLinBuffers;             // chunk_empty[b]
     const uint32_t drain = cempty0 + 8 * kLinBuffers;
+    const uint32_t clocal0 = drain + 8;                            // PAIR follower: chunk_empty, local
     const uint32_t smem0 = tc::smem_u32(smem);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     // PAIR: the barriers that count both CTAs (full, chunk_empty, drain) live
-    // in the leader, rank 0; empty and chunk_full exist in both (the MMA
-    // commit multicasts to the two)
+    // in the leader, rank 0 (chunk_empty counts the leader's epilogue warps
+    // and one arrival forwarded for the follower's); empty and chunk_full
+    // exist in both (the MMA commit multicasts to the two)
     const uint32_t rank = PAIR ? tc::cluster_rank() : 0;
     const bool leader = rank == 0;
     const int unit = PAIR ? (int)tc::cluster_id_x() : (int)blockIdx.x;        // tile walker
@@ -253,7 +307,10 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
         }
         for (int b = 0; b < kLinBuffers; ++b) {
             tc::mbar_init(cfull0 + 8 * b, 1);
-            tc::mbar_init(cempty0 + 8 * b, (PAIR ? 2 : 1) * kLinEpiWarps);   // one arrival per epilogue warp
+            // one arrival per epilogue warp of this CTA; PAIR: and one
+            // forwarded for all of the follower's (see the forwarder below)
+            tc::mbar_init(cempty0 + 8 * b, kLinEpiWarps + (PAIR ? 1 : 0));
+            tc::mbar_init(clocal0 + 8 * b, kLinEpiWarps);
         }
         tc::mbar_init(drain, 1);
         *abort = 0;
@@ -432,6 +489,33 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
             else
                 tc::mma_commit(drain);
             tc::mbar_wait(drain, 0, nullptr, kLinWaitNs);
+        } else if (PAIR && lane == 0) {
+            // ---------------------------------------------------- forwarder
+            // The follower's epilogue warps release each chunk buffer on
+            // their own CTA's barrier; this thread, which has no global
+            // stores in flight, passes one cluster-scope arrival on to the
+            // leader's chunk_empty.  (A cluster-scope release from an
+            // epilogue warp would first wait for that warp's output stores
+            // to drain.)
+            int buf = 0;
+            uint32_t buf_phase = 0;
+            bool ok = true;
+            for (int t = unit; t < a.tiles && ok; t += units) {
+                const TileInfo ti = tile_info<BK, PAIR, HEADS>(t, a);
+                if (!ti.live) continue;
+                const int chunks = (ti.kb_end + C::chunk_blocks - 1) / C::chunk_blocks;
+                for (int c = 0; c < chunks; ++c) {
+                    if (!tc::mbar_wait(clocal0 + 8 * buf, buf_phase, abort, kLinWaitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_cluster(tc::mapa(cempty0 + 8 * buf, 0));
+                    if (++buf == kLinBuffers) {
+                        buf = 0;
+                        buf_phase ^= 1;
+                    }
+                }
+            }
         }
     } else {
         // -------------------------------------------------------- epilogue
@@ -446,6 +530,39 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
             if (!ti.live) continue;
             const int mb = ti.mb, nb = ti.nb;
             const int chunks = (ti.kb_end + C::chunk_blocks - 1) / C::chunk_blocks;
+            // heads mode: per-warp output geometry of the staged stores
+            float* const stg = epi_stage + (warp - 2) * kLinStageFloats;
+            const int64_t r_rd = (int64_t)mb * C::tile_rows + (int)rank * kLinBM + 32 * quarter + (lane >> 2);
+            const int64_t out_rd = (int64_t)ti.b * a.syb + (int64_t)ti.h * a.syh + r_rd * a.ldy + 4 * (lane & 3);
+            const int n0 = nb * kLinBN + col0;
+            if (HEADS && VEC && chunks == 1) {
+                // one K chunk (a head-wide K): stream TMEM to the output 32
+                // columns at a time instead of holding the row in registers
+                const bool ready = tc::mbar_wait(cfull0 + 8 * buf, buf_phase, abort, kLinWaitNs);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + buf * kLinBN + col0;
+#pragma unroll 1
+                for (int g = 0; g < kLinEpiCols / 32; ++g) {
+                    if (n0 + 32 * g >= a.N) break;   // uniform over the warp
+                    float v[32];
+                    tc::tmem_ld32(tbase + 32 * g, v);
+                    tc::tmem_ld_wait();
+                    heads_store16(stg, lane, v, 0, n0 + 32 * g, r_rd, out_rd, a);
+                    if (n0 + 32 * g + 16 < a.N) heads_store16(stg, lane, v, 16, n0 + 32 * g + 16, r_rd, out_rd, a);
+                }
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive((PAIR && !leader ? clocal0 : cempty0) + 8 * buf);
+                if (++buf == kLinBuffers) {
+                    buf = 0;
+                    buf_phase ^= 1;
+                }
+                continue;
+            }
             float acc[kLinEpiCols];
 #pragma unroll
             for (int j = 0; j < kLinEpiCols; ++j) acc[j] = 0.0f;
@@ -471,12 +588,7 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                 }
                 tc::fence_before_sync();
                 __syncwarp();
-                if (lane == 0) {
-                    if constexpr (PAIR)
-                        tc::mbar_arrive_cluster(tc::mapa(cempty0 + 8 * buf, 0));
-                    else
-                        tc::mbar_arrive(cempty0 + 8 * buf);
-                }
+                if (lane == 0) tc::mbar_arrive((PAIR && !leader ? clocal0 : cempty0) + 8 * buf);
                 if (++buf == kLinBuffers) {
                     buf = 0;
                     buf_phase ^= 1;
@@ -484,10 +596,15 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
             }
             if (!ok) break;
             const int64_t row = (int64_t)mb * C::tile_rows + row_in_tile;
-            const int n0 = nb * kLinBN + col0;
             int64_t yoff = row * a.ldy;
             if constexpr (HEADS) yoff += ti.b * a.syb + ti.h * a.syh;
-            if (row < a.M) {
+            if constexpr (HEADS && VEC) {
+#pragma unroll
+                for (int g = 0; g < kLinEpiCols / 16; ++g) {
+                    if (n0 + 16 * g >= a.N) break;   // uniform over the warp
+                    heads_store16(stg, lane, acc, 16 * g, n0 + 16 * g, r_rd, out_rd, a);
+                }
+            } else if (row < a.M) {
 #pragma unroll
                 for (int g = 0; g < kLinEpiCols / 16; ++g) {
                     if (n0 + 16 * g < a.N) {
@@ -725,10 +842,11 @@ static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi
                          cudaStream_t s, const HeadsOperand* hx = nullptr, const HeadsOperand* hw = nullptr, int B = 1)
 {
     using C = LinCfg<BK, PAIR>;
+    const size_t smem = C::smem + (HEADS ? kLinEpiStageBytes : 0);
     DeviceInfo di;
     if (device_info(&di) != GBX_OK) return GBX_ECUDA;
-    if ((size_t)di.max_smem_optin < C::smem)
-        return set_error(GBX_ERANGE, "gbx_linear: needs %zu bytes of shared memory per CTA", C::smem);
+    if ((size_t)di.max_smem_optin < smem)
+        return set_error(GBX_ERANGE, "gbx_linear: needs %zu bytes of shared memory per CTA", smem);
     const int64_t m_blocks = (a.M + C::tile_rows - 1) / C::tile_rows;
     const int64_t zs = HEADS ? (int64_t)a.H * B : 1;
     if (m_blocks * a.n_blocks * zs > 0x7fffffffLL) return set_error(GBX_ERANGE, "gbx_linear: too many tiles");
@@ -767,11 +885,11 @@ static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi
     }
     auto k = linear_tf32x3_kernel<BK, VEC, PAIR, HEADS>;
     // per device, so set on every call (a host-side attribute write)
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(GBX_ECUDA, "gbx_linear: shared-memory attribute refused");
     if constexpr (!PAIR) {
         const int grid = a.tiles < di.sm_count ? a.tiles : di.sm_count;
-        k<<<grid, kLinThreads, C::smem, s>>>(mxh, mxl, mwh, mwl, a);
+        k<<<grid, kLinThreads, smem, s>>>(mxh, mxl, mwh, mwl, a);
         return check_launch("gbx_linear");
     } else {
         cudaLaunchConfig_t cfg = {};
@@ -781,7 +899,7 @@ static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
         cfg.blockDim = dim3(kLinThreads);
-        cfg.dynamicSmemBytes = C::smem;
+        cfg.dynamicSmemBytes = smem;
         cfg.stream = s;
         cfg.attrs = attr;
         cfg.numAttrs = 1;

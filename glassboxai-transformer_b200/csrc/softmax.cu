@@ -46,7 +46,10 @@ struct ScoreEpilogue {
 
 // POW2: scale is a power of two, so raw / scale == raw * (1/scale) exactly.
 // PAIR_OUT: out and out_lo receive the tf32 pair of each probability
-// (tf32.cuh), the operand form of the attention-output contraction.
+// (tf32.cuh), the operand form of the attention-output contraction; with
+// the causal prefill mask (q_off 0) only columns below
+// round_up(p + 1, 256) are written: the rest are zero, and the
+// contraction, whose row tiles are 128 or 256 rows high, never reads them.
 template <int TPR, int V4, bool ATTN, bool POW2, bool PAIR_OUT>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads)
 softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep)
@@ -118,12 +121,14 @@ softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int
     }
     s = row_sum<TPR>(s, red[1]);
 
+    // PAIR_OUT: columns written (a multiple of 4)
+    const int wend = (PAIR_OUT && ATTN && ep.causal && ep.q_off == 0) ? min(L, ((last + 256) >> 8) << 8) : L;
     if (valid) {
         const float r = 1.0f / s;
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
             const int c = k * TPR + lane;
-            if (c < n4) {
+            if (c < n4 && (!PAIR_OUT || 4 * c < wend)) {
                 const float4 q = make_float4(div_by(v[k].x, s, r), div_by(v[k].y, s, r), div_by(v[k].z, s, r),
                                              div_by(v[k].w, s, r));
                 if constexpr (PAIR_OUT) {
@@ -166,7 +171,8 @@ softmax_general_kernel(const float* in, float* out, float* out_lo, int64_t rows,
         }
         s = block_sum(s, red[1]);
         const float r = 1.0f / s;
-        for (int i = threadIdx.x; i < L; i += kGeneralCTA) {
+        const int wend = (PAIR_OUT && ATTN && ep.causal && ep.q_off == 0) ? min(L, ((last + 256) >> 8) << 8) : L;
+        for (int i = threadIdx.x; i < wend; i += kGeneralCTA) {
             const float q = div_by(orow[i], s, r);
             if constexpr (PAIR_OUT) {
                 float hv, lv;

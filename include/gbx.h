@@ -175,8 +175,10 @@ int gbx_attn_softmax_rows(const float* scores, float* probs, int64_t rows, int L
  * gbx_attn_softmax_rows with the probabilities written as the tf32 pair
  * gbx_attn_values reads: probs_hi, probs_lo are exactly gbx_split_tf32 of
  * gbx_attn_softmax_rows' output, in one pass.  No counterpart in the
- * reference: it feeds the attention-output contraction.  probs_hi may alias
- * scores; probs_lo may alias neither.
+ * reference: it feeds the attention-output contraction.  With causal and
+ * q_off 0, only the columns below round_up(p + 1, 256) of row p (p = row % S)
+ * are written: the others are zero, and gbx_attn_values never reads them.
+ * probs_hi may alias scores; probs_lo may alias neither.
  */
 int gbx_attn_softmax_rows_pair(const float* scores, float* probs_hi, float* probs_lo, int64_t rows, int L, int S,
                                int q_off, float scale, int causal, gbx_stream_t stream);

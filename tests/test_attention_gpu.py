@@ -177,12 +177,23 @@ def test_attn_softmax_pair_is_split_of_softmax(gbx, cuda, S, scale):
     hi = torch.empty_like(scores)
     lo = torch.empty_like(scores)
     gbx.attn_softmax_rows_pair(scores, hi, lo, rows=rows, L=S, S=S, scale=scale)
-    assert torch.equal(hi.view(torch.int32), want_hi.view(torch.int32))
-    assert torch.equal(lo.view(torch.int32), want_lo.view(torch.int32))
+    # causal prefill: row p is written below round_up(p + 1, 256) (the rest are zeros nothing reads)
+    p_of = np.arange(rows) % S
+    written = np.arange(S)[None, :] < np.minimum(S, (p_of[:, None] + 256) // 256 * 256)
+    wm = torch.from_numpy(written).cuda()
+    assert torch.equal(hi.view(torch.int32)[wm], want_hi.view(torch.int32)[wm])
+    assert torch.equal(lo.view(torch.int32)[wm], want_lo.view(torch.int32)[wm])
+    assert not torch.any(want_hi[~wm] != 0)
     # in place (hi over the scores)
     s2 = scores.clone()
     gbx.attn_softmax_rows_pair(s2, s2, lo, rows=rows, L=S, S=S, scale=scale)
-    assert torch.equal(s2.view(torch.int32), want_hi.view(torch.int32))
+    assert torch.equal(s2.view(torch.int32)[wm], want_hi.view(torch.int32)[wm])
+    # without the mask every entry is written
+    gbx.attn_softmax_rows(scores, p, rows=rows, L=S, S=S, scale=scale, causal=False)
+    want_hi, want_lo = _split(gbx, torch, p)
+    gbx.attn_softmax_rows_pair(scores, hi, lo, rows=rows, L=S, S=S, scale=scale, causal=False)
+    assert torch.equal(hi.view(torch.int32), want_hi.view(torch.int32))
+    assert torch.equal(lo.view(torch.int32), want_lo.view(torch.int32))
     with pytest.raises(gbx.GbxError):
         gbx.attn_softmax_rows_pair(scores, hi, hi, rows=rows, L=S, S=S, scale=scale)
 

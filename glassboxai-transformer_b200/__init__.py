@@ -60,6 +60,7 @@ SIGNATURES = {
     "gbx_select_tokens": [_vp, _i64, _int, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
     "gbx_split_tf32": [_vp, _vp, _vp, _i64, _vp],
     "gbx_linear": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp],
+    "gbx_linear_splitk": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _vp, _i64, _vp, _vp],
 }
 _RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
 
@@ -207,3 +208,12 @@ def attn_values(p_hi, p_lo, vt_hi, vt_lo, out, *, ld_out, B, S, H, hd, out_lo=No
     """out[(b*S+p)*ld_out + h*hd + i] = sum_s P[b, h, p, s] vt[b, h, i, s] on the tensor cores."""
     _check(lib().gbx_attn_values(_p(p_hi), _p(p_lo), _p(vt_hi), _p(vt_lo), _p(out), _p(out_lo), ld_out, B, S, H, hd,
                                  1 if causal else 0, _p(err_flag), _stream(stream)))
+
+
+def linear_splitk(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, ksplit, workspace, workspace_floats=None, bias=None,
+                  resid=None, y_lo=None, act=ACT_NONE, err_flag=None, stream=None):
+    """linear with K in ksplit slices, partial sums in `workspace` (>= ksplit*M*N floats)."""
+    if workspace_floats is None:
+        workspace_floats = workspace.numel() if hasattr(workspace, "numel") else 0
+    _check(lib().gbx_linear_splitk(_p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(resid), _p(y), _p(y_lo), M,
+                                   N, K, act, ksplit, _p(workspace), workspace_floats, _p(err_flag), _stream(stream)))

@@ -944,6 +944,7 @@ extern "C" int gbx_split_tf32(const float* x, float* hi, float* lo, int64_t n, g
 // pairs (M 256 tiles over two SMs) for M >= kLinPairMinRows unless
 // GBX_LINEAR_PAIR=0; GBX_LINEAR_PAIR=1 forces them.  Read once.
 constexpr int64_t kLinPairMinRows = 1024;
+constexpr int kLinMaxSplit = 16;   // K slices of gbx_linear_splitk
 
 static int env_int(const char* name, int dflt)
 {
@@ -1120,4 +1121,138 @@ extern "C" int gbx_transpose_heads(const float* v, int64_t ld, float* vt, int B,
     if (grid.y > 65535) return set_error(GBX_ERANGE, "gbx_transpose_heads: hd=%d", hd);
     transpose_heads_kernel<<<grid, dim3(32, 8), 0, reinterpret_cast<cudaStream_t>(stream)>>>(v, ld, vt, S, H, hd);
     return check_launch("gbx_transpose_heads");
+}
+
+// ------------------------------------------------------------------ split K
+// y[m, n] = act(sum_s ws[s][m][n] + bias[n]) + resid[m, n], the slices added
+// in the order s = 0, 1, ... (so results do not depend on scheduling), then
+// the tf32 split when y_lo is given: gbx_linear's epilogue on the summed
+// K slices.
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+splitk_reduce_kernel(const float* __restrict__ ws, int ksplit, const LinearArgs a)
+{
+    const int64_t MN = a.M * (int64_t)a.N;
+    if constexpr (VEC) {
+        const int64_t n4 = MN / 4;
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+             i += (int64_t)gridDim.x * blockDim.x) {
+            float4 v = *reinterpret_cast<const float4*>(ws + 4 * i);
+            for (int s = 1; s < ksplit; ++s) {
+                const float4 w = *reinterpret_cast<const float4*>(ws + s * MN + 4 * i);
+                v = make_float4(v.x + w.x, v.y + w.y, v.z + w.z, v.w + w.w);
+            }
+            // the epilogue of epi_store16, on 4 columns (N % 4 == 0: all in one row)
+            const int n = (int)((4 * i) % a.N);
+            if (a.bias) {
+                const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + n));
+                v = make_float4(v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
+            }
+            if (a.act == GBX_ACT_GELU) v = make_float4(gelu_tanh(v.x), gelu_tanh(v.y), gelu_tanh(v.z), gelu_tanh(v.w));
+            if (a.resid) {
+                const float4 r = *reinterpret_cast<const float4*>(a.resid + 4 * i);
+                v = make_float4(r.x + v.x, r.y + v.y, r.z + v.z, r.w + v.w);
+            }
+            if (a.y_lo) {
+                float4 h, l;
+                split4(v, h, l);
+                *reinterpret_cast<float4*>(a.y + 4 * i) = h;
+                *reinterpret_cast<float4*>(a.y_lo + 4 * i) = l;
+            } else {
+                *reinterpret_cast<float4*>(a.y + 4 * i) = v;
+            }
+        }
+    } else {
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < MN; i += (int64_t)gridDim.x * blockDim.x) {
+            float v = ws[i];
+            for (int s = 1; s < ksplit; ++s) v += ws[s * MN + i];
+            const int64_t row = i / a.N;
+            const int n = (int)(i - row * a.N);
+            const float o = epi_value(v, n, row, a);
+            if (a.y_lo) {
+                float h, l;
+                split_value(o, h, l);
+                a.y[i] = h;
+                a.y_lo[i] = l;
+            } else {
+                a.y[i] = o;
+            }
+        }
+    }
+}
+
+// gbx_linear with K cut into ksplit slices of K / ksplit: every slice is a
+// "head" of the heads mode (its x and w columns a box offset in K), written
+// as fp32 partial sums into ws, then splitk_reduce_kernel adds the slices and
+// applies the epilogue.  Returns GBX_OK after enqueueing both launches.
+static int linear_splitk(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo, const float* bias,
+                         const float* resid, float* y, float* y_lo, int64_t M, int N, int K, int act, int ksplit,
+                         float* ws, int* err_flag, cudaStream_t s, const char* what)
+{
+    const int Kp = K / ksplit;
+    const HeadsOperand x{x_hi, x_lo, K, Kp, 0, (int)M, true};
+    const HeadsOperand w{w_hi, w_lo, K, Kp, 0, N, true};
+    int rc = heads_gemm(what, x, w, ws, nullptr, N, M * (int64_t)N, 0, 1, ksplit, (int)M, N, Kp, 0, 0, err_flag, s);
+    if (rc != GBX_OK) return rc;
+    LinearArgs a;
+    a.bias = bias;
+    a.resid = resid;
+    a.y = y;
+    a.y_lo = y_lo;
+    a.err = err_flag;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.act = act;
+    const bool vec = N % 4 == 0 && aligned16(y) && (!y_lo || aligned16(y_lo)) && (!resid || aligned16(resid)) &&
+                     (!bias || aligned16(bias)) && aligned16(ws);
+    const int64_t work = vec ? (M * (int64_t)N / 4 + 255) / 256 : (M * (int64_t)N + 255) / 256;
+    if (vec) {
+        const int grid = persistent_grid(splitk_reduce_kernel<true>, 256, 0, work, 8);
+        if (grid < 1) return GBX_ECUDA;
+        splitk_reduce_kernel<true><<<grid, 256, 0, s>>>(ws, ksplit, a);
+    } else {
+        const int grid = persistent_grid(splitk_reduce_kernel<false>, 256, 0, work, 8);
+        if (grid < 1) return GBX_ECUDA;
+        splitk_reduce_kernel<false><<<grid, 256, 0, s>>>(ws, ksplit, a);
+    }
+    return check_launch(what);
+}
+
+// Arguments of the split-K entry points: GBX_OK, or the code gbx_linear
+// would return; *use_split is false when the call should simply run
+// gbx_linear (ksplit 1, or a shape the sliced tensor maps cannot take).
+static int splitk_args(const char* what, const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
+                       const float* y, const float* y_lo, int64_t M, int N, int K, int ksplit, bool* use_split)
+{
+    *use_split = false;
+    if (ksplit < 1 || ksplit > kLinMaxSplit) return set_error(GBX_EINVAL, "%s: ksplit=%d", what, ksplit);
+    if (M < 0 || N <= 0 || K <= 0) return set_error(GBX_EINVAL, "%s: M=%lld N=%d K=%d", what, (long long)M, N, K);
+    if (M > 0x7fffffffLL) return set_error(GBX_ERANGE, "%s: M=%lld", what, (long long)M);
+    auto al16 = [](const void* p) { return p == nullptr || aligned16(p); };
+    *use_split = ksplit > 1 && M > 0 && K % ksplit == 0 && (K / ksplit) % 4 == 0 && x_hi && w_hi && y &&
+                 al16(x_hi) && al16(x_lo) && al16(w_hi) && al16(w_lo) && y_lo != y;
+    return GBX_OK;
+}
+
+extern "C" int gbx_linear_splitk(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
+                                 const float* bias, const float* resid, float* y, float* y_lo, int64_t M, int N, int K,
+                                 int act, int ksplit, float* workspace, int64_t workspace_floats, int* err_flag,
+                                 gbx_stream_t stream)
+{
+    bool split = false;
+    if (int rc = splitk_args("gbx_linear_splitk", x_hi, x_lo, w_hi, w_lo, y, y_lo, M, N, K, ksplit, &split)) return rc;
+    if (!split) return gbx_linear(x_hi, x_lo, w_hi, w_lo, bias, resid, y, y_lo, M, N, K, act, err_flag, stream);
+    if (act != GBX_ACT_NONE && act != GBX_ACT_GELU) return set_error(GBX_EINVAL, "gbx_linear_splitk: act=%d", act);
+    if (!workspace || workspace_floats < (int64_t)ksplit * M * N)
+        return set_error(GBX_EINVAL, "gbx_linear_splitk: workspace of %lld floats, %lld needed",
+                         (long long)workspace_floats, (long long)ksplit * M * N);
+    const float* ws_end = workspace + (int64_t)ksplit * M * N;
+    auto overlaps = [&](const float* p, int64_t n) { return p && p < ws_end && workspace < p + n; };
+    if (overlaps(y, M * (int64_t)N) || overlaps(y_lo, M * (int64_t)N) || overlaps(resid, M * (int64_t)N) ||
+        overlaps(x_hi, M * (int64_t)K) || overlaps(x_lo, M * (int64_t)K) || overlaps(w_hi, (int64_t)N * K) ||
+        overlaps(w_lo, (int64_t)N * K))
+        return set_error(GBX_EINVAL, "gbx_linear_splitk: workspace overlaps an operand");
+    return linear_splitk(x_hi, x_lo, w_hi, w_lo, bias, resid, y, y_lo, M, N, K, act, ksplit, workspace, err_flag,
+                         reinterpret_cast<cudaStream_t>(stream), "gbx_linear_splitk");
 }

@@ -55,6 +55,20 @@ namespace {
 // the low half of the probabilities
 constexpr int64_t kScoreGroupFloats = (int64_t)1 << 28;
 
+// K slices for a contraction of M rows x N outputs over K: a contraction with
+// fewer output tiles than half the GPU's tile slots (one 1024-token sequence
+// against a d x d matrix) is cut into slices, ksplit doubling while the
+// tiles still fit in the slots and each slice keeps at least 256 of K.
+int splitk_of(int64_t M, int N, int K, int sm_count)
+{
+    const bool pair_tiles = M >= 1024;   // gbx_linear's CTA-pair threshold
+    const int64_t slots = pair_tiles ? sm_count / 2 : sm_count;
+    const int64_t tiles = ((M + (pair_tiles ? 255 : 127)) / (pair_tiles ? 256 : 128)) * ((N + 255) / 256);
+    int ks = 1;
+    while (ks < 8 && tiles * ks * 2 <= slots && K % (8 * ks) == 0 && K / (2 * ks) >= 256) ks *= 2;
+    return ks;
+}
+
 struct DevBuf {
     float* p = nullptr;
     size_t n = 0;
@@ -87,7 +101,9 @@ struct TransformerModel::Impl {
     // activations (ln, qkv, scores (as probabilities), vt, attn and up hold
     // the hi half of a tf32 pair, *_lo the low half)
     DevBuf h, ln, ln_lo, qkv, qkv_lo, scores, probs_lo, vt, vt_lo, attn, attn_lo, up, up_lo, last_h, last_y, logits;
+    DevBuf splitk_ws;      // partial sums of the K-split contractions
     int score_group = 1;   // sequences per attention launch
+    int sm_count = 148;
     int32_t* ids = nullptr;
     size_t ids_n = 0;
     int32_t* err = nullptr;
@@ -120,7 +136,7 @@ struct TransformerModel::Impl {
     ~Impl()
     {
         for (DevBuf* b : {&h, &ln, &ln_lo, &qkv, &qkv_lo, &scores, &probs_lo, &vt, &vt_lo, &attn, &attn_lo, &up, &up_lo,
-                          &last_h, &last_y, &logits})
+                          &last_h, &last_y, &logits, &splitk_ws})
             b->release();
         for (float* p : owned) cudaFree(p);
         if (ids) cudaFree(ids);
@@ -153,6 +169,8 @@ bool TransformerModel::loadModel(const std::string& ggufPath)
     Impl& m = *impl_;
     if (cudaGetDevice(&m.device) != cudaSuccess) return fail("no CUDA device");
     if (cudaStreamCreateWithFlags(&m.stream, cudaStreamNonBlocking) != cudaSuccess) return fail("stream");
+    if (cudaDeviceGetAttribute(&m.sm_count, cudaDevAttrMultiProcessorCount, m.device) != cudaSuccess || m.sm_count < 1)
+        return fail("no CUDA device properties");
     if (cudaMalloc(&m.err, sizeof(int32_t)) != cudaSuccess || cudaMalloc(&m.sel_ids, 2 * sizeof(int32_t)) != cudaSuccess ||
         cudaMalloc(&m.sel_logit, sizeof(float)) != cudaSuccess || cudaMalloc(&m.sel_u, sizeof(double)) != cudaSuccess)
         return fail("cudaMalloc");
@@ -248,12 +266,20 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
     int64_t G = kScoreGroupFloats / per_seq;
     G = G < 1 ? 1 : (G > B ? B : G);
     m.score_group = (int)G;
+    // the largest split-K workspace of the four contractions
+    size_t ws = 1;
+    const int64_t shapes[4][2] = {{3 * d, d}, {d, d}, {F, d}, {d, F}};
+    for (const auto& nk : shapes) {
+        const int ks = splitk_of(tokens, (int)nk[0], (int)nk[1], m.sm_count);
+        if (ks > 1 && (size_t)(ks * tokens * nk[0]) > ws) ws = (size_t)(ks * tokens * nk[0]);
+    }
     const bool ok = m.h.ensure(tokens * d) && m.ln.ensure(tokens * d) && m.ln_lo.ensure(tokens * d) &&
                     m.qkv.ensure(tokens * 3 * d) && m.qkv_lo.ensure(tokens * 3 * d) &&
                     m.scores.ensure((size_t)(G * per_seq)) && m.probs_lo.ensure((size_t)(G * per_seq)) &&
                     m.vt.ensure((size_t)(G * seq * d)) && m.vt_lo.ensure((size_t)(G * seq * d)) &&
                     m.attn.ensure(tokens * d) && m.attn_lo.ensure(tokens * d) && m.up.ensure(tokens * F) &&
-                    m.up_lo.ensure(tokens * F) && m.last_h.ensure(B * d) && m.last_y.ensure(B * d) &&
+                    m.up_lo.ensure(tokens * F) && m.splitk_ws.ensure(ws) && m.last_h.ensure(B * d) &&
+                    m.last_y.ensure(B * d) &&
                     m.logits.ensure((size_t)B * vocab_);
     if (!ok) return fail("cudaMalloc of activation buffers failed");
     if ((size_t)tokens > m.ids_n) {
@@ -354,10 +380,17 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
     auto check = [&](int r) {
         if (rc == GBX_OK && r != GBX_OK) rc = r;
     };
-    // y[M, Nout] = act(x . W^T + bias) + resid on the tensor cores, x and W as tf32 pairs
+    // y[M, Nout] = act(x . W^T + bias) + resid on the tensor cores, x and W as
+    // tf32 pairs; K-split (splitk_of) when the output tiles are few
     auto linear = [&](const float* xh, const float* xl, const Impl::Pair& W, const float* bias, const float* resid,
                       float* y, float* y_lo, int64_t M, int Nout, int K, int act) {
-        check(gbx_linear(xh, xl, W.hi, W.lo, bias, resid, y, y_lo, M, Nout, K, act, m.err, gs));
+        const int ks = splitk_of(M, Nout, K, m.sm_count);
+        if (ks > 1) {
+            check(gbx_linear_splitk(xh, xl, W.hi, W.lo, bias, resid, y, y_lo, M, Nout, K, act, ks, m.splitk_ws.p,
+                                    (int64_t)m.splitk_ws.n, m.err, gs));
+        } else {
+            check(gbx_linear(xh, xl, W.hi, W.lo, bias, resid, y, y_lo, M, Nout, K, act, m.err, gs));
+        }
     };
 
     if (cudaMemcpyAsync(m.ids, tokenIDs.data(), N * sizeof(int32_t), cudaMemcpyHostToDevice, st) != cudaSuccess ||

@@ -264,6 +264,24 @@ int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const fl
                const float* resid, float* y, float* y_lo, int64_t M, int N, int K, int act, int* err_flag,
                gbx_stream_t stream);
 
+/*
+ * gbx_linear with K cut into ksplit slices of K / ksplit (1 <= ksplit <= 16),
+ * for contractions with too few output tiles to fill the GPU (one sequence
+ * of 1024 tokens against a d x d projection: 16 CTA-pair tiles for 74 SM
+ * pairs).  No counterpart in the reference: the same result as gbx_linear
+ * (same epilogue, same operands) from ksplit times the tiles.  Each slice's
+ * fp32 partial sums go to `workspace` (device, at least ksplit * M * N
+ * floats, overlapping no operand), then one pass adds the slices in order
+ * (s = 0, 1, ...: deterministic) and applies bias, act, resid and the
+ * optional tf32 split.  Rounding differs from gbx_linear's by ksplit - 1 fp32
+ * additions per output.  When ksplit is 1, or K / ksplit is not a multiple
+ * of 4, or an operand is off 16-byte alignment, it runs gbx_linear instead
+ * and leaves the workspace untouched.
+ */
+int gbx_linear_splitk(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo, const float* bias,
+                      const float* resid, float* y, float* y_lo, int64_t M, int N, int K, int act, int ksplit,
+                      float* workspace, int64_t workspace_floats, int* err_flag, gbx_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * The per-head attention products on the tcgen05 tensor cores, for B
  * sequences of S tokens, H heads of width hd, every operand a tf32 pair (the

@@ -364,6 +364,68 @@ def test_linear_rejects_bad_arguments(gbx, cuda):
         gbx.linear(x, None, w, None, y, M=8, N=8, K=8, y_lo=y)
 
 
+@pytest.mark.parametrize("M,N,K,ksplit,act,res,pair", [
+    (1024, 1024, 1024, 4, 0, 1, False), (1024, 1024, 4096, 4, 0, 1, False), (256, 1600, 1600, 4, 0, 1, False),
+    (300, 6400, 1600, 2, 1, 0, True), (37, 100, 20, 5, 1, 1, False), (64, 96, 64, 16, 0, 0, True),
+    (50, 70, 36, 3, 1, 1, True)])
+def test_linear_splitk(gbx, cuda, M, N, K, ksplit, act, res, pair):
+    """K in slices (every slice a head of the heads mode), then the ordered
+    sum of the partials with the epilogue: within gbx_linear's bound plus
+    one fp32 addition per slice."""
+    import torch
+    rng = np.random.default_rng(M + N + K + ksplit)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    r = rng.standard_normal((M, N)).astype(np.float32)
+    xd, wd, bd, rd = (torch.from_numpy(a).cuda() for a in (x, w, b, r))
+    xh, xl = _split(gbx, torch, xd)
+    wh, wl = _split(gbx, torch, wd)
+    full, y = _guarded(torch, M, N)
+    full_lo, y_lo = _guarded(torch, M, N)
+    ws_full = torch.full((ksplit * M * N + 128,), float("nan"), device="cuda")
+    ws = ws_full[64:64 + ksplit * M * N]
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gbx.linear_splitk(xh, xl, wh, wl, y, M=M, N=N, K=K, ksplit=ksplit, workspace=ws, bias=bd,
+                      resid=rd if res else None, y_lo=y_lo if pair else None, act=act, err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    want, tol = _expected(x, w, b, r if res else None, act)
+    mag = np.abs(x.astype(np.float64)) @ np.abs(w.astype(np.float64)).T
+    tol = tol + (ksplit + 1) * 2.0 ** -24 * mag * (1.2 if act else 1.0)
+    got = y.cpu().numpy().astype(np.float64)
+    if pair:
+        got = got + y_lo.cpu().numpy()
+        _check_guards(full_lo)
+    _assert_within(got, want, tol, f"split-K {M}x{N}x{K}/{ksplit} act={act} resid={res} pair={pair}")
+    _check_guards(full)
+    h = ws_full.cpu().numpy()
+    assert np.all(np.isnan(h[:64])) and np.all(np.isnan(h[-64:])), "write outside the workspace"
+
+
+def test_linear_splitk_falls_back_and_checks_workspace(gbx, cuda):
+    import torch
+    rng = np.random.default_rng(5)
+    M, N, K = 40, 64, 30   # K / 4 is not a multiple of 4: gbx_linear runs, the workspace is untouched
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+    w = torch.from_numpy((0.02 * rng.standard_normal((N, K))).astype(np.float32)).cuda()
+    y1 = torch.empty((M, N), device="cuda")
+    y2 = torch.empty((M, N), device="cuda")
+    ws = torch.full((4 * M * N,), 7.0, device="cuda")
+    gbx.linear(x, None, w, None, y1, M=M, N=N, K=K)
+    gbx.linear_splitk(x, None, w, None, y2, M=M, N=N, K=K, ksplit=4, workspace=ws)
+    assert torch.equal(y1, y2) and bool(torch.all(ws == 7.0))
+    K = 64
+    x = torch.zeros((M, K), device="cuda")
+    w = torch.zeros((N, K), device="cuda")
+    with pytest.raises(gbx.GbxError):   # workspace too small
+        gbx.linear_splitk(x, None, w, None, y1, M=M, N=N, K=K, ksplit=4, workspace=ws, workspace_floats=4 * M * N - 1)
+    with pytest.raises(gbx.GbxError):   # workspace overlapping the output
+        gbx.linear_splitk(x, None, w, None, ws, M=M, N=N, K=K, ksplit=2, workspace=ws)
+    with pytest.raises(gbx.GbxError):
+        gbx.linear_splitk(x, None, w, None, y1, M=M, N=N, K=K, ksplit=17, workspace=ws)
+
+
 _SUBPROCESS_CASES = r"""
 import importlib, sys
 import numpy as np, torch

@@ -61,6 +61,7 @@ SIGNATURES = {
     "gbx_split_tf32": [_vp, _vp, _vp, _i64, _vp],
     "gbx_linear": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp],
     "gbx_linear_splitk": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _vp, _i64, _vp, _vp],
+    "gbx_linear_splitk_noalloc": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp],
 }
 _RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
 
@@ -217,3 +218,14 @@ def linear_splitk(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, ksplit, workspace, work
         workspace_floats = workspace.numel() if hasattr(workspace, "numel") else 0
     _check(lib().gbx_linear_splitk(_p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(resid), _p(y), _p(y_lo), M,
                                    N, K, act, ksplit, _p(workspace), workspace_floats, _p(err_flag), _stream(stream)))
+
+
+NOALLOC_SCRATCH_FLOATS = 1 << 22
+
+
+def linear_splitk_noalloc(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, ksplit, bias=None, resid=None, y_lo=None,
+                          act=ACT_NONE, err_flag=None, stream=None):
+    """linear_splitk with the partial sums in the library's own scratch array
+    (ksplit*M*N <= NOALLOC_SCRATCH_FLOATS); allocates nothing."""
+    _check(lib().gbx_linear_splitk_noalloc(_p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(resid), _p(y),
+                                           _p(y_lo), M, N, K, act, ksplit, _p(err_flag), _stream(stream)))

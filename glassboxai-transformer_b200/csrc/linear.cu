@@ -1256,3 +1256,59 @@ extern "C" int gbx_linear_splitk(const float* x_hi, const float* x_lo, const flo
     return linear_splitk(x_hi, x_lo, w_hi, w_lo, bias, resid, y, y_lo, M, N, K, act, ksplit, workspace, err_flag,
                          reinterpret_cast<cudaStream_t>(stream), "gbx_linear_splitk");
 }
+
+// ------------------------------------------------------------------ split K, no allocation
+// gbx_linear_splitk for callers that cannot allocate device memory: the
+// partial sums go to this file-scope array instead of a caller's workspace.
+// Every GPU that loads the library holds it (16 MiB) until the process exits.
+// Its name is only a host-side stand-in in host code; the device address
+// comes from cudaGetSymbolAddress, once per device (splitk_scratch_of).
+constexpr int64_t kNoAllocScratchFloats = (int64_t)1 << 22;
+static __device__ __align__(256) float g_splitk_scratch[kNoAllocScratchFloats];
+
+// The scratch array's device address on the current device, looked up on
+// the first call for that device (with it current) and cached; nullptr and a
+// recorded error when the runtime cannot give it.
+static float* splitk_scratch_of(const char* what)
+{
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static float* addr[kMaxDevices] = {};
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_error(GBX_ECUDA, "%s: no current CUDA device (or device %d beyond %d)", what, dev, kMaxDevices);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_splitk_scratch);
+        if (e != cudaSuccess || !p) {
+            set_error(GBX_ECUDA, "%s: cudaGetSymbolAddress of the scratch array failed: %s", what, cudaGetErrorString(e));
+            return nullptr;
+        }
+        addr[dev] = static_cast<float*>(p);
+    }
+    return addr[dev];
+}
+
+extern "C" int gbx_linear_splitk_noalloc(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
+                                         const float* bias, const float* resid, float* y, float* y_lo, int64_t M, int N,
+                                         int K, int act, int ksplit, int* err_flag, gbx_stream_t stream)
+{
+    bool split = false;
+    if (int rc = splitk_args("gbx_linear_splitk_noalloc", x_hi, x_lo, w_hi, w_lo, y, y_lo, M, N, K, ksplit, &split))
+        return rc;
+    if (!split) return gbx_linear(x_hi, x_lo, w_hi, w_lo, bias, resid, y, y_lo, M, N, K, act, err_flag, stream);
+    if (act != GBX_ACT_NONE && act != GBX_ACT_GELU)
+        return set_error(GBX_EINVAL, "gbx_linear_splitk_noalloc: act=%d", act);
+    if ((int64_t)ksplit * M * N > kNoAllocScratchFloats)
+        return set_error(GBX_ERANGE,
+                         "gbx_linear_splitk_noalloc: ksplit * M * N = %lld partial sums exceed the library's scratch "
+                         "of %lld floats; use gbx_linear_splitk with a workspace",
+                         (long long)ksplit * M * N, (long long)kNoAllocScratchFloats);
+    float* ws = splitk_scratch_of("gbx_linear_splitk_noalloc");
+    if (!ws) return GBX_ECUDA;
+    return linear_splitk(x_hi, x_lo, w_hi, w_lo, bias, resid, y, y_lo, M, N, K, act, ksplit, ws, err_flag,
+                         reinterpret_cast<cudaStream_t>(stream), "gbx_linear_splitk_noalloc");
+}

@@ -282,6 +282,27 @@ int gbx_linear_splitk(const float* x_hi, const float* x_lo, const float* w_hi, c
                       const float* resid, float* y, float* y_lo, int64_t M, int N, int K, int act, int ksplit,
                       float* workspace, int64_t workspace_floats, int* err_flag, gbx_stream_t stream);
 
+/*
+ * gbx_linear_splitk for callers that cannot allocate device memory: a binding
+ * or plugin host that owns every device buffer and gives the library only
+ * the inputs and outputs, or a latency-critical caller for which
+ * cudaMalloc's implicit synchronization is not acceptable.  No counterpart
+ * in the reference.  The partial sums go to a scratch array inside the
+ * library (16 MiB, held on every GPU that loads the library until the
+ * process exits), so ksplit * M * N may be at most 4,194,304 (GBX_ERANGE
+ * otherwise; gbx_linear_splitk takes any size).  Nothing is allocated,
+ * freed or cleared per call: every call writes each scratch element it later
+ * reads.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current) and caches it; make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls that can overlap on the GPU (other streams, other host threads)
+ * race on it and must be serialised by the caller.  Results are those of
+ * gbx_linear_splitk; ksplit 1 or an unsliceable shape runs gbx_linear.
+ */
+int gbx_linear_splitk_noalloc(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
+                              const float* bias, const float* resid, float* y, float* y_lo, int64_t M, int N, int K,
+                              int act, int ksplit, int* err_flag, gbx_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * The per-head attention products on the tcgen05 tensor cores, for B
  * sequences of S tokens, H heads of width hd, every operand a tf32 pair (the

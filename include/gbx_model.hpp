@@ -42,9 +42,11 @@
 //     argmax / temperature sampling of transformer.cu:994-1028 runs on the
 //     device (gbx_select_tokens), so the logits never cross to the host.
 //   - The weight contractions (QKV, projection, FFN up/down) run on the
-//     tcgen05 tensor cores (gbx_linear) with fp32 operands carried as tf32
-//     pairs, their bias, GELU and residual fused into the epilogue; the
-//     per-head score and P.V products are fp32 cuBLAS GEMMs.  The hot path
+//     tcgen05 tensor cores (gbx_linear, gbx_linear_splitk when the output
+//     tiles are few) with fp32 operands carried as tf32 pairs, their bias,
+//     GELU and residual fused into the epilogue; the per-head score and
+//     P.V products run on the same kernel (gbx_attn_scores,
+//     gbx_attn_values), every head of every sequence in one launch.  The hot path
 //     itself (embed, LayerNorm, score epilogue + softmax, logits) runs on the
 //     sm_100a kernels behind gbx.h.  Loading keeps a tf32 pair of every f32
 //     weight matrix on the device (two extra fp32 copies); f16 / bf16

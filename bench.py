@@ -698,7 +698,7 @@ def run_linear(args, shape, G, g, f32):
                       "speedup_vs_sgemm": sg / us}), flush=True)
 
 
-ATTN_KERNELS = ["attn_scores", "attn_values", "attn_block"]
+ATTN_KERNELS = ["attn_scores", "attn_values", "attn_block", "attn_fused"]
 
 
 def run_attn(args, shape, G, g, f32):
@@ -734,6 +734,12 @@ def run_attn(args, shape, G, g, f32):
 
     def values():
         G.attn_values(dots, p_lo, vt, vt_lo, out, ld_out=d, B=B, S=S, H=H, hd=hd, out_lo=out_lo, err_flag=err)
+
+    def fused():
+        G.transpose_heads(qh[:, 2 * d:], vt, ld=3 * d, B=B, S=S, H=H, hd=hd)
+        G.transpose_heads(ql[:, 2 * d:], vt_lo, ld=3 * d, B=B, S=S, H=H, hd=hd)
+        G.attn_fused(qh, ql, qh[:, d:], ql[:, d:], vt, vt_lo, out, ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=hd,
+                     scale=scale, out_lo=out_lo, err_flag=err)
 
     def block():
         G.attn_scores(qh, ql, qh[:, d:], ql[:, d:], dots2, ld=3 * d, B=B, S=S, H=H, hd=hd, err_flag=err)
@@ -775,18 +781,19 @@ def run_attn(args, shape, G, g, f32):
         return statistics.median([1000.0 * a.elapsed_time(e) for a, e in evs])
 
     ours, ref = {"attn_scores": (scores, ref_scores), "attn_values": (values, ref_values),
-                 "attn_block": (block, ref_block)}[args.kernel]
+                 "attn_block": (block, ref_block), "attn_fused": (fused, ref_block)}[args.kernel]
     us = timed(ours)
     if int(err.item()) != 0:
         raise SystemExit("an attention product reported a pipeline timeout")
     rus = timed(ref)
     per = 2.0 * B * H * S * S * hd   # one dense product, flops
-    flop = {"attn_scores": per, "attn_values": per, "attn_block": 2 * per}[args.kernel]
+    flop = {"attn_scores": per, "attn_values": per, "attn_block": 2 * per, "attn_fused": 2 * per}[args.kernel]
     print(json.dumps({"kernel": args.kernel, "workload": args.workload, "sequences": B, "seq": S, "heads": H,
                       "head_dim": hd, "causal": True, "median_us": us,
                       "dense_equiv_tflops": flop / (us * 1e-6) / 1e12,
                       "cublas_fp32_us": rus, "speedup_vs_cublas_fp32": rus / us,
-                      "cublas_path": "torch.bmm fp32 (TF32 off), dense; block: + scale, mask, torch.softmax"}),
+                      "cublas_path": "torch.bmm fp32 (TF32 off), dense; block, fused: + scale, mask, torch.softmax",
+                      "fused_includes": "the two V transposes" if args.kernel == "attn_fused" else None}),
           flush=True)
 
 

@@ -56,6 +56,7 @@ SIGNATURES = {
     "gbx_attn_scores": [_vp, _vp, _vp, _vp, _i64, _vp, _int, _int, _int, _int, _int, _vp, _vp],
     "gbx_transpose_heads": [_vp, _i64, _vp, _int, _int, _int, _int, _vp],
     "gbx_attn_values": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, _vp],
+    "gbx_attn_fused": [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _f, _int, _vp, _vp],
     "gbx_logits": [_vp, _i64, _vp, _int, _vp, _int, _int, _vp],
     "gbx_select_tokens": [_vp, _i64, _int, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
     "gbx_split_tf32": [_vp, _vp, _vp, _i64, _vp],
@@ -229,3 +230,10 @@ def linear_splitk_noalloc(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, ksplit, bias=No
     (ksplit*M*N <= NOALLOC_SCRATCH_FLOATS); allocates nothing."""
     _check(lib().gbx_linear_splitk_noalloc(_p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(resid), _p(y),
                                            _p(y_lo), M, N, K, act, ksplit, _p(err_flag), _stream(stream)))
+
+
+def attn_fused(q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo, out, *, ld, ld_out, B, S, H, hd, scale, out_lo=None, causal=True,
+               err_flag=None, stream=None):
+    """Self-attention of every head in one fused launch (tf32 pairs in; see gbx.h)."""
+    _check(lib().gbx_attn_fused(_p(q_hi), _p(q_lo), _p(k_hi), _p(k_lo), ld, _p(vt_hi), _p(vt_lo), _p(out), _p(out_lo),
+                                ld_out, B, S, H, hd, scale, 1 if causal else 0, _p(err_flag), _stream(stream)))

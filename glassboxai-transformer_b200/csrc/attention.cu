@@ -1,0 +1,550 @@
+// attention.cu -- causal self-attention of every head of every sequence in
+// one kernel on the sm_100a tensor cores, replacing attentionScoresKernel,
+// the per-head softmaxKernel launches and attentionOutputKernel
+// (transformer.cu:213-249, launched at :834-846):
+//   out[b, p, h*64 + i] = sum_s softmax_s(q_p . k_s / scale, s <= p) v[s, i]
+// without the [S, S] scores or probabilities ever reaching HBM.
+//
+// Precision is that of the rest of the library: every operand is a tf32 pair
+// and each product is formed as hi.hi + hi.lo + lo.hi; TMEM accumulates at
+// most 64 products of a sum (one head width, or one step of 64 keys), and
+// the output is summed over the steps in fp32 registers.  The softmax is the
+// online form: per row a running maximum m and sum l, e = expf(x - m), and a
+// rescale of the running output by expf(m_old - m_new) when the maximum
+// grows; the scores are divided by `scale` exactly (q = x * (1/scale) plus one
+// FMA correction, as gbx_attn_softmax_rows does) and keys past the diagonal
+// weigh exactly 0.  It differs from the reference's single-pass softmax only
+// in rounding (a few fp32 ulps of each weight).
+//
+// One CTA works on one (head, 128-query tile) unit at a time, persistent over
+// the units (longest first), 320 threads:
+//   warp 0      TMA producer: the unit's Q tile (128 x 64, hi and lo), then per
+//               step of 64 keys the K tile and the V^T tile into a two-stage
+//               ring (128-byte swizzled rows, 32 floats per K block)
+//   warp 1      owns 512 TMEM columns; one thread issues the MMAs:
+//                 S[j] = Q K_j^T                      (kind::tf32, M 128, N 64)
+//                 O[j] = P_j V_j                      (A = P_j from TMEM)
+//               S[j+1] is issued before O[j], so the tensor core computes the
+//               next scores while the softmax warps work on these
+//   warps 2-9   softmax: warps w and w + 4 own query rows 32 (w % 4) .. +31,
+//               32 of the 64 columns each; a thread reads its S[j] columns
+//               from TMEM, writes its part of P_j as a tf32 pair back into
+//               TMEM (hi over S[j]), then adds its 32 columns of O[j-1] into
+//               fp32 registers with the pending rescale
+// TMEM columns: S/P_hi [0,64) and [64,128), P_lo [128,192) and [192,256),
+// O [256,320) and [320,384), each double-buffered by step parity.
+// Every mbarrier wait is bounded (1 s, %globaltimer): a wait that runs out
+// sets the CTA's abort word, every role leaves its loops, loads and MMAs in
+// flight are waited for (bounded), TMEM is freed and GBX_LINEAR_TIMEOUT is
+// OR-ed into the error flag.  No cluster multicast.
+#include <cuda.h>
+
+#include "gbx_common.cuh"
+#include "tcgen05.cuh"
+#include "tensormap.cuh"
+#include "tf32.cuh"
+
+namespace gbx {
+
+constexpr int kAttQ = 128;        // query rows per unit (TMEM lanes)
+constexpr int kAttKT = 64;        // keys per step
+constexpr int kAttHD = 64;        // head width
+constexpr int kAttSoftWarps = 8;
+constexpr int kAttThreads = 64 + 32 * kAttSoftWarps;
+constexpr uint64_t kAttWaitNs = 1000000000ull;
+// shared memory: Q (2 planes x 2 K blocks x 128 rows x 128 B), then two ring
+// stages of K (2 x 2 x 64 rows x 128 B) and V^T (the same)
+constexpr uint32_t kAttQBlock = 128 * 128;                 // one plane, one K block of Q
+constexpr uint32_t kAttKVBlock = 64 * 128;                 // one plane, one K block of K or V^T
+constexpr uint32_t kAttQBytes = 4 * kAttQBlock;            // 64 KB
+constexpr uint32_t kAttKVBytes = 4 * kAttKVBlock;          // 32 KB
+constexpr uint32_t kAttStages = 2;
+constexpr uint32_t kAttData = kAttQBytes + kAttStages * 2 * kAttKVBytes;   // 192 KB
+// barriers: qfull qempty kfull[2] kempty[2] vfull[2] vempty[2] sfull[2] pfull[2] pvdone[2] ofull[2] oempty[2] drain
+constexpr int kAttBars = 21;
+// after the barriers and the TMEM slot: the softmax halves' exchange slots
+constexpr size_t kAttXBytes = 2 * 4 * 2 * 32 * sizeof(float);
+constexpr size_t kAttSmem = kAttData + 1024 + 8 * kAttBars + 16 + kAttXBytes;
+constexpr uint32_t kTmS = 0, kTmPlo = 128, kTmO = 256, kTmCols = 512;
+
+struct AttnArgs {
+    float* out;
+    float* out_lo;
+    int64_t ld_out;
+    int B, S, H;
+    int nqt;      // query tiles per head
+    int units;    // B * H * nqt
+    float scale;
+    float rscale;
+    int pow2;     // scale is a power of two: x / scale == x * rscale exactly
+    int causal;
+    int* err;
+};
+
+struct AttnUnit {
+    int b, h, qt, nkt;
+};
+
+__device__ __forceinline__ AttnUnit attn_unit(int u, const AttnArgs& a)
+{
+    const int Z = a.B * a.H;
+    AttnUnit w;
+    w.qt = a.nqt - 1 - u / Z;   // the longest query tiles first
+    const int z = u - (u / Z) * Z;
+    w.b = z / a.H;
+    w.h = z - w.b * a.H;
+    const int kend = a.causal ? min(a.S, (w.qt + 1) * kAttQ) : a.S;
+    w.nkt = (kend + kAttKT - 1) / kAttKT;
+    return w;
+}
+
+__device__ __forceinline__ float att_div(float x, float d, float rd)
+{
+    const float q = x * rd;
+    return fmaf(fmaf(-q, d, x), rd, q);
+}
+
+__global__ void __launch_bounds__(kAttThreads, 1)
+attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_constant__ CUtensorMap map_ql,
+                  const __grid_constant__ CUtensorMap map_kh, const __grid_constant__ CUtensorMap map_kl,
+                  const __grid_constant__ CUtensorMap map_vh, const __grid_constant__ CUtensorMap map_vl,
+                  const AttnArgs a)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAttData);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kAttBars);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const uint32_t b0 = tc::smem_u32(bars);
+    const uint32_t qfull = b0, qempty = b0 + 8;
+    auto kfull = [&](int s) { return b0 + 16 + 8 * s; };
+    auto kempty = [&](int s) { return b0 + 32 + 8 * s; };
+    auto vfull = [&](int s) { return b0 + 48 + 8 * s; };
+    auto vempty = [&](int s) { return b0 + 64 + 8 * s; };
+    auto sfull = [&](int i) { return b0 + 80 + 8 * i; };
+    auto pfull = [&](int i) { return b0 + 96 + 8 * i; };
+    auto pvdone = [&](int i) { return b0 + 112 + 8 * i; };
+    auto ofull = [&](int i) { return b0 + 128 + 8 * i; };
+    auto oempty = [&](int i) { return b0 + 144 + 8 * i; };
+    const uint32_t drain = b0 + 160;
+    const uint32_t smem0 = tc::smem_u32(smem);
+    const uint32_t qbase = smem0;
+    auto kbase = [&](int s) { return smem0 + kAttQBytes + s * 2 * kAttKVBytes; };
+    auto vbase = [&](int s) { return smem0 + kAttQBytes + s * 2 * kAttKVBytes + kAttKVBytes; };
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        tc::mbar_init(qfull, 1);
+        tc::mbar_init(qempty, 1);
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(kfull(s), 1);
+            tc::mbar_init(kempty(s), 1);
+            tc::mbar_init(vfull(s), 1);
+            tc::mbar_init(vempty(s), 1);
+            tc::mbar_init(sfull(s), 1);
+            tc::mbar_init(pfull(s), kAttSoftWarps);
+            tc::mbar_init(pvdone(s), 1);
+            tc::mbar_init(ofull(s), 1);
+            tc::mbar_init(oempty(s), kAttSoftWarps);
+        }
+        tc::mbar_init(drain, 1);
+        *abort = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch(&map_qh);
+        tc::tma_prefetch(&map_ql);
+        tc::tma_prefetch(&map_kh);
+        tc::tma_prefetch(&map_kl);
+        tc::tma_prefetch(&map_vh);
+        tc::tma_prefetch(&map_vl);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tc::smem_u32(tmem_slot), kTmCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------------------------------------------- producer
+            int st = 0;
+            uint32_t ph = 0, qph = 0;
+            bool ok = true;
+            int q_loads = 0;
+            uint32_t issued = 0, lastpar = 0;   // ring stages with loads issued, parity of their last phase
+            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+                const AttnUnit w = attn_unit(u, a);
+                if (!tc::mbar_wait(qempty, qph ^ 1, abort, kAttWaitNs)) break;
+                tc::mbar_arrive_expect_tx(qfull, kAttQBytes);
+                for (int p = 0; p < 2; ++p)
+                    for (int kb = 0; kb < 2; ++kb)
+                        tc::tma_load_4d(qbase + (2 * p + kb) * kAttQBlock, p ? &map_ql : &map_qh, qfull, 32 * kb, w.h,
+                                        w.qt * kAttQ, w.b);
+                ++q_loads;
+                qph ^= 1;
+                for (int j = 0; j < w.nkt; ++j) {
+                    if (!tc::mbar_wait(kempty(st), ph ^ 1, abort, kAttWaitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(kfull(st), kAttKVBytes);
+                    for (int p = 0; p < 2; ++p)
+                        for (int kb = 0; kb < 2; ++kb)
+                            tc::tma_load_4d(kbase(st) + (2 * p + kb) * kAttKVBlock, p ? &map_kl : &map_kh, kfull(st),
+                                            32 * kb, w.h, j * kAttKT, w.b);
+                    if (!tc::mbar_wait(vempty(st), ph ^ 1, abort, kAttWaitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(vfull(st), kAttKVBytes);
+                    for (int p = 0; p < 2; ++p)
+                        for (int kb = 0; kb < 2; ++kb)
+                            tc::tma_load_4d(vbase(st) + (2 * p + kb) * kAttKVBlock, p ? &map_vl : &map_vh, vfull(st),
+                                            j * kAttKT + 32 * kb, 0, w.h, w.b);
+                    issued |= 1u << st;
+                    lastpar = (lastpar & ~(1u << st)) | (ph << st);
+                    if (++st == 2) {
+                        st = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            // every load issued has landed before the CTA may exit
+            if (q_loads) tc::mbar_wait(qfull, (q_loads - 1) & 1, nullptr, kAttWaitNs);
+            for (int s = 0; s < 2; ++s)
+                if (issued & (1u << s)) {
+                    tc::mbar_wait(kfull(s), (lastpar >> s) & 1, nullptr, kAttWaitNs);
+                    tc::mbar_wait(vfull(s), (lastpar >> s) & 1, nullptr, kAttWaitNs);
+                }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------------------------------------------- MMA issuer
+            const uint32_t idesc = tc::idesc_tf32(kAttQ, kAttKT);   // both products: M 128, N 64
+            int kst = 0, vst = 0;
+            uint32_t kph = 0, vph = 0, qph = 0;
+            uint32_t g = 0;   // global step (buffer = g & 1, its use count = g >> 1)
+            bool ok = true;
+            // O[gg] = P_gg V_gg, the V tile in ring stage vst
+            auto pv = [&](uint32_t gg) -> bool {
+                const uint32_t i = gg & 1;
+                if (!tc::mbar_wait(pfull(i), (gg >> 1) & 1, abort, kAttWaitNs)) return false;
+                if (!tc::mbar_wait(vfull(vst), vph, abort, kAttWaitNs)) return false;
+                if (gg >= 2 && !tc::mbar_wait(oempty(i), ((gg - 2) >> 1) & 1, abort, kAttWaitNs)) return false;
+                tc::fence_after_sync();
+                const uint32_t d = tmem + kTmO + 64 * i;
+                const uint32_t phi = tmem + kTmS + 64 * i, plo = tmem + kTmPlo + 64 * i;
+#pragma unroll
+                for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) {
+                        const uint32_t k8 = 32 * kb + 8 * ks;   // key column of this K step
+                        const uint64_t vh = tc::smem_desc(vbase(vst) + kb * kAttKVBlock + 32 * ks, 128);
+                        const uint64_t vl = tc::smem_desc(vbase(vst) + (2 + kb) * kAttKVBlock + 32 * ks, 128);
+                        tc::mma_tf32_ts(d, phi + k8, vh, idesc, (kb | ks) != 0);
+                        tc::mma_tf32_ts(d, phi + k8, vl, idesc, 1);
+                        tc::mma_tf32_ts(d, plo + k8, vh, idesc, 1);
+                    }
+                tc::mma_commit(ofull(i));
+                tc::mma_commit(vempty(vst));
+                tc::mma_commit(pvdone(i));
+                if (++vst == 2) {
+                    vst = 0;
+                    vph ^= 1;
+                }
+                return true;
+            };
+            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+                const AttnUnit w = attn_unit(u, a);
+                if (!tc::mbar_wait(qfull, qph, abort, kAttWaitNs)) break;
+                qph ^= 1;
+                for (int j = 0; j < w.nkt; ++j, ++g) {
+                    const uint32_t i = g & 1;
+                    // S[g] overwrites buffer i: P_{g-2} there has been read by its MMA
+                    if (g >= 2 && !tc::mbar_wait(pvdone(i), ((g - 2) >> 1) & 1, abort, kAttWaitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    if (!tc::mbar_wait(kfull(kst), kph, abort, kAttWaitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t d = tmem + kTmS + 64 * i;
+#pragma unroll
+                    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint64_t qh = tc::smem_desc(qbase + kb * kAttQBlock + 32 * ks, 128);
+                            const uint64_t ql = tc::smem_desc(qbase + (2 + kb) * kAttQBlock + 32 * ks, 128);
+                            const uint64_t kh = tc::smem_desc(kbase(kst) + kb * kAttKVBlock + 32 * ks, 128);
+                            const uint64_t kl = tc::smem_desc(kbase(kst) + (2 + kb) * kAttKVBlock + 32 * ks, 128);
+                            tc::mma_tf32(d, qh, kh, idesc, (kb | ks) != 0);
+                            tc::mma_tf32(d, qh, kl, idesc, 1);
+                            tc::mma_tf32(d, ql, kh, idesc, 1);
+                        }
+                    tc::mma_commit(sfull(i));
+                    tc::mma_commit(kempty(kst));
+                    if (j == w.nkt - 1) tc::mma_commit(qempty);   // the unit's last read of Q
+                    if (++kst == 2) {
+                        kst = 0;
+                        kph ^= 1;
+                    }
+                    if (j >= 1 && !pv(g - 1)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                if (ok && !pv(g - 1)) ok = false;
+            }
+            // every MMA issued has completed before TMEM is freed
+            tc::mma_commit(drain);
+            tc::mbar_wait(drain, 0, nullptr, kAttWaitNs);
+        }
+    } else {
+        // -------------------------------------------------------- softmax
+        // Warps w and w + 4 share query rows 32 (w % 4) .. +31 (the TMEM lane
+        // quarter they may read); `half` picks the 32 of the 64 key (and
+        // output) columns this thread owns.  The two halves of a row exchange
+        // their step maxima through shared memory (double-buffered by step
+        // parity) at a 64-thread named barrier, keep their own partial sums
+        // (the same rescales apply to both) and add them at the end.
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row_in_tile = 32 * quarter + lane;
+        const uint32_t lane_addr = (uint32_t)(32 * quarter) << 16;
+        const uint32_t col = 32 * half;
+        float* const xmax = reinterpret_cast<float*>(tmem_slot + 4);   // [2 parity][4 quarter][2 half][32]
+        const int bar_id = 1 + quarter;                             // named barriers 1-4
+        auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
+        uint32_t g = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+            const AttnUnit w = attn_unit(u, a);
+            const int p = w.qt * kAttQ + row_in_tile;   // this thread's query position
+            const int lim = a.causal ? min(p + 1, a.S) : a.S;
+            float m = -INFINITY, l = 0.0f, alpha_pend = 0.0f;
+            float o[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = 0.0f;
+            // adds O[gg] (the running output rescaled first) and releases its buffer
+            auto take_o = [&](uint32_t gg, float alpha) -> bool {
+                const uint32_t i = gg & 1;
+                const bool ready = tc::mbar_wait(ofull(i), (gg >> 1) & 1, abort, kAttWaitNs);
+                if (!__all_sync(0xffffffffu, ready)) return false;
+                tc::fence_after_sync();
+                float v[32];
+                tc::tmem_ld32(tmem + lane_addr + kTmO + 64 * i + col, v);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha, v[c]);
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(oempty(i));
+                return true;
+            };
+            for (int j = 0; j < w.nkt; ++j, ++g) {
+                const uint32_t i = g & 1;
+                const bool ready = tc::mbar_wait(sfull(i), (g >> 1) & 1, abort, kAttWaitNs);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                float s[32];
+                tc::tmem_ld32(tmem + lane_addr + kTmS + 64 * i + col, s);
+                tc::tmem_ld_wait();
+                // keys k0 .. k0 + nvis - 1 of this thread's 32 are visible to its row
+                const int k0 = j * kAttKT + (int)col;
+                const int nvis = max(0, min(32, lim - k0));
+                const bool full = __all_sync(0xffffffffu, nvis == 32);
+                float mt = -INFINITY;
+                if (a.pow2) {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) s[c] *= a.rscale;   // exact: scale is a power of two
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) s[c] = att_div(s[c], a.scale, a.rscale);
+                }
+                if (full) {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) mt = fmaxf(mt, s[c]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c)
+                        if (c < nvis) mt = fmaxf(mt, s[c]);
+                }
+                // the row's step maximum: both halves
+                float* const xm = xmax + (((i * 4 + quarter) * 2) * 32);
+                xm[half * 32 + lane] = mt;
+                pair_sync();
+                mt = fmaxf(mt, xm[(1 - half) * 32 + lane]);
+                const float m_new = fmaxf(m, mt);
+                const float alpha = m_new == -INFINITY ? 1.0f : expf(m - m_new);
+                float sum = 0.0f;
+                if (full) {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        s[c] = expf(s[c] - m_new);
+                        sum += s[c];
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        s[c] = c < nvis ? expf(s[c] - m_new) : 0.0f;
+                        sum += s[c];
+                    }
+                }
+                l = fmaf(l, alpha, sum);
+                m = m_new;
+                // P as a tf32 pair (each weight is finite and at most 1): hi
+                // over S[g], lo in its own columns
+                float lo[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const float h = to_tf32(s[c]);
+                    lo[c] = to_tf32(s[c] - h);
+                    s[c] = h;
+                }
+                tc::tmem_st32(tmem + lane_addr + kTmS + 64 * i + col, s);
+                tc::tmem_st32(tmem + lane_addr + kTmPlo + 64 * i + col, lo);
+                tc::tmem_st_wait();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(pfull(i));
+                if (j >= 1 && !take_o(g - 1, alpha_pend)) {
+                    ok = false;
+                    break;
+                }
+                alpha_pend = alpha;
+            }
+            if (!ok || !take_o(g - 1, alpha_pend)) {
+                ok = false;
+                break;
+            }
+            // the row's sum: both halves (the slot of the last step's parity
+            // is free again: both halves have passed that step's barrier)
+            float* const xl = xmax + ((((g & 1) * 4 + quarter) * 2) * 32);
+            xl[half * 32 + lane] = l;
+            pair_sync();
+            l += xl[(1 - half) * 32 + lane];
+            pair_sync();   // the slot is read before either half writes it again
+            if (p < a.S) {
+                const float rl = 1.0f / l;
+                const int64_t off = ((int64_t)w.b * a.S + p) * a.ld_out + (int64_t)w.h * kAttHD + col;
+#pragma unroll
+                for (int c = 0; c < 32; c += 4) {
+                    float4 v = make_float4(att_div(o[c], l, rl), att_div(o[c + 1], l, rl), att_div(o[c + 2], l, rl),
+                                           att_div(o[c + 3], l, rl));
+                    if (a.out_lo) {
+                        float4 h4, l4;
+                        split4(v, h4, l4);
+                        *reinterpret_cast<float4*>(a.out + off + c) = h4;
+                        *reinterpret_cast<float4*>(a.out_lo + off + c) = l4;
+                    } else {
+                        *reinterpret_cast<float4*>(a.out + off + c) = v;
+                    }
+                }
+            }
+        }
+    }
+
+    __syncthreads();   // every role has left its loop (all waits are bounded)
+    if (warp == 1) {
+        __syncwarp();
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmCols);
+    }
+    if (threadIdx.x == 0 && *abort && a.err) atomicOr(a.err, GBX_LINEAR_TIMEOUT);
+}
+
+// One plane of a heads-mode operand as a 4-D map: dims (inner k, then d1, d2,
+// d3) with element strides s1 < s2 < s3, boxes of 32 x box1 x box2 x 1 and
+// the 128-byte swizzle.
+static int attn_map(CUtensorMap* m, const float* base, const cuuint64_t (&dims)[4], const cuuint64_t (&strides)[3],
+                    cuuint32_t box1, cuuint32_t box2)
+{
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return set_error(GBX_ECUDA, "gbx_attn_fused: cuTensorMapEncodeTiled unavailable from the driver");
+    cuuint64_t sb[3];
+    for (int i = 0; i < 3; ++i) sb[i] = strides[i] * sizeof(float);
+    const cuuint32_t box[4] = {32, box1, box2, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, sb, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(GBX_EINVAL, "gbx_attn_fused: tensor map rejected (CUresult %d)", (int)r);
+    return GBX_OK;
+}
+
+}  // namespace gbx
+
+using namespace gbx;
+
+extern "C" int gbx_attn_fused(const float* q_hi, const float* q_lo, const float* k_hi, const float* k_lo, int64_t ld,
+                              const float* vt_hi, const float* vt_lo, float* out, float* out_lo, int64_t ld_out, int B,
+                              int S, int H, int hd, float scale, int causal, int* err_flag, gbx_stream_t stream)
+{
+    if (B <= 0 || S <= 0 || H <= 0 || hd <= 0)
+        return set_error(GBX_EINVAL, "gbx_attn_fused: B=%d S=%d H=%d hd=%d", B, S, H, hd);
+    if (hd != kAttHD) return set_error(GBX_EINVAL, "gbx_attn_fused: head width %d (64 only)", hd);
+    if (!(scale >= 1.17549435e-38f) || scale == INFINITY)
+        return set_error(GBX_EINVAL, "gbx_attn_fused: scale=%g must be a normal positive float", (double)scale);
+    if (!q_hi || !q_lo || !k_hi || !k_lo || !vt_hi || !vt_lo || !out)
+        return set_error(GBX_EINVAL, "gbx_attn_fused: null pointer");
+    if (ld < (int64_t)H * hd || ld_out < (int64_t)H * hd)
+        return set_error(GBX_EINVAL, "gbx_attn_fused: ld=%lld ld_out=%lld < H*hd", (long long)ld, (long long)ld_out);
+    if (out_lo == out) return set_error(GBX_EINVAL, "gbx_attn_fused: out_lo aliases out");
+    // the tensor maps: 16-byte bases and strides; the vector output stores
+    const bool al = aligned16(q_hi) && aligned16(q_lo) && aligned16(k_hi) && aligned16(k_lo) && aligned16(vt_hi) &&
+                    aligned16(vt_lo) && aligned16(out) && (!out_lo || aligned16(out_lo));
+    if (!al || ld % 4 || ld_out % 4 || S % 4)
+        return set_error(GBX_EINVAL, "gbx_attn_fused: operands need 16-byte alignment and ld, ld_out, S multiples of 4");
+    const int nqt = (S + kAttQ - 1) / kAttQ;
+    if ((int64_t)B * H * nqt > 0x7fffffffLL || (int64_t)B * S > 0x7fffffffLL)
+        return set_error(GBX_ERANGE, "gbx_attn_fused: B=%d H=%d S=%d too large", B, H, S);
+    DeviceInfo di;
+    if (device_info(&di) != GBX_OK) return GBX_ECUDA;
+    if ((size_t)di.max_smem_optin < kAttSmem)
+        return set_error(GBX_ERANGE, "gbx_attn_fused: needs %zu bytes of shared memory per CTA", kAttSmem);
+
+    // Q and K: element (b, s, h, i) at b*S*ld + s*ld + h*64 + i, dims (i, h, s, b);
+    // V^T: element (b, h, i, s) at ((b*H + h)*64 + i)*S + s, dims (s, i, h, b)
+    CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+    const cuuint64_t dqk[4] = {(cuuint64_t)hd, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+    const cuuint64_t sqk[3] = {(cuuint64_t)hd, (cuuint64_t)ld, (cuuint64_t)S * ld};
+    const cuuint64_t dv[4] = {(cuuint64_t)S, (cuuint64_t)hd, (cuuint64_t)H, (cuuint64_t)B};
+    const cuuint64_t sv[3] = {(cuuint64_t)S, (cuuint64_t)hd * S, (cuuint64_t)H * hd * S};
+    int rc;
+    if ((rc = attn_map(&mqh, q_hi, dqk, sqk, 1, kAttQ)) || (rc = attn_map(&mql, q_lo, dqk, sqk, 1, kAttQ)) ||
+        (rc = attn_map(&mkh, k_hi, dqk, sqk, 1, kAttKT)) || (rc = attn_map(&mkl, k_lo, dqk, sqk, 1, kAttKT)) ||
+        (rc = attn_map(&mvh, vt_hi, dv, sv, kAttHD, 1)) || (rc = attn_map(&mvl, vt_lo, dv, sv, kAttHD, 1)))
+        return rc;
+    AttnArgs a;
+    a.out = out;
+    a.out_lo = out_lo;
+    a.ld_out = ld_out;
+    a.B = B;
+    a.S = S;
+    a.H = H;
+    a.nqt = nqt;
+    a.units = B * H * nqt;
+    a.scale = scale;
+    a.rscale = 1.0f / scale;
+    {
+        int e = 0;
+        a.pow2 = frexpf(scale, &e) == 0.5f ? 1 : 0;
+    }
+    a.causal = causal ? 1 : 0;
+    a.err = err_flag;
+    if (cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem) !=
+        cudaSuccess)
+        return set_error(GBX_ECUDA, "gbx_attn_fused: shared-memory attribute refused");
+    const int grid = a.units < di.sm_count ? a.units : di.sm_count;
+    attn_fused_kernel<<<grid, kAttThreads, kAttSmem, reinterpret_cast<cudaStream_t>(stream)>>>(mqh, mql, mkh, mkl, mvh,
+                                                                                              mvl, a);
+    return check_launch("gbx_attn_fused");
+}

@@ -44,6 +44,7 @@
 #include "gbx_common.cuh"
 #include "gelu.cuh"
 #include "tcgen05.cuh"
+#include "tensormap.cuh"
 #include "tf32.cuh"
 
 namespace gbx {
@@ -760,25 +761,6 @@ __global__ void __launch_bounds__(256) split_tf32_scalar_kernel(const float* x, 
 }
 
 // ------------------------------------------------------------------ host
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_tiled()
-{
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
 // Row-major [rows, K] fp32, boxes of box_rows x BK with the BK-wide swizzle.
 static int make_map(CUtensorMap* m, const float* base, int64_t rows, int K, int box_rows, int BK)
 {

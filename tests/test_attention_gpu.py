@@ -198,6 +198,66 @@ def test_attn_softmax_pair_is_split_of_softmax(gbx, cuda, S, scale):
         gbx.attn_softmax_rows_pair(scores, hi, hi, rows=rows, L=S, S=S, scale=scale)
 
 
+def run_fused(gbx, torch, B, S, H, causal, pair_out):
+    hd = 64
+    d = H * hd
+    qkv = _qkv(torch, B, S, H, hd, 11 * S + B + H)
+    hi, lo = _split(gbx, torch, qkv)
+    vt_hi = torch.empty(B * H * hd * S, dtype=torch.float32, device="cuda")
+    vt_lo = torch.empty_like(vt_hi)
+    gbx.transpose_heads(hi[:, 2 * d:], vt_hi, ld=3 * d, B=B, S=S, H=H, hd=hd)
+    gbx.transpose_heads(lo[:, 2 * d:], vt_lo, ld=3 * d, B=B, S=S, H=H, hd=hd)
+    full, out = _guarded(torch, B * S * d)
+    full_lo, out_lo = _guarded(torch, B * S * d)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 8.0
+    gbx.attn_fused(hi, lo, hi[:, d:], lo[:, d:], vt_hi, vt_lo, out, ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=hd,
+                   scale=scale, out_lo=out_lo if pair_out else None, causal=causal, err_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    x = qkv.cpu().numpy()
+    q, k, v = (_heads(x[:, c * d:(c + 1) * d], B, S, H, hd) for c in range(3))
+    sc = (q @ k.transpose(0, 1, 3, 2)) / scale
+    mag = (np.abs(q) @ np.abs(k).transpose(0, 1, 3, 2)) / scale
+    if causal:
+        mask = np.triu(np.ones((S, S), bool), 1)[None, None]
+        sc = np.where(mask, -np.inf, sc)
+        mag = np.where(mask, 0.0, mag)
+    w = np.exp(sc - sc.max(axis=-1, keepdims=True))
+    w /= w.sum(axis=-1, keepdims=True)
+    exact = (w @ v).transpose(0, 2, 1, 3).reshape(B * S, d)
+    wv = (w @ np.abs(v)).transpose(0, 2, 1, 3).reshape(B * S, d)
+    # the scores' product bound moves each weight by at most 2 max|ds| of itself;
+    # 2^-17 covers the exponentials, the online rescales and the P.V products
+    ds = (48 * 2.0 ** -23 + 2.0 ** -24 + 2.0 ** -20) * mag + 4 * np.finfo(np.float32).eps * np.abs(np.where(np.isinf(sc), 0, sc))
+    dmax = ds.max(axis=-1).transpose(0, 2, 1).reshape(B * S, H)
+    tol = (2 * np.repeat(dmax, hd, axis=1) + 2.0 ** -17) * wv + 1e-6
+    got = out.cpu().numpy().astype(np.float64)
+    if pair_out:
+        got = got + out_lo.cpu().numpy()
+        _check_guards(full_lo)
+    _assert_within(got.reshape(B * S, d), exact, tol, f"fused attention B{B} S{S} H{H} causal={causal} pair={pair_out}")
+    _check_guards(full)
+
+
+# S 1024: 8 query tiles and 16 steps of keys; S 200, 36, 132: ragged tiles and steps
+@pytest.mark.parametrize("B,S,H", [(2, 64, 3), (1, 1024, 2), (2, 200, 2), (3, 36, 2), (1, 132, 1), (4, 256, 4)])
+@pytest.mark.parametrize("causal,pair_out", [(True, True), (True, False), (False, False)])
+def test_attn_fused(gbx, cuda, B, S, H, causal, pair_out):
+    import torch
+    run_fused(gbx, torch, B, S, H, causal, pair_out)
+
+
+def test_attn_fused_rejects_other_shapes(gbx, cuda):
+    import torch
+    x = torch.zeros(1 << 16, dtype=torch.float32, device="cuda")
+    for kw in (dict(hd=32), dict(S=6), dict(ld=3 * 64 + 2), dict(B=0)):
+        args = dict(ld=3 * 64, ld_out=64, B=1, S=8, H=1, hd=64, scale=8.0)
+        args.update(kw)
+        with pytest.raises(gbx.GbxError):
+            gbx.attn_fused(x, x, x, x, x, x, x[1024:], **args)
+
+
 def test_attn_products_reject_bad_arguments(gbx, cuda):
     import torch
     x = torch.zeros(4096, dtype=torch.float32, device="cuda")

@@ -9,7 +9,11 @@
 //   for each layer l:
 //     gbx_layernorm_pair                   ln = LN1(h), as a tf32 pair     (:827-828)
 //     gbx_linear                           qkv = ln . Wqkv^T + b_qkv, as a tf32 pair (:830-832)
-//     per group of sequences, every head in one launch each:
+//     head width 64 (every GPT-2 size): gbx_transpose_heads (V hi, lo),
+//       gbx_attn_fused                     attn = softmax(mask(Q K^T / sqrt(hd))) V, every
+//                                          head of every sequence in one launch, no [S, S]
+//                                          matrix in memory (:834-846)
+//     other widths, per group of sequences, every head in one launch each:
 //       gbx_attn_scores                    raw[b][h] = Q_bh . K_bh^T, causal tiles only
 //                                                                          (:834-837, without
 //                                                                          the scale and mask)
@@ -40,6 +44,7 @@
 // at a time (sequences are taken in groups that fit).
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <random>
 
@@ -102,7 +107,8 @@ struct TransformerModel::Impl {
     // the hi half of a tf32 pair, *_lo the low half)
     DevBuf h, ln, ln_lo, qkv, qkv_lo, scores, probs_lo, vt, vt_lo, attn, attn_lo, up, up_lo, last_h, last_y, logits;
     DevBuf splitk_ws;      // partial sums of the K-split contractions
-    int score_group = 1;   // sequences per attention launch
+    int score_group = 1;   // sequences per attention launch (unfused path)
+    bool fused = false;    // attention in one gbx_attn_fused launch (head width 64)
     int sm_count = 148;
     int32_t* ids = nullptr;
     size_t ids_n = 0;
@@ -266,6 +272,15 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
     int64_t G = kScoreGroupFloats / per_seq;
     G = G < 1 ? 1 : (G > B ? B : G);
     m.score_group = (int)G;
+    // the fused attention needs no score buffers and transposes V of every
+    // sequence at once
+    static const bool unfused_env = [] {
+        const char* e = getenv("GBX_ATTN_UNFUSED");
+        return e && *e && *e != '0';
+    }();
+    m.fused = !unfused_env && headDim_ == 64 && seq % 4 == 0 && d % 4 == 0;
+    const int64_t score_floats = m.fused ? 1 : G * per_seq;
+    const int64_t vt_floats = m.fused ? tokens * d : G * seq * d;
     // the largest split-K workspace of the four contractions
     size_t ws = 1;
     const int64_t shapes[4][2] = {{3 * d, d}, {d, d}, {F, d}, {d, F}};
@@ -275,8 +290,8 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
     }
     const bool ok = m.h.ensure(tokens * d) && m.ln.ensure(tokens * d) && m.ln_lo.ensure(tokens * d) &&
                     m.qkv.ensure(tokens * 3 * d) && m.qkv_lo.ensure(tokens * 3 * d) &&
-                    m.scores.ensure((size_t)(G * per_seq)) && m.probs_lo.ensure((size_t)(G * per_seq)) &&
-                    m.vt.ensure((size_t)(G * seq * d)) && m.vt_lo.ensure((size_t)(G * seq * d)) &&
+                    m.scores.ensure((size_t)score_floats) && m.probs_lo.ensure((size_t)score_floats) &&
+                    m.vt.ensure((size_t)vt_floats) && m.vt_lo.ensure((size_t)vt_floats) &&
                     m.attn.ensure(tokens * d) && m.attn_lo.ensure(tokens * d) && m.up.ensure(tokens * F) &&
                     m.up_lo.ensure(tokens * F) && m.splitk_ws.ensure(ws) && m.last_h.ensure(B * d) &&
                     m.last_y.ensure(B * d) &&
@@ -404,7 +419,15 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
         const Impl::LayerW& W = m.wpairs[l];
         check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
         linear(m.ln.p, m.ln_lo.p, W.qkv, L.qkv_b, nullptr, m.qkv.p, m.qkv_lo.p, N, 3 * d, d, GBX_ACT_NONE);
-        for (int b0 = 0; b0 < batch; b0 += m.score_group) {
+        if (m.fused) {
+            // attn = softmax(mask(Q K^T / sqrt(hd))) V for every head of every
+            // sequence in one launch, as a tf32 pair
+            check(gbx_transpose_heads(m.qkv.p + 2 * d, 3 * d, m.vt.p, batch, S, H, hd, gs));
+            check(gbx_transpose_heads(m.qkv_lo.p + 2 * d, 3 * d, m.vt_lo.p, batch, S, H, hd, gs));
+            check(gbx_attn_fused(m.qkv.p, m.qkv_lo.p, m.qkv.p + d, m.qkv_lo.p + d, 3 * d, m.vt.p, m.vt_lo.p, m.attn.p,
+                                 m.attn_lo.p, d, batch, S, H, hd, scale, 1, m.err, gs));
+        }
+        for (int b0 = 0; !m.fused && b0 < batch; b0 += m.score_group) {
             const int g = batch - b0 < m.score_group ? batch - b0 : m.score_group;
             const float* qh = m.qkv.p + (int64_t)b0 * S * 3 * d;
             const float* ql = m.qkv_lo.p + (int64_t)b0 * S * 3 * d;

@@ -1,11 +1,13 @@
 """End-to-end parity of the drop-in TransformerModel (libgbx_model.so: the
-C++ forward over the sm_100a kernels, with fp32 cuBLAS contractions) against
+C++ forward over the sm_100a kernels, every contraction on the tcgen05
+tensor cores with fp32-grade tf32 pairs) against
 the reference's own TransformerModel::forward (its transformer.cu, compiled
 unmodified, run on the same GPU) on random-init GPT-2 GGUF files.
 
 Tolerance.  Both forwards are fp32 throughout; they differ in the order of
-every sum (the reference's GEMVs and 256-wide tree reductions against cuBLAS
-and shuffle reductions), and those rounding differences pass through every
+every sum (the reference's GEMVs and 256-wide tree reductions against the
+tensor cores' sums and shuffle reductions; for head width 64 the online
+softmax of the fused attention), and those rounding differences pass through every
 layer.  The logits must agree within 1e-5 absolute + 1e-3 relative, which is
 two orders of magnitude above the observed differences and far below the
 logits' spread (they pick the same top token)."""
@@ -154,3 +156,37 @@ def test_forward_gpt2_small_shapes_match_reference(gm, orc, cuda, tmp_path):
     err = np.abs(got.astype(np.float64) - want)
     assert np.all(err <= 1e-5 + 1e-3 * np.abs(want)), f"max abs err {err.max():.3g}"
     assert int(np.argmax(got)) == int(np.argmax(want))
+
+
+_UNFUSED_FORWARD = r"""
+import importlib, sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+gm = importlib.import_module("glassboxai-transformer_b200.model")
+ids = np.load(sys.argv[3])
+np.save(sys.argv[4], gm.Model(sys.argv[2]).forward(ids, batch=int(sys.argv[5])))
+"""
+
+
+def test_fused_attention_forward_matches_unfused(gm, cuda, tmp_path):
+    """The forward with the fused attention (head width 64) against the same
+    forward on the unfused per-head products (GBX_ATTN_UNFUSED=1, another
+    process): they differ only in the attention's rounding."""
+    import os
+    import subprocess
+    import sys
+    path = str(tmp_path / "small.gguf")
+    write_tiny_gpt2(path, GGML_F16, d=768, heads=12, ff=3072, layers=2, ctx=256, seed=41)
+    ids = np.random.default_rng(8).integers(0, 50257, 3 * 200).astype(np.int32)
+    np.save(tmp_path / "ids.npy", ids)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, GBX_ATTN_UNFUSED="1")
+    out = subprocess.run([sys.executable, "-c", _UNFUSED_FORWARD, root, path, str(tmp_path / "ids.npy"),
+                          str(tmp_path / "unfused.npy"), "3"], env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stdout + out.stderr
+    want = np.load(tmp_path / "unfused.npy")
+    got = gm.Model(path).forward(ids, batch=3)
+    assert got.shape == want.shape
+    err = np.abs(got.astype(np.float64) - want)
+    assert np.all(err <= 1e-5 + 1e-3 * np.abs(want)), f"max abs err {err.max():.3g}"
+    assert np.array_equal(np.argmax(got.reshape(3, -1), axis=1), np.argmax(want.reshape(3, -1), axis=1))

@@ -17,16 +17,18 @@
 // in rounding (a few fp32 ulps of each weight).
 //
 // One CTA works on one (head, 128-query tile) unit at a time, persistent over
-// the units (longest first), 320 threads:
+// the units (longest first), 352 threads:
 //   warp 0      TMA producer: the unit's Q tile (128 x 64, hi and lo), then per
 //               step of 64 keys the K tile and the V^T tile into a two-stage
 //               ring (128-byte swizzled rows, 32 floats per K block)
-//   warp 1      owns 512 TMEM columns; one thread issues the MMAs:
+//   warp 1      owns 512 TMEM columns; one thread issues the score MMAs
 //                 S[j] = Q K_j^T                      (kind::tf32, M 128, N 64)
+//   warp 2      one thread issues the value MMAs
 //                 O[j] = P_j V_j                      (A = P_j from TMEM)
-//               S[j+1] is issued before O[j], so the tensor core computes the
-//               next scores while the softmax warps work on these
-//   warps 2-9   softmax: warps w and w + 4 own query rows 32 (w % 4) .. +31,
+//               (at N 64, 24 MMAs per product and step, one thread issuing
+//               both bounded the kernel); S[j+1] runs while the softmax
+//               warps work on S[j]
+//   warps 3-10  softmax: warps w and w + 4 own query rows 32 (w % 4) .. +31,
 //               32 of the 64 columns each; a thread reads its S[j] columns
 //               from TMEM, writes its part of P_j as a tf32 pair back into
 //               TMEM (hi over S[j]), then adds its 32 columns of O[j-1] into
@@ -50,7 +52,7 @@ constexpr int kAttQ = 128;        // query rows per unit (TMEM lanes)
 constexpr int kAttKT = 64;        // keys per step
 constexpr int kAttHD = 64;        // head width
 constexpr int kAttSoftWarps = 8;
-constexpr int kAttThreads = 64 + 32 * kAttSoftWarps;
+constexpr int kAttThreads = 96 + 32 * kAttSoftWarps;
 constexpr uint64_t kAttWaitNs = 1000000000ull;
 // shared memory: Q (2 planes x 2 K blocks x 128 rows x 128 B), then two ring
 // stages of K (2 x 2 x 64 rows x 128 B) and V^T (the same)
@@ -60,8 +62,9 @@ constexpr uint32_t kAttQBytes = 4 * kAttQBlock;            // 64 KB
 constexpr uint32_t kAttKVBytes = 4 * kAttKVBlock;          // 32 KB
 constexpr uint32_t kAttStages = 2;
 constexpr uint32_t kAttData = kAttQBytes + kAttStages * 2 * kAttKVBytes;   // 192 KB
-// barriers: qfull qempty kfull[2] kempty[2] vfull[2] vempty[2] sfull[2] pfull[2] pvdone[2] ofull[2] oempty[2] drain
-constexpr int kAttBars = 21;
+// barriers: qfull qempty kfull[2] kempty[2] vfull[2] vempty[2] sfull[2] pfull[2] pvdone[2] ofull[2] oempty[2]
+// drain drain2
+constexpr int kAttBars = 22;
 // after the barriers and the TMEM slot: the softmax halves' exchange slots
 constexpr size_t kAttXBytes = 2 * 4 * 2 * 32 * sizeof(float);
 constexpr size_t kAttSmem = kAttData + 1024 + 8 * kAttBars + 16 + kAttXBytes;
@@ -126,7 +129,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
     auto pvdone = [&](int i) { return b0 + 112 + 8 * i; };
     auto ofull = [&](int i) { return b0 + 128 + 8 * i; };
     auto oempty = [&](int i) { return b0 + 144 + 8 * i; };
-    const uint32_t drain = b0 + 160;
+    const uint32_t drain = b0 + 160, drain2 = b0 + 168;
     const uint32_t smem0 = tc::smem_u32(smem);
     const uint32_t qbase = smem0;
     auto kbase = [&](int s) { return smem0 + kAttQBytes + s * 2 * kAttKVBytes; };
@@ -149,6 +152,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
             tc::mbar_init(oempty(s), kAttSoftWarps);
         }
         tc::mbar_init(drain, 1);
+        tc::mbar_init(drain2, 1);
         *abort = 0;
         tc::fence_mbar_init();
         tc::tma_prefetch(&map_qh);
@@ -222,41 +226,15 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---------------------------------------------------- MMA issuer
-            const uint32_t idesc = tc::idesc_tf32(kAttQ, kAttKT);   // both products: M 128, N 64
-            int kst = 0, vst = 0;
-            uint32_t kph = 0, vph = 0, qph = 0;
+            // ---------------------------------------------- score MMA issuer
+            const uint32_t idesc = tc::idesc_tf32(kAttQ, kAttKT);   // M 128, N 64
+            // shared-memory descriptors of the K blocks' first K step; a K
+            // step of 8 floats advances the address field by 32 bytes
+            const uint64_t dq = tc::smem_desc(qbase, 128);
+            int kst = 0;
+            uint32_t kph = 0, qph = 0;
             uint32_t g = 0;   // global step (buffer = g & 1, its use count = g >> 1)
             bool ok = true;
-            // O[gg] = P_gg V_gg, the V tile in ring stage vst
-            auto pv = [&](uint32_t gg) -> bool {
-                const uint32_t i = gg & 1;
-                if (!tc::mbar_wait(pfull(i), (gg >> 1) & 1, abort, kAttWaitNs)) return false;
-                if (!tc::mbar_wait(vfull(vst), vph, abort, kAttWaitNs)) return false;
-                if (gg >= 2 && !tc::mbar_wait(oempty(i), ((gg - 2) >> 1) & 1, abort, kAttWaitNs)) return false;
-                tc::fence_after_sync();
-                const uint32_t d = tmem + kTmO + 64 * i;
-                const uint32_t phi = tmem + kTmS + 64 * i, plo = tmem + kTmPlo + 64 * i;
-#pragma unroll
-                for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        const uint32_t k8 = 32 * kb + 8 * ks;   // key column of this K step
-                        const uint64_t vh = tc::smem_desc(vbase(vst) + kb * kAttKVBlock + 32 * ks, 128);
-                        const uint64_t vl = tc::smem_desc(vbase(vst) + (2 + kb) * kAttKVBlock + 32 * ks, 128);
-                        tc::mma_tf32_ts(d, phi + k8, vh, idesc, (kb | ks) != 0);
-                        tc::mma_tf32_ts(d, phi + k8, vl, idesc, 1);
-                        tc::mma_tf32_ts(d, plo + k8, vh, idesc, 1);
-                    }
-                tc::mma_commit(ofull(i));
-                tc::mma_commit(vempty(vst));
-                tc::mma_commit(pvdone(i));
-                if (++vst == 2) {
-                    vst = 0;
-                    vph ^= 1;
-                }
-                return true;
-            };
             for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
                 const AttnUnit w = attn_unit(u, a);
                 if (!tc::mbar_wait(qfull, qph, abort, kAttWaitNs)) break;
@@ -274,14 +252,15 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                     }
                     tc::fence_after_sync();
                     const uint32_t d = tmem + kTmS + 64 * i;
+                    const uint64_t dk = tc::smem_desc(kbase(kst), 128);
 #pragma unroll
                     for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
                         for (int ks = 0; ks < 4; ++ks) {
-                            const uint64_t qh = tc::smem_desc(qbase + kb * kAttQBlock + 32 * ks, 128);
-                            const uint64_t ql = tc::smem_desc(qbase + (2 + kb) * kAttQBlock + 32 * ks, 128);
-                            const uint64_t kh = tc::smem_desc(kbase(kst) + kb * kAttKVBlock + 32 * ks, 128);
-                            const uint64_t kl = tc::smem_desc(kbase(kst) + (2 + kb) * kAttKVBlock + 32 * ks, 128);
+                            const uint64_t qh = dq + ((kb * kAttQBlock + 32 * ks) >> 4);
+                            const uint64_t ql = dq + (((2 + kb) * kAttQBlock + 32 * ks) >> 4);
+                            const uint64_t kh = dk + ((kb * kAttKVBlock + 32 * ks) >> 4);
+                            const uint64_t kl = dk + (((2 + kb) * kAttKVBlock + 32 * ks) >> 4);
                             tc::mma_tf32(d, qh, kh, idesc, (kb | ks) != 0);
                             tc::mma_tf32(d, qh, kl, idesc, 1);
                             tc::mma_tf32(d, ql, kh, idesc, 1);
@@ -293,27 +272,69 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                         kst = 0;
                         kph ^= 1;
                     }
-                    if (j >= 1 && !pv(g - 1)) {
-                        ok = false;
-                        break;
-                    }
                 }
-                if (ok && !pv(g - 1)) ok = false;
             }
-            // every MMA issued has completed before TMEM is freed
+            // every MMA this thread issued has completed before TMEM is freed
             tc::mma_commit(drain);
             tc::mbar_wait(drain, 0, nullptr, kAttWaitNs);
         }
+    } else if (warp == 2) {
+        if (lane == 0) {
+            // --------------------------------------------- values MMA issuer
+            // O[g] = P_g V_g with P_g read from TMEM.  A second issuing thread:
+            // at N 64 one thread issuing both products bounds the kernel.
+            const uint32_t idesc = tc::idesc_tf32(kAttQ, kAttKT);   // M 128, N 64
+            int vst = 0;
+            uint32_t vph = 0;
+            uint32_t g = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+                const AttnUnit w = attn_unit(u, a);
+                for (int j = 0; j < w.nkt; ++j, ++g) {
+                    const uint32_t i = g & 1;
+                    if (!tc::mbar_wait(pfull(i), (g >> 1) & 1, abort, kAttWaitNs) ||
+                        !tc::mbar_wait(vfull(vst), vph, abort, kAttWaitNs) ||
+                        (g >= 2 && !tc::mbar_wait(oempty(i), ((g - 2) >> 1) & 1, abort, kAttWaitNs))) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t d = tmem + kTmO + 64 * i;
+                    const uint32_t phi = tmem + kTmS + 64 * i, plo = tmem + kTmPlo + 64 * i;
+                    const uint64_t dv = tc::smem_desc(vbase(vst), 128);
+#pragma unroll
+                    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint32_t k8 = 32 * kb + 8 * ks;   // key column of this K step
+                            const uint64_t vh = dv + ((kb * kAttKVBlock + 32 * ks) >> 4);
+                            const uint64_t vl = dv + (((2 + kb) * kAttKVBlock + 32 * ks) >> 4);
+                            tc::mma_tf32_ts(d, phi + k8, vh, idesc, (kb | ks) != 0);
+                            tc::mma_tf32_ts(d, phi + k8, vl, idesc, 1);
+                            tc::mma_tf32_ts(d, plo + k8, vh, idesc, 1);
+                        }
+                    tc::mma_commit(ofull(i));
+                    tc::mma_commit(vempty(vst));
+                    tc::mma_commit(pvdone(i));
+                    if (++vst == 2) {
+                        vst = 0;
+                        vph ^= 1;
+                    }
+                }
+            }
+            tc::mma_commit(drain2);
+            tc::mbar_wait(drain2, 0, nullptr, kAttWaitNs);
+        }
     } else {
         // -------------------------------------------------------- softmax
-        // Warps w and w + 4 share query rows 32 (w % 4) .. +31 (the TMEM lane
+        // Warps w and w + 4 (3 <= w <= 6) share query rows 32 (w % 4) .. +31 (the TMEM lane
         // quarter they may read); `half` picks the 32 of the 64 key (and
         // output) columns this thread owns.  The two halves of a row exchange
         // their step maxima through shared memory (double-buffered by step
         // parity) at a 64-thread named barrier, keep their own partial sums
         // (the same rescales apply to both) and add them at the end.
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int half = (warp - 3) >> 2;
         const int row_in_tile = 32 * quarter + lane;
         const uint32_t lane_addr = (uint32_t)(32 * quarter) << 16;
         const uint32_t col = 32 * half;

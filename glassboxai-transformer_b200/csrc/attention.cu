@@ -340,7 +340,22 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
         const uint32_t col = 32 * half;
         float* const xmax = reinterpret_cast<float*>(tmem_slot + 4);   // [2 parity][4 quarter][2 half][32]
         const int bar_id = 1 + quarter;                             // named barriers 1-4
-        auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
+        // The pair's barrier also decides, for both halves alike, whether to
+        // stop: it returns the OR of the two halves' `stop` (a half never
+        // leaves its loop alone, which would leave the other waiting at the
+        // barrier for ever).
+        auto pair_sync = [&](bool stop) -> bool {
+            uint32_t any;
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\t"
+                "setp.ne.u32 q, %2, 0;\n\t"
+                "bar.red.or.pred p, %1, 64, q;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(any)
+                : "r"(bar_id), "r"((uint32_t)stop)
+                : "memory");
+            return any != 0;
+        };
         uint32_t g = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
@@ -369,15 +384,19 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
             };
             for (int j = 0; j < w.nkt; ++j, ++g) {
                 const uint32_t i = g & 1;
-                const bool ready = tc::mbar_wait(sfull(i), (g >> 1) & 1, abort, kAttWaitNs);
-                if (!__all_sync(0xffffffffu, ready)) {
-                    ok = false;
-                    break;
-                }
-                tc::fence_after_sync();
+                // a failed wait here or in the previous step's take_o stops
+                // both halves at this step's barrier
+                const bool ready =
+                    ok && __all_sync(0xffffffffu, tc::mbar_wait(sfull(i), (g >> 1) & 1, abort, kAttWaitNs));
                 float s[32];
-                tc::tmem_ld32(tmem + lane_addr + kTmS + 64 * i + col, s);
-                tc::tmem_ld_wait();
+                if (ready) {
+                    tc::fence_after_sync();
+                    tc::tmem_ld32(tmem + lane_addr + kTmS + 64 * i + col, s);
+                    tc::tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) s[c] = 0.0f;
+                }
                 // keys k0 .. k0 + nvis - 1 of this thread's 32 are visible to its row
                 const int k0 = j * kAttKT + (int)col;
                 const int nvis = max(0, min(32, lim - k0));
@@ -401,7 +420,10 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 // the row's step maximum: both halves
                 float* const xm = xmax + (((i * 4 + quarter) * 2) * 32);
                 xm[half * 32 + lane] = mt;
-                pair_sync();
+                if (pair_sync(!ready)) {
+                    ok = false;
+                    break;
+                }
                 mt = fmaxf(mt, xm[(1 - half) * 32 + lane]);
                 const float m_new = fmaxf(m, mt);
                 const float alpha = m_new == -INFINITY ? 1.0f : expf(m - m_new);
@@ -436,23 +458,21 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 tc::fence_before_sync();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(pfull(i));
-                if (j >= 1 && !take_o(g - 1, alpha_pend)) {
-                    ok = false;
-                    break;
-                }
+                if (j >= 1 && !take_o(g - 1, alpha_pend)) ok = false;   // both stop at the next barrier
                 alpha_pend = alpha;
             }
-            if (!ok || !take_o(g - 1, alpha_pend)) {
-                ok = false;
-                break;
-            }
+            // the last step's output (skipped once a barrier has decided to stop)
+            if (ok && !take_o(g - 1, alpha_pend)) ok = false;
             // the row's sum: both halves (the slot of the last step's parity
             // is free again: both halves have passed that step's barrier)
             float* const xl = xmax + ((((g & 1) * 4 + quarter) * 2) * 32);
             xl[half * 32 + lane] = l;
-            pair_sync();
+            if (pair_sync(!ok)) {
+                ok = false;
+                break;
+            }
             l += xl[(1 - half) * 32 + lane];
-            pair_sync();   // the slot is read before either half writes it again
+            pair_sync(false);   // the slot is read before either half writes it again
             if (p < a.S) {
                 const float rl = 1.0f / l;
                 const int64_t off = ((int64_t)w.b * a.S + p) * a.ld_out + (int64_t)w.h * kAttHD + col;

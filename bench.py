@@ -736,9 +736,7 @@ def run_attn(args, shape, G, g, f32):
         G.attn_values(dots, p_lo, vt, vt_lo, out, ld_out=d, B=B, S=S, H=H, hd=hd, out_lo=out_lo, err_flag=err)
 
     def fused():
-        G.transpose_heads(qh[:, 2 * d:], vt, ld=3 * d, B=B, S=S, H=H, hd=hd)
-        G.transpose_heads(ql[:, 2 * d:], vt_lo, ld=3 * d, B=B, S=S, H=H, hd=hd)
-        G.attn_fused(qh, ql, qh[:, d:], ql[:, d:], vt, vt_lo, out, ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=hd,
+        G.attn_fused(qh, ql, qh[:, d:], ql[:, d:], qh[:, 2 * d:], ql[:, 2 * d:], out, ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=hd,
                      scale=scale, out_lo=out_lo, err_flag=err)
 
     def block():
@@ -792,8 +790,7 @@ def run_attn(args, shape, G, g, f32):
                       "head_dim": hd, "causal": True, "median_us": us,
                       "dense_equiv_tflops": flop / (us * 1e-6) / 1e12,
                       "cublas_fp32_us": rus, "speedup_vs_cublas_fp32": rus / us,
-                      "cublas_path": "torch.bmm fp32 (TF32 off), dense; block, fused: + scale, mask, torch.softmax",
-                      "fused_includes": "the two V transposes" if args.kernel == "attn_fused" else None}),
+                      "cublas_path": "torch.bmm fp32 (TF32 off), dense; block, fused: + scale, mask, torch.softmax"}),
           flush=True)
 
 

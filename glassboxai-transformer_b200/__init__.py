@@ -232,8 +232,8 @@ def linear_splitk_noalloc(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, ksplit, bias=No
                                            _p(y_lo), M, N, K, act, ksplit, _p(err_flag), _stream(stream)))
 
 
-def attn_fused(q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo, out, *, ld, ld_out, B, S, H, hd, scale, out_lo=None, causal=True,
+def attn_fused(q_hi, q_lo, k_hi, k_lo, v_hi, v_lo, out, *, ld, ld_out, B, S, H, hd, scale, out_lo=None, causal=True,
                err_flag=None, stream=None):
     """Self-attention of every head in one fused launch (tf32 pairs in; see gbx.h)."""
-    _check(lib().gbx_attn_fused(_p(q_hi), _p(q_lo), _p(k_hi), _p(k_lo), ld, _p(vt_hi), _p(vt_lo), _p(out), _p(out_lo),
+    _check(lib().gbx_attn_fused(_p(q_hi), _p(q_lo), _p(k_hi), _p(k_lo), ld, _p(v_hi), _p(v_lo), _p(out), _p(out_lo),
                                 ld_out, B, S, H, hd, scale, 1 if causal else 0, _p(err_flag), _stream(stream)))

@@ -19,8 +19,12 @@
 // One CTA works on one (head, 128-query tile) unit at a time, persistent over
 // the units (longest first), 352 threads:
 //   warp 0      TMA producer: the unit's Q tile (128 x 64, hi and lo), then per
-//               step of 64 keys the K tile and the V^T tile into a two-stage
-//               ring (128-byte swizzled rows, 32 floats per K block)
+//               step of 64 keys the K tile and the V tile into a two-stage
+//               ring (128-byte swizzled rows, 32 floats per block), both
+//               straight from the QKV rows: V is the MMA's B operand in
+//               MN-major form (head columns contiguous, 32-byte swizzle
+//               atoms, the one layout of an MN-major tf32 operand), so no
+//               transpose
 //   warp 1      owns 512 TMEM columns; one thread issues the score MMAs
 //                 S[j] = Q K_j^T                      (kind::tf32, M 128, N 64)
 //   warp 2      one thread issues the value MMAs
@@ -55,9 +59,9 @@ constexpr int kAttSoftWarps = 8;
 constexpr int kAttThreads = 96 + 32 * kAttSoftWarps;
 constexpr uint64_t kAttWaitNs = 1000000000ull;
 // shared memory: Q (2 planes x 2 K blocks x 128 rows x 128 B), then two ring
-// stages of K (2 x 2 x 64 rows x 128 B) and V^T (the same)
+// stages of K (2 x 2 x 64 rows x 128 B) and V (the same)
 constexpr uint32_t kAttQBlock = 128 * 128;                 // one plane, one K block of Q
-constexpr uint32_t kAttKVBlock = 64 * 128;                 // one plane, one K block of K or V^T
+constexpr uint32_t kAttKVBlock = 64 * 128;                 // one plane, 32 columns of K or V
 constexpr uint32_t kAttQBytes = 4 * kAttQBlock;            // 64 KB
 constexpr uint32_t kAttKVBytes = 4 * kAttKVBlock;          // 32 KB
 constexpr uint32_t kAttStages = 2;
@@ -207,7 +211,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                     for (int p = 0; p < 2; ++p)
                         for (int kb = 0; kb < 2; ++kb)
                             tc::tma_load_4d(vbase(st) + (2 * p + kb) * kAttKVBlock, p ? &map_vl : &map_vh, vfull(st),
-                                            j * kAttKT + 32 * kb, 0, w.h, w.b);
+                                            32 * kb, w.h, j * kAttKT, w.b);
                     issued |= 1u << st;
                     lastpar = (lastpar & ~(1u << st)) | (ph << st);
                     if (++st == 2) {
@@ -283,7 +287,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
             // --------------------------------------------- values MMA issuer
             // O[g] = P_g V_g with P_g read from TMEM.  A second issuing thread:
             // at N 64 one thread issuing both products bounds the kernel.
-            const uint32_t idesc = tc::idesc_tf32(kAttQ, kAttKT);   // M 128, N 64
+            const uint32_t idesc = tc::idesc_tf32_bmn(kAttQ, kAttHD);   // M 128, N 64, B MN-major
             int vst = 0;
             uint32_t vph = 0;
             uint32_t g = 0;
@@ -301,18 +305,20 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                     tc::fence_after_sync();
                     const uint32_t d = tmem + kTmO + 64 * i;
                     const uint32_t phi = tmem + kTmS + 64 * i, plo = tmem + kTmPlo + 64 * i;
-                    const uint64_t dv = tc::smem_desc(vbase(vst), 128);
+                    // V is MN-major: key rows of 128 bytes (32 head columns) in
+                    // 4-row (512 B) swizzle atoms, a K step of 8 keys is 1 KB,
+                    // head columns 32..63 sit one box (8 KB) on, the low plane
+                    // two boxes on
+                    const uint64_t dv = tc::smem_desc_mn128_b32(vbase(vst), kAttKVBlock, 512);
 #pragma unroll
-                    for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-                        for (int ks = 0; ks < 4; ++ks) {
-                            const uint32_t k8 = 32 * kb + 8 * ks;   // key column of this K step
-                            const uint64_t vh = dv + ((kb * kAttKVBlock + 32 * ks) >> 4);
-                            const uint64_t vl = dv + (((2 + kb) * kAttKVBlock + 32 * ks) >> 4);
-                            tc::mma_tf32_ts(d, phi + k8, vh, idesc, (kb | ks) != 0);
-                            tc::mma_tf32_ts(d, phi + k8, vl, idesc, 1);
-                            tc::mma_tf32_ts(d, plo + k8, vh, idesc, 1);
-                        }
+                    for (int t = 0; t < kAttKT / 8; ++t) {
+                        const uint32_t k8 = 8 * t;   // key column of this K step
+                        const uint64_t vh = dv + ((1024u * t) >> 4);
+                        const uint64_t vl = dv + ((2 * kAttKVBlock + 1024u * t) >> 4);
+                        tc::mma_tf32_ts(d, phi + k8, vh, idesc, t != 0);
+                        tc::mma_tf32_ts(d, phi + k8, vl, idesc, 1);
+                        tc::mma_tf32_ts(d, plo + k8, vh, idesc, 1);
+                    }
                     tc::mma_commit(ofull(i));
                     tc::mma_commit(vempty(vst));
                     tc::mma_commit(pvdone(i));
@@ -504,9 +510,10 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
 
 // One plane of a heads-mode operand as a 4-D map: dims (inner k, then d1, d2,
 // d3) with element strides s1 < s2 < s3, boxes of 32 x box1 x box2 x 1 and
-// the 128-byte swizzle.
+// the 128-byte swizzle (16-byte atoms for the K-major Q and K; 32-byte atoms
+// for V, the MMA's MN-major operand).
 static int attn_map(CUtensorMap* m, const float* base, const cuuint64_t (&dims)[4], const cuuint64_t (&strides)[3],
-                    cuuint32_t box1, cuuint32_t box2)
+                    cuuint32_t box1, cuuint32_t box2, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B)
 {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return set_error(GBX_ECUDA, "gbx_attn_fused: cuTensorMapEncodeTiled unavailable from the driver");
@@ -515,7 +522,7 @@ static int attn_map(CUtensorMap* m, const float* base, const cuuint64_t (&dims)[
     const cuuint32_t box[4] = {32, box1, box2, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, sb, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(GBX_EINVAL, "gbx_attn_fused: tensor map rejected (CUresult %d)", (int)r);
     return GBX_OK;
@@ -526,7 +533,7 @@ static int attn_map(CUtensorMap* m, const float* base, const cuuint64_t (&dims)[
 using namespace gbx;
 
 extern "C" int gbx_attn_fused(const float* q_hi, const float* q_lo, const float* k_hi, const float* k_lo, int64_t ld,
-                              const float* vt_hi, const float* vt_lo, float* out, float* out_lo, int64_t ld_out, int B,
+                              const float* v_hi, const float* v_lo, float* out, float* out_lo, int64_t ld_out, int B,
                               int S, int H, int hd, float scale, int causal, int* err_flag, gbx_stream_t stream)
 {
     if (B <= 0 || S <= 0 || H <= 0 || hd <= 0)
@@ -534,16 +541,16 @@ extern "C" int gbx_attn_fused(const float* q_hi, const float* q_lo, const float*
     if (hd != kAttHD) return set_error(GBX_EINVAL, "gbx_attn_fused: head width %d (64 only)", hd);
     if (!(scale >= 1.17549435e-38f) || scale == INFINITY)
         return set_error(GBX_EINVAL, "gbx_attn_fused: scale=%g must be a normal positive float", (double)scale);
-    if (!q_hi || !q_lo || !k_hi || !k_lo || !vt_hi || !vt_lo || !out)
+    if (!q_hi || !q_lo || !k_hi || !k_lo || !v_hi || !v_lo || !out)
         return set_error(GBX_EINVAL, "gbx_attn_fused: null pointer");
     if (ld < (int64_t)H * hd || ld_out < (int64_t)H * hd)
         return set_error(GBX_EINVAL, "gbx_attn_fused: ld=%lld ld_out=%lld < H*hd", (long long)ld, (long long)ld_out);
     if (out_lo == out) return set_error(GBX_EINVAL, "gbx_attn_fused: out_lo aliases out");
     // the tensor maps: 16-byte bases and strides; the vector output stores
-    const bool al = aligned16(q_hi) && aligned16(q_lo) && aligned16(k_hi) && aligned16(k_lo) && aligned16(vt_hi) &&
-                    aligned16(vt_lo) && aligned16(out) && (!out_lo || aligned16(out_lo));
-    if (!al || ld % 4 || ld_out % 4 || S % 4)
-        return set_error(GBX_EINVAL, "gbx_attn_fused: operands need 16-byte alignment and ld, ld_out, S multiples of 4");
+    const bool al = aligned16(q_hi) && aligned16(q_lo) && aligned16(k_hi) && aligned16(k_lo) && aligned16(v_hi) &&
+                    aligned16(v_lo) && aligned16(out) && (!out_lo || aligned16(out_lo));
+    if (!al || ld % 4 || ld_out % 4)
+        return set_error(GBX_EINVAL, "gbx_attn_fused: operands need 16-byte alignment and ld, ld_out multiples of 4");
     const int nqt = (S + kAttQ - 1) / kAttQ;
     if ((int64_t)B * H * nqt > 0x7fffffffLL || (int64_t)B * S > 0x7fffffffLL)
         return set_error(GBX_ERANGE, "gbx_attn_fused: B=%d H=%d S=%d too large", B, H, S);
@@ -552,17 +559,15 @@ extern "C" int gbx_attn_fused(const float* q_hi, const float* q_lo, const float*
     if ((size_t)di.max_smem_optin < kAttSmem)
         return set_error(GBX_ERANGE, "gbx_attn_fused: needs %zu bytes of shared memory per CTA", kAttSmem);
 
-    // Q and K: element (b, s, h, i) at b*S*ld + s*ld + h*64 + i, dims (i, h, s, b);
-    // V^T: element (b, h, i, s) at ((b*H + h)*64 + i)*S + s, dims (s, i, h, b)
+    // Q, K and V: element (b, s, h, i) at b*S*ld + s*ld + h*64 + i, dims (i, h, s, b)
     CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
     const cuuint64_t dqk[4] = {(cuuint64_t)hd, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
     const cuuint64_t sqk[3] = {(cuuint64_t)hd, (cuuint64_t)ld, (cuuint64_t)S * ld};
-    const cuuint64_t dv[4] = {(cuuint64_t)S, (cuuint64_t)hd, (cuuint64_t)H, (cuuint64_t)B};
-    const cuuint64_t sv[3] = {(cuuint64_t)S, (cuuint64_t)hd * S, (cuuint64_t)H * hd * S};
     int rc;
     if ((rc = attn_map(&mqh, q_hi, dqk, sqk, 1, kAttQ)) || (rc = attn_map(&mql, q_lo, dqk, sqk, 1, kAttQ)) ||
         (rc = attn_map(&mkh, k_hi, dqk, sqk, 1, kAttKT)) || (rc = attn_map(&mkl, k_lo, dqk, sqk, 1, kAttKT)) ||
-        (rc = attn_map(&mvh, vt_hi, dv, sv, kAttHD, 1)) || (rc = attn_map(&mvl, vt_lo, dv, sv, kAttHD, 1)))
+        (rc = attn_map(&mvh, v_hi, dqk, sqk, 1, kAttKT, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) ||
+        (rc = attn_map(&mvl, v_lo, dqk, sqk, 1, kAttKT, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)))
         return rc;
     AttnArgs a;
     a.out = out;

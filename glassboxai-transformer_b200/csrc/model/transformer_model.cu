@@ -9,9 +9,10 @@
 //   for each layer l:
 //     gbx_layernorm_pair                   ln = LN1(h), as a tf32 pair     (:827-828)
 //     gbx_linear                           qkv = ln . Wqkv^T + b_qkv, as a tf32 pair (:830-832)
-//     head width 64 (every GPT-2 size): gbx_transpose_heads (V hi, lo),
+//     head width 64 (every GPT-2 size):
 //       gbx_attn_fused                     attn = softmax(mask(Q K^T / sqrt(hd))) V, every
-//                                          head of every sequence in one launch, no [S, S]
+//                                          head of every sequence in one launch, Q, K and V
+//                                          read from the QKV rows as they lie, no [S, S]
 //                                          matrix in memory (:834-846)
 //     other widths, per group of sequences, every head in one launch each:
 //       gbx_attn_scores                    raw[b][h] = Q_bh . K_bh^T, causal tiles only
@@ -278,9 +279,9 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
         const char* e = getenv("GBX_ATTN_UNFUSED");
         return e && *e && *e != '0';
     }();
-    m.fused = !unfused_env && headDim_ == 64 && seq % 4 == 0 && d % 4 == 0;
+    m.fused = !unfused_env && headDim_ == 64 && d % 4 == 0;
     const int64_t score_floats = m.fused ? 1 : G * per_seq;
-    const int64_t vt_floats = m.fused ? tokens * d : G * seq * d;
+    const int64_t vt_floats = m.fused ? 1 : G * seq * d;
     // the largest split-K workspace of the four contractions
     size_t ws = 1;
     const int64_t shapes[4][2] = {{3 * d, d}, {d, d}, {F, d}, {d, F}};
@@ -422,10 +423,8 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
         if (m.fused) {
             // attn = softmax(mask(Q K^T / sqrt(hd))) V for every head of every
             // sequence in one launch, as a tf32 pair
-            check(gbx_transpose_heads(m.qkv.p + 2 * d, 3 * d, m.vt.p, batch, S, H, hd, gs));
-            check(gbx_transpose_heads(m.qkv_lo.p + 2 * d, 3 * d, m.vt_lo.p, batch, S, H, hd, gs));
-            check(gbx_attn_fused(m.qkv.p, m.qkv_lo.p, m.qkv.p + d, m.qkv_lo.p + d, 3 * d, m.vt.p, m.vt_lo.p, m.attn.p,
-                                 m.attn_lo.p, d, batch, S, H, hd, scale, 1, m.err, gs));
+            check(gbx_attn_fused(m.qkv.p, m.qkv_lo.p, m.qkv.p + d, m.qkv_lo.p + d, 3 * d, m.qkv.p + 2 * d,
+                                 m.qkv_lo.p + 2 * d, m.attn.p, m.attn_lo.p, d, batch, S, H, hd, scale, 1, m.err, gs));
         }
         for (int b0 = 0; !m.fused && b0 < batch; b0 += m.score_group) {
             const int g = batch - b0 < m.score_group ? batch - b0 : m.score_group;

@@ -375,5 +375,21 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N)
     return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// The same with B MN-major (bit 16): B's N index contiguous in memory.
+__host__ __device__ constexpr uint32_t idesc_tf32_bmn(int M, int N) { return idesc_tf32(M, N) | (1u << 16); }
+
+// MN-major tf32 operand tile.  A 32-bit MN-major operand takes only the
+// 128-byte swizzle with 32-byte atoms (layout type 1; the tensor map's
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes it): 32 consecutive N elements
+// (128 bytes) per row, a row per K index, 4-row swizzle atoms stacked along
+// K at sbo bytes; the next 32 N elements start lbo bytes on.  (CUTLASS's
+// make_umma_desc<Major::MN> with SWIZZLE_128B_BASE32B: LBO is the stride
+// between 128-byte blocks of N, SBO the stride between 4-row groups of K.)
+__device__ __forceinline__ uint64_t smem_desc_mn128_b32(uint32_t addr, uint32_t lbo, uint32_t sbo)
+{
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)1 << 61);
+}
+
 }  // namespace tc
 }  // namespace gbx

@@ -354,19 +354,20 @@ int gbx_attn_values(const float* p_hi, const float* p_lo, const float* vt_hi, co
  *   out[(b*S + p)*ld_out + h*64 + i] = sum_s w_ps v[b, s, h*64 + i],
  *   w_p = softmax over s of q_p . k_s / scale (s <= p when causal)
  * q, k: tf32 pairs with row stride ld, as gbx_attn_scores takes them (the Q
- * and K column blocks of the QKV output); vt_hi, vt_lo: gbx_transpose_heads
- * of V's two planes.  out_lo NULL: out receives the fp32 result; otherwise
+ * and K column blocks of the QKV output); v_hi, v_lo: V's two planes with the
+ * same row stride (the QKV output's V column block, read as it lies: no
+ * transpose).  out_lo NULL: out receives the fp32 result; otherwise
  * out and out_lo its tf32 pair (the projection's x operand).  The softmax is
  * the online form (running maximum and sum per row, the running output
  * rescaled when the maximum grows), so the weights differ from the
  * reference's single-pass softmax only in rounding; keys past the diagonal
- * weigh exactly 0.  hd must be 64 (every GPT-2 size); S, ld and ld_out
- * multiples of 4; operands 16-byte aligned.  Other shapes return
+ * weigh exactly 0.  hd must be 64 (every GPT-2 size); ld and ld_out
+ * multiples of 4; operands 16-byte aligned; any S >= 1.  Other shapes return
  * GBX_EINVAL: use gbx_attn_scores, gbx_attn_softmax_rows_pair and
  * gbx_attn_values.  err_flag: as gbx_linear (GBX_LINEAR_TIMEOUT).
  */
 int gbx_attn_fused(const float* q_hi, const float* q_lo, const float* k_hi, const float* k_lo, int64_t ld,
-                   const float* vt_hi, const float* vt_lo, float* out, float* out_lo, int64_t ld_out, int B, int S,
+                   const float* v_hi, const float* v_lo, float* out, float* out_lo, int64_t ld_out, int B, int S,
                    int H, int hd, float scale, int causal, int* err_flag, gbx_stream_t stream);
 
 #ifdef __cplusplus

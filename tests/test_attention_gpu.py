@@ -203,15 +203,11 @@ def run_fused(gbx, torch, B, S, H, causal, pair_out):
     d = H * hd
     qkv = _qkv(torch, B, S, H, hd, 11 * S + B + H)
     hi, lo = _split(gbx, torch, qkv)
-    vt_hi = torch.empty(B * H * hd * S, dtype=torch.float32, device="cuda")
-    vt_lo = torch.empty_like(vt_hi)
-    gbx.transpose_heads(hi[:, 2 * d:], vt_hi, ld=3 * d, B=B, S=S, H=H, hd=hd)
-    gbx.transpose_heads(lo[:, 2 * d:], vt_lo, ld=3 * d, B=B, S=S, H=H, hd=hd)
     full, out = _guarded(torch, B * S * d)
     full_lo, out_lo = _guarded(torch, B * S * d)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     scale = 8.0
-    gbx.attn_fused(hi, lo, hi[:, d:], lo[:, d:], vt_hi, vt_lo, out, ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=hd,
+    gbx.attn_fused(hi, lo, hi[:, d:], lo[:, d:], hi[:, 2 * d:], lo[:, 2 * d:], out, ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=hd,
                    scale=scale, out_lo=out_lo if pair_out else None, causal=causal, err_flag=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -240,8 +236,10 @@ def run_fused(gbx, torch, B, S, H, causal, pair_out):
     _check_guards(full)
 
 
-# S 1024: 8 query tiles and 16 steps of keys; S 200, 36, 132: ragged tiles and steps
-@pytest.mark.parametrize("B,S,H", [(2, 64, 3), (1, 1024, 2), (2, 200, 2), (3, 36, 2), (1, 132, 1), (4, 256, 4)])
+# S 1024: 8 query tiles and 16 steps of keys; S 200, 37, 130, 1: ragged tiles and
+# steps (any S: V is read from the QKV rows in place)
+@pytest.mark.parametrize("B,S,H", [(2, 64, 3), (1, 1024, 2), (2, 200, 2), (3, 37, 2), (1, 130, 1), (4, 256, 4),
+                                   (2, 1, 2)])
 @pytest.mark.parametrize("causal,pair_out", [(True, True), (True, False), (False, False)])
 def test_attn_fused(gbx, cuda, B, S, H, causal, pair_out):
     import torch
@@ -251,7 +249,7 @@ def test_attn_fused(gbx, cuda, B, S, H, causal, pair_out):
 def test_attn_fused_rejects_other_shapes(gbx, cuda):
     import torch
     x = torch.zeros(1 << 16, dtype=torch.float32, device="cuda")
-    for kw in (dict(hd=32), dict(S=6), dict(ld=3 * 64 + 2), dict(B=0)):
+    for kw in (dict(hd=32), dict(ld_out=66), dict(ld=3 * 64 + 2), dict(B=0)):
         args = dict(ld=3 * 64, ld_out=64, B=1, S=8, H=1, hd=64, scale=8.0)
         args.update(kw)
         with pytest.raises(gbx.GbxError):

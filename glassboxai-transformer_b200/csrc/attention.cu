@@ -17,7 +17,8 @@
 // in rounding (a few fp32 ulps of each weight).
 //
 // One CTA works on one (head, 128-query tile) unit at a time, persistent over
-// the units (longest first), 352 threads:
+// the units (longest first, each round of units dealt in the opposite
+// direction to the last), 352 threads:
 //   warp 0      TMA producer: the unit's Q tile (128 x 64, hi and lo), then per
 //               step of 64 keys the K tile and the V tile into a two-stage
 //               ring (128-byte swizzled rows, 32 floats per block), both
@@ -71,7 +72,9 @@ constexpr uint32_t kAttData = kAttQBytes + kAttStages * 2 * kAttKVBytes;   // 19
 constexpr int kAttBars = 22;
 // after the barriers and the TMEM slot: the softmax halves' exchange slots
 constexpr size_t kAttXBytes = 2 * 4 * 2 * 32 * sizeof(float);
-constexpr size_t kAttSmem = kAttData + 1024 + 8 * kAttBars + 16 + kAttXBytes;
+// then each softmax warp's output staging block: 32 rows x 16 floats
+constexpr size_t kAttStageBytes = kAttSoftWarps * 32 * 16 * sizeof(float);
+constexpr size_t kAttSmem = kAttData + 1024 + 8 * kAttBars + 16 + kAttXBytes + kAttStageBytes;
 constexpr uint32_t kTmS = 0, kTmPlo = 128, kTmO = 256, kTmCols = 512;
 
 struct AttnArgs {
@@ -103,6 +106,19 @@ __device__ __forceinline__ AttnUnit attn_unit(int u, const AttnArgs& a)
     const int kend = a.causal ? min(a.S, (w.qt + 1) * kAttQ) : a.S;
     w.nkt = (kend + kAttKT - 1) / kAttKT;
     return w;
+}
+
+// The unit a CTA takes in its k-th round (a.units when none is left):
+// rounds of gridDim.x units in the longest-first order, dealt forwards in
+// even rounds and backwards in odd ones, so a CTA that drew a longer unit
+// in one round draws a shorter one in the next.  For 8 x 16 heads x 1024
+// causal on 148 SMs the busiest CTA gets 64 key steps (70 dealt forwards
+// every round; 62.3 on average); for one sequence of 25 heads, 16 (22).
+__device__ __forceinline__ int attn_round_unit(int k, const AttnArgs& a)
+{
+    const long long G = gridDim.x;
+    const long long u = k * G + ((k & 1) ? G - 1 - (long long)blockIdx.x : (long long)blockIdx.x);
+    return u < a.units ? (int)u : a.units;
 }
 
 __device__ __forceinline__ float att_div(float x, float d, float rd)
@@ -183,7 +199,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
             bool ok = true;
             int q_loads = 0;
             uint32_t issued = 0, lastpar = 0;   // ring stages with loads issued, parity of their last phase
-            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+            for (int k = 0, u = attn_round_unit(0, a); u < a.units && ok; u = attn_round_unit(++k, a)) {
                 const AttnUnit w = attn_unit(u, a);
                 if (!tc::mbar_wait(qempty, qph ^ 1, abort, kAttWaitNs)) break;
                 tc::mbar_arrive_expect_tx(qfull, kAttQBytes);
@@ -239,7 +255,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
             uint32_t kph = 0, qph = 0;
             uint32_t g = 0;   // global step (buffer = g & 1, its use count = g >> 1)
             bool ok = true;
-            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+            for (int k = 0, u = attn_round_unit(0, a); u < a.units && ok; u = attn_round_unit(++k, a)) {
                 const AttnUnit w = attn_unit(u, a);
                 if (!tc::mbar_wait(qfull, qph, abort, kAttWaitNs)) break;
                 qph ^= 1;
@@ -292,7 +308,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
             uint32_t vph = 0;
             uint32_t g = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+            for (int k = 0, u = attn_round_unit(0, a); u < a.units && ok; u = attn_round_unit(++k, a)) {
                 const AttnUnit w = attn_unit(u, a);
                 for (int j = 0; j < w.nkt; ++j, ++g) {
                     const uint32_t i = g & 1;
@@ -345,6 +361,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
         const uint32_t lane_addr = (uint32_t)(32 * quarter) << 16;
         const uint32_t col = 32 * half;
         float* const xmax = reinterpret_cast<float*>(tmem_slot + 4);   // [2 parity][4 quarter][2 half][32]
+        float* const stage = xmax + 2 * 4 * 2 * 32 + (warp - 3) * 32 * 16;
         const int bar_id = 1 + quarter;                             // named barriers 1-4
         // The pair's barrier also decides, for both halves alike, whether to
         // stop: it returns the OR of the two halves' `stop` (a half never
@@ -364,30 +381,100 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
         };
         uint32_t g = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+        float o[32];   // the running output of this thread's 32 columns
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c] = 0.0f;
+        float alpha_pend = 0.0f;
+        // adds O[gg] (the running output rescaled first) and releases its buffer
+        auto take_o = [&](uint32_t gg, float alpha) -> bool {
+            const uint32_t i = gg & 1;
+            const bool ready = tc::mbar_wait(ofull(i), (gg >> 1) & 1, abort, kAttWaitNs);
+            if (!__all_sync(0xffffffffu, ready)) return false;
+            tc::fence_after_sync();
+            float v[32];
+            tc::tmem_ld32(tmem + lane_addr + kTmO + 64 * i + col, v);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha, v[c]);
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(oempty(i));
+            return true;
+        };
+        // A unit's last output and its epilogue (the two halves' row sums
+        // added, the division, the stores) wait until the next unit's first
+        // step has written its P: the tensor pipe runs that step's value
+        // product and the next score product meanwhile, instead of waiting
+        // for the epilogue.  `pend`: unit pw (this half's row sum pl) waits.
+        bool pend = false;
+        AttnUnit pw{};
+        float pl = 0.0f;
+        // Takes pw's last output O[g - 1], writes pw's rows and clears the
+        // running output; false stops both halves (decided at the pair's
+        // barrier).  xpar: the exchange slot's parity, one that no half
+        // reads any more (not that of the step whose barrier was passed last).
+        auto finish = [&](bool good, uint32_t xpar) -> bool {
+            good = good && take_o(g - 1, alpha_pend);
+            float* const xl = xmax + (((xpar * 4 + quarter) * 2) * 32);
+            xl[half * 32 + lane] = pl;
+            if (pair_sync(!good)) return false;
+            const float lsum = pl + xl[(1 - half) * 32 + lane];
+            pair_sync(false);   // the slot is read before either half writes it again
+            {
+                const float rl = 1.0f / lsum;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) o[c] = att_div(o[c], lsum, rl);
+            }
+            // The warp's 32 rows x 32 columns leave through its staging block,
+            // 16 columns of one plane at a time: each lane writes 64 bytes of
+            // its own row, then each store instruction writes 64 contiguous
+            // bytes of 8 rows (a lane per 16 bytes) instead of 16 bytes of 32
+            // rows.  16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3)
+            // (conflict-free both ways).
+            {
+                const int r0 = pw.qt * kAttQ + 32 * quarter;   // the warp's first query row
+                const int64_t base = ((int64_t)pw.b * a.S + r0) * a.ld_out + (int64_t)pw.h * kAttHD + col;
+                const int rr = lane >> 2, cq = lane & 3;          // read side: row in an 8-row group, chunk
+#pragma unroll
+                for (int pn = 0; pn < 2; ++pn) {
+                    if (pn == 1 && !a.out_lo) break;
+                    float* const dst = pn ? a.out_lo : a.out;
+#pragma unroll
+                    for (int hb = 0; hb < 2; ++hb) {
+                        __syncwarp();
+#pragma unroll
+                        for (int cc = 0; cc < 4; ++cc) {
+                            float4 v = make_float4(o[16 * hb + 4 * cc], o[16 * hb + 4 * cc + 1], o[16 * hb + 4 * cc + 2],
+                                                   o[16 * hb + 4 * cc + 3]);
+                            if (a.out_lo) {
+                                float4 h4, l4;
+                                split4(v, h4, l4);
+                                v = pn ? l4 : h4;
+                            }
+                            *reinterpret_cast<float4*>(stage + lane * 16 + 4 * (cc ^ ((lane >> 1) & 3))) = v;
+                        }
+                        __syncwarp();
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            const int r = 8 * t + rr;
+                            const float4 v =
+                                *reinterpret_cast<const float4*>(stage + r * 16 + 4 * (cq ^ ((r >> 1) & 3)));
+                            if (r0 + r < a.S)
+                                *reinterpret_cast<float4*>(dst + base + (int64_t)r * a.ld_out + 16 * hb + 4 * cq) = v;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = 0.0f;
+            return true;
+        };
+        for (int k = 0, u = attn_round_unit(0, a); u < a.units; u = attn_round_unit(++k, a)) {
             const AttnUnit w = attn_unit(u, a);
             const int p = w.qt * kAttQ + row_in_tile;   // this thread's query position
             const int lim = a.causal ? min(p + 1, a.S) : a.S;
-            float m = -INFINITY, l = 0.0f, alpha_pend = 0.0f;
-            float o[32];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = 0.0f;
-            // adds O[gg] (the running output rescaled first) and releases its buffer
-            auto take_o = [&](uint32_t gg, float alpha) -> bool {
-                const uint32_t i = gg & 1;
-                const bool ready = tc::mbar_wait(ofull(i), (gg >> 1) & 1, abort, kAttWaitNs);
-                if (!__all_sync(0xffffffffu, ready)) return false;
-                tc::fence_after_sync();
-                float v[32];
-                tc::tmem_ld32(tmem + lane_addr + kTmO + 64 * i + col, v);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha, v[c]);
-                tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(oempty(i));
-                return true;
-            };
+            float m = -INFINITY, l = 0.0f;
+            bool broke = false;   // both halves left the step loop at the same barrier
             for (int j = 0; j < w.nkt; ++j, ++g) {
                 const uint32_t i = g & 1;
                 // a failed wait here or in the previous step's take_o stops
@@ -427,7 +514,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 float* const xm = xmax + (((i * 4 + quarter) * 2) * 32);
                 xm[half * 32 + lane] = mt;
                 if (pair_sync(!ready)) {
-                    ok = false;
+                    broke = true;
                     break;
                 }
                 mt = fmaxf(mt, xm[(1 - half) * 32 + lane]);
@@ -464,39 +551,29 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 tc::fence_before_sync();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(pfull(i));
-                if (j >= 1 && !take_o(g - 1, alpha_pend)) ok = false;   // both stop at the next barrier
+                if (j == 0) {
+                    // the previous unit's last output and rows
+                    if (pend && !finish(true, (g + 1) & 1)) {
+                        broke = true;
+                        break;
+                    }
+                    pend = false;
+                } else if (!take_o(g - 1, alpha_pend)) {
+                    ok = false;   // both stop at the next barrier (this unit's or the next's, or finish's)
+                }
                 alpha_pend = alpha;
             }
-            // the last step's output (skipped once a barrier has decided to stop)
-            if (ok && !take_o(g - 1, alpha_pend)) ok = false;
-            // the row's sum: both halves (the slot of the last step's parity
-            // is free again: both halves have passed that step's barrier)
-            float* const xl = xmax + ((((g & 1) * 4 + quarter) * 2) * 32);
-            xl[half * 32 + lane] = l;
-            if (pair_sync(!ok)) {
+            if (broke) {
                 ok = false;
+                pend = false;
                 break;
             }
-            l += xl[(1 - half) * 32 + lane];
-            pair_sync(false);   // the slot is read before either half writes it again
-            if (p < a.S) {
-                const float rl = 1.0f / l;
-                const int64_t off = ((int64_t)w.b * a.S + p) * a.ld_out + (int64_t)w.h * kAttHD + col;
-#pragma unroll
-                for (int c = 0; c < 32; c += 4) {
-                    float4 v = make_float4(att_div(o[c], l, rl), att_div(o[c + 1], l, rl), att_div(o[c + 2], l, rl),
-                                           att_div(o[c + 3], l, rl));
-                    if (a.out_lo) {
-                        float4 h4, l4;
-                        split4(v, h4, l4);
-                        *reinterpret_cast<float4*>(a.out + off + c) = h4;
-                        *reinterpret_cast<float4*>(a.out_lo + off + c) = l4;
-                    } else {
-                        *reinterpret_cast<float4*>(a.out + off + c) = v;
-                    }
-                }
-            }
+            pend = true;
+            pw = w;
+            pl = l;
         }
+        // the last unit (a failed take_o of its last step is decided here)
+        if (pend && !finish(ok, g & 1)) ok = false;
     }
 
     __syncthreads();   // every role has left its loop (all waits are bounded)

@@ -9,12 +9,13 @@
 // and each product is formed as hi.hi + hi.lo + lo.hi; TMEM accumulates at
 // most 64 products of a sum (one head width, or one step of 64 keys), and
 // the output is summed over the steps in fp32 registers.  The softmax is the
-// online form: per row a running maximum m and sum l, e = expf(x - m), and a
-// rescale of the running output by expf(m_old - m_new) when the maximum
-// grows; the scores are divided by `scale` exactly (q = x * (1/scale) plus one
-// FMA correction, as gbx_attn_softmax_rows does) and keys past the diagonal
-// weigh exactly 0.  It differs from the reference's single-pass softmax only
-// in rounding (a few fp32 ulps of each weight).
+// online form: per row a running maximum m and sum l of the raw scores x,
+// weights e = 2^(x c - m c) with c = log2(e) / scale (one FFMA and the
+// hardware's base-2 exponential), and a rescale of the running output by
+// 2^((m_old - m_new) c) when the maximum grows; keys past the diagonal weigh
+// exactly 0 and the output is divided by l exactly.  It differs from the
+// reference's single-pass softmax only in rounding (about 2^-21 of each
+// weight: the exponential's approximation and the rounding of x c).
 //
 // One CTA works on one (head, 128-query tile) unit at a time, persistent over
 // the units (longest first, each round of units dealt in the opposite
@@ -84,9 +85,7 @@ struct AttnArgs {
     int B, S, H;
     int nqt;      // query tiles per head
     int units;    // B * H * nqt
-    float scale;
-    float rscale;
-    int pow2;     // scale is a power of two: x / scale == x * rscale exactly
+    float c2;     // log2(e) / scale: a weight is 2^(x c2 - m c2) for raw score x, row maximum m
     int causal;
     int* err;
 };
@@ -119,6 +118,17 @@ __device__ __forceinline__ int attn_round_unit(int k, const AttnArgs& a)
     const long long G = gridDim.x;
     const long long u = k * G + ((k & 1) ? G - 1 - (long long)blockIdx.x : (long long)blockIdx.x);
     return u < a.units ? (int)u : a.units;
+}
+
+// 2^x by the hardware's base-2 approximation (ex2.approx, subnormal results
+// flushed to 0: such a weight is below 2^-126 of the row's largest, which
+// weighs 1).  The softmax's exponentials are e^y = 2^(y log2 e), with the
+// 1/scale folded into the same constant.
+__device__ __forceinline__ float att_exp2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ float att_div(float x, float d, float rd)
@@ -494,14 +504,7 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 const int k0 = j * kAttKT + (int)col;
                 const int nvis = max(0, min(32, lim - k0));
                 const bool full = __all_sync(0xffffffffu, nvis == 32);
-                float mt = -INFINITY;
-                if (a.pow2) {
-#pragma unroll
-                    for (int c = 0; c < 32; ++c) s[c] *= a.rscale;   // exact: scale is a power of two
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 32; ++c) s[c] = att_div(s[c], a.scale, a.rscale);
-                }
+                float mt = -INFINITY;   // on the raw scores (the maximum commutes with 1/scale)
                 if (full) {
 #pragma unroll
                     for (int c = 0; c < 32; ++c) mt = fmaxf(mt, s[c]);
@@ -519,20 +522,19 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 }
                 mt = fmaxf(mt, xm[(1 - half) * 32 + lane]);
                 const float m_new = fmaxf(m, mt);
-                const float alpha = m_new == -INFINITY ? 1.0f : expf(m - m_new);
+                // e^((x - m) / scale) = 2^(x c2 - m c2): one FFMA and one
+                // exponential per weight (m_new is finite once a key is
+                // visible).  Every column's exponential is formed and the
+                // hidden ones are then set to 0: one loop for full and masked
+                // steps (two loops, one per case, spill at the 168-register cap)
+                const float alpha = m_new == -INFINITY ? 1.0f : att_exp2((m - m_new) * a.c2);
+                const float mc = m_new == -INFINITY ? 0.0f : m_new * a.c2;
                 float sum = 0.0f;
-                if (full) {
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) {
-                        s[c] = expf(s[c] - m_new);
-                        sum += s[c];
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 32; ++c) {
-                        s[c] = c < nvis ? expf(s[c] - m_new) : 0.0f;
-                        sum += s[c];
-                    }
+                for (int c = 0; c < 32; ++c) {
+                    const float e = att_exp2(fmaf(s[c], a.c2, -mc));
+                    s[c] = c < nvis ? e : 0.0f;
+                    sum += s[c];
                 }
                 l = fmaf(l, alpha, sum);
                 m = m_new;
@@ -655,12 +657,7 @@ extern "C" int gbx_attn_fused(const float* q_hi, const float* q_lo, const float*
     a.H = H;
     a.nqt = nqt;
     a.units = B * H * nqt;
-    a.scale = scale;
-    a.rscale = 1.0f / scale;
-    {
-        int e = 0;
-        a.pow2 = frexpf(scale, &e) == 0.5f ? 1 : 0;
-    }
+    a.c2 = (float)(1.4426950408889634 / (double)scale);   // log2(e) / scale
     a.causal = causal ? 1 : 0;
     a.err = err_flag;
     if (cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem) !=

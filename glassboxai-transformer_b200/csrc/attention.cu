@@ -15,7 +15,8 @@
 // 2^((m_old - m_new) c) when the maximum grows; keys past the diagonal weigh
 // exactly 0 and the output is divided by l exactly.  It differs from the
 // reference's single-pass softmax only in rounding (about 2^-21 of each
-// weight: the exponential's approximation and the rounding of x c).
+// weight: the exponential's approximation and the rounding of x c; the
+// weights' tf32 pair carries them to 2^-21 as well).
 //
 // One CTA works on one (head, 128-query tile) unit at a time, persistent over
 // the units (longest first, each round of units dealt in the opposite
@@ -538,13 +539,18 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 }
                 l = fmaf(l, alpha, sum);
                 m = m_new;
-                // P as a tf32 pair (each weight is finite and at most 1): hi
-                // over S[g], lo in its own columns
+                // P as a tf32 pair, hi over S[g], lo in its own columns.  Each
+                // weight is in [0, 1]: hi = the weight rounded to 10 mantissa
+                // bits, ties away from 0 (carry 0x1000 into the kept bits,
+                // clear the 13 dropped ones; two integer operations, where the
+                // cvt.rna conversion measured slower), lo = the exact
+                // remainder, whose own low 13 bits the MMA ignores (at most
+                // 2^-21 of the weight)
                 float lo[32];
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
-                    const float h = to_tf32(s[c]);
-                    lo[c] = to_tf32(s[c] - h);
+                    const float h = __uint_as_float((__float_as_uint(s[c]) + 0x1000u) & 0xffffe000u);
+                    lo[c] = s[c] - h;
                     s[c] = h;
                 }
                 tc::tmem_st32(tmem + lane_addr + kTmS + 64 * i + col, s);

@@ -510,9 +510,12 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
 #pragma unroll
                     for (int c = 0; c < 32; ++c) mt = fmaxf(mt, s[c]);
                 } else {
+                    // hidden keys become -inf, whose weight 2^-inf is exactly 0
 #pragma unroll
-                    for (int c = 0; c < 32; ++c)
-                        if (c < nvis) mt = fmaxf(mt, s[c]);
+                    for (int c = 0; c < 32; ++c) {
+                        s[c] = c < nvis ? s[c] : -INFINITY;
+                        mt = fmaxf(mt, s[c]);
+                    }
                 }
                 // the row's step maximum: both halves
                 float* const xm = xmax + (((i * 4 + quarter) * 2) * 32);
@@ -525,16 +528,15 @@ attn_fused_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_const
                 const float m_new = fmaxf(m, mt);
                 // e^((x - m) / scale) = 2^(x c2 - m c2): one FFMA and one
                 // exponential per weight (m_new is finite once a key is
-                // visible).  Every column's exponential is formed and the
-                // hidden ones are then set to 0: one loop for full and masked
-                // steps (two loops, one per case, spill at the 168-register cap)
+                // visible; a hidden key's -inf gives 0).  One loop for full and
+                // masked steps: two loops, one per case, spill at the
+                // 168-register cap
                 const float alpha = m_new == -INFINITY ? 1.0f : att_exp2((m - m_new) * a.c2);
                 const float mc = m_new == -INFINITY ? 0.0f : m_new * a.c2;
                 float sum = 0.0f;
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
-                    const float e = att_exp2(fmaf(s[c], a.c2, -mc));
-                    s[c] = c < nvis ? e : 0.0f;
+                    s[c] = att_exp2(fmaf(s[c], a.c2, -mc));
                     sum += s[c];
                 }
                 l = fmaf(l, alpha, sum);

@@ -246,6 +246,17 @@ def test_attn_fused(gbx, cuda, B, S, H, causal, pair_out):
     run_fused(gbx, torch, B, S, H, causal, pair_out)
 
 
+# More units than a B200 has SMs (148), so each CTA runs several rounds: the
+# rounds dealt in alternating directions, and each unit's epilogue deferred
+# past the next unit's first step (6 x 40 heads x 2 query tiles: 480 units,
+# 3-4 a CTA; 3 x 50 x 2 ragged tiles: 300 units)
+@pytest.mark.parametrize("B,S,H,causal,pair_out", [(6, 256, 40, True, True), (3, 200, 50, False, False)])
+def test_attn_fused_several_units_per_cta(gbx, cuda, B, S, H, causal, pair_out):
+    import torch
+    assert B * H * -(-S // 128) > 2 * torch.cuda.get_device_properties(0).multi_processor_count
+    run_fused(gbx, torch, B, S, H, causal, pair_out)
+
+
 def test_attn_fused_rejects_other_shapes(gbx, cuda):
     import torch
     x = torch.zeros(1 << 16, dtype=torch.float32, device="cuda")

@@ -39,7 +39,11 @@
 //               32 of the 64 columns each; a thread reads its S[j] columns
 //               from TMEM, writes its part of P_j as a tf32 pair back into
 //               TMEM (hi over S[j]), then adds its 32 columns of O[j-1] into
-//               fp32 registers with the pending rescale
+//               fp32 registers with the pending rescale.  A unit's last
+//               output and its rows wait until the next unit's first P is
+//               written; each warp's 32 x 32 block of rows leaves through a
+//               shared-memory staging block (64 contiguous bytes of 8 rows a
+//               store instruction)
 // TMEM columns: S/P_hi [0,64) and [64,128), P_lo [128,192) and [192,256),
 // O [256,320) and [320,384), each double-buffered by step parity.
 // Every mbarrier wait is bounded (1 s, %globaltimer): a wait that runs out

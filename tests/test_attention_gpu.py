@@ -1,6 +1,9 @@
-"""Parity of the per-head attention products on the tensor cores
-(gbx_attn_scores, gbx_transpose_heads, gbx_attn_softmax_rows_pair,
-gbx_attn_values), called through the C ABI.
+"""Parity of the attention on the tensor cores, called through the C ABI: the
+per-head products (gbx_attn_scores, gbx_transpose_heads,
+gbx_attn_softmax_rows_pair, gbx_attn_values) and the fused kernel
+(gbx_attn_fused, Q, K and V read from the QKV rows in place; held to a
+float64 softmax-attention within a bound on the score error plus 2^-17 of
+sum w |v|).
 
 Reference semantics: attentionScoresKernel (transformer.cu:213-232) forms
 dot[h][p][s] = sum_i Q[p, h*hd+i] K[s, h*hd+i] for every key s <= p;

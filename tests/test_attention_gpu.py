@@ -201,7 +201,7 @@ def test_attn_softmax_pair_is_split_of_softmax(gbx, cuda, S, scale):
         gbx.attn_softmax_rows_pair(scores, hi, hi, rows=rows, L=S, S=S, scale=scale)
 
 
-def run_fused(gbx, torch, B, S, H, causal, pair_out):
+def run_fused(gbx, torch, B, S, H, causal, pair_out, scale=8.0):
     hd = 64
     d = H * hd
     qkv = _qkv(torch, B, S, H, hd, 11 * S + B + H)
@@ -209,7 +209,6 @@ def run_fused(gbx, torch, B, S, H, causal, pair_out):
     full, out = _guarded(torch, B * S * d)
     full_lo, out_lo = _guarded(torch, B * S * d)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    scale = 8.0
     gbx.attn_fused(hi, lo, hi[:, d:], lo[:, d:], hi[:, 2 * d:], lo[:, 2 * d:], out, ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=hd,
                    scale=scale, out_lo=out_lo if pair_out else None, causal=causal, err_flag=err)
     torch.cuda.synchronize()
@@ -258,6 +257,14 @@ def test_attn_fused_several_units_per_cta(gbx, cuda, B, S, H, causal, pair_out):
     import torch
     assert B * H * -(-S // 128) > 2 * torch.cuda.get_device_properties(0).multi_processor_count
     run_fused(gbx, torch, B, S, H, causal, pair_out)
+
+
+# a scale that is not a power of two (the weights fold log2(e) / scale into one
+# constant, so every scale takes the same path)
+@pytest.mark.parametrize("causal", [True, False])
+def test_attn_fused_other_scale(gbx, cuda, causal):
+    import torch
+    run_fused(gbx, torch, 2, 200, 3, causal, True, scale=float(np.sqrt(np.float32(80.0))))
 
 
 def test_attn_fused_rejects_other_shapes(gbx, cuda):

@@ -2,7 +2,7 @@
 """Benchmark of the B200 layer-kernel hot path (one JSON line on rank 0).
 
 A step is one pass of the hot path of ``TransformerModel::forward`` over one
-batch (see glassboxai-transformer_b200/chain.py): embed, then per layer
+batch (glassboxai-transformer_b200/chain.py): embed, then per layer
 residual+LayerNorm, row softmax over every head of every sequence,
 residual+LayerNorm and bias+GELU, then the final LayerNorm of each
 sequence's last row.  Default workload: GPT-2 XL prefill, 32 sequences x 1024
@@ -11,18 +11,30 @@ tokens per GPU, d 1600, ff 6400, 25 heads, 48 layers, bf16 GGUF tables.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 N > 1 runs one process per GPU under torch.distributed.run; each rank owns
-whole sequences (weak scaling: the per-GPU batch is fixed), no collective
-touches the data; the step time is the max over ranks.
+whole sequences, no collective touches the data, and every time is the max
+over ranks.  ``value`` is timed with no per-launch instrumentation; the
+per-kernel figures come from a separate instrumented pass after it.  The
+default line also carries, measured in the same run:
 
-``--impl reference`` times the reference's loops on the host cores (the
-oracle's restatement, all cores) on a bounded sample of the same workload,
-and, when the reference build is present, also the reference's own CUDA
-kernels on one GPU; only rank 0 runs it.
+  strong_1m      the 1,048,576-token workload split across the N ranks
+                 (strong scaling), each rank's final rows copied to host
+                 memory inside the timed region (the host gather)
+  decode, small  the launch-bound GPT-2 XL decode step and GPT-2 small chain,
+                 replayed as CUDA graphs
+  model_forward  (N = 1) the drop-in TransformerModel forward end to end on a
+                 random-init GPT-2 medium GGUF file
+  cpu_baseline   (N = 1) the reference's loops on the host cores
+
+``--impl reference`` runs the reference's side only (rank 0; the product
+library is never loaded): its loops restated in C on all host cores, one
+bounded token sample through every layer of the chain per step, and its own
+CUDA kernels (transformer.cu compiled unmodified) on one GPU.
 """
 from __future__ import annotations
 
 import argparse
 import importlib
+import importlib.util
 import json
 import math
 import os
@@ -34,36 +46,28 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+PKG = "glassboxai-transformer_b200"
 
 METRIC = "layer-kernel HBM GB/s (% of B200 peak); tokens/s at GPT-2 XL shape, 1-8 GPU"
 
-# name -> (ChainShape kwargs, description, Chain kwargs, scaling)
-#   weak:   every rank runs the whole batch given here (per-GPU work fixed as N grows)
-#   strong: the batch given here is the global batch, split across ranks by whole sequences
-WORKLOADS = {
-    "gpt2-xl-prefill": (dict(batch=32, seq=1024, d=1600, ff=6400, heads=25, layers=48, vocab=50257, n_ctx=1024,
-                             table_dtype=30),
-                        "GPT-2 XL prefill B32xS1024 per GPU, d1600, ff6400, 25 heads, 48 layers, bf16 GGUF tables",
-                        dict(score_std=1.0), "weak"),
-    "gpt2-medium-prefill": (dict(batch=8, seq=1024, d=1024, ff=4096, heads=16, layers=24, vocab=50257, n_ctx=1024,
-                                 table_dtype=1),
-                            "GPT-2 medium prefill B8xS1024, d1024, ff4096, 16 heads, 24 layers, f16 GGUF tables",
-                            dict(score_std=1.0), "weak"),
-    "gpt2-xl-decode": (dict(batch=256, seq=1, d=1600, ff=6400, heads=25, layers=48, vocab=50257, n_ctx=2048,
-                            table_dtype=30, kv_len=2048, pos_off=2047),
-                       "GPT-2 XL decode step B256xS1 at position 2047, 2048-long softmax rows, d1600, ff6400, "
-                       "25 heads, 48 layers, bf16 tables", dict(score_std=math.sqrt(2.0)), "weak"),
-    "gpt2-small-chain": (dict(batch=1, seq=64, d=768, ff=3072, heads=12, layers=12, vocab=50257, n_ctx=1024,
-                              table_dtype=0),
-                         "GPT-2 small chain B1xS64, d768, ff3072, 12 heads, 12 layers, f32 tables",
-                         dict(score_std=1.0), "weak"),
-    "tokens-1m-sharded": (dict(batch=512, seq=2048, d=4096, ff=16384, heads=32, layers=1, vocab=50257, n_ctx=2048,
-                               table_dtype=1, chunk=64),
-                          "1,048,576 tokens (B512xS2048) split by whole sequences across the GPUs, d4096, ff16384, "
-                          "32 heads, f16 tables; embed + one layer of the chain + final LN per step, in passes of "
-                          "64 sequences", dict(score_std=1.0), "strong"),
-}
-DEFAULT_WORKLOAD = "gpt2-xl-prefill"
+
+def _load_workloads():
+    """The workload table, loaded from its file so that importing it does not
+    import the package (whose __init__ maps libgbx.so)."""
+    name = "gbx_workloads"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, PKG, "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+WL = _load_workloads()
+WORKLOADS = WL.WORKLOADS
+DEFAULT_WORKLOAD = WL.DEFAULT_WORKLOAD
+DTYPE_NAME = {0: "f32", 1: "f16", 30: "bf16"}
 
 
 def load_peak():
@@ -97,14 +101,20 @@ NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_po
 
 
 class ClockSampler:
-    def __init__(self, index, period=0.1):
-        self.index, self.period = index, period
+    """SM clock and clock-event reasons of one GPU, sampled by NVML every
+    `period` seconds on a thread while the `with` block runs."""
+
+    def __init__(self, index, period=0.1, enabled=True):
+        self.index, self.period, self.enabled = index, period, enabled
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()
         self._t = None
 
     def __enter__(self):
+        self._nv = None
+        if not self.enabled:
+            return self
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -149,7 +159,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # distributed plumbing (timing only: no collective on the data path)
 
-def dist_setup(n_gpus):
+def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -183,6 +193,18 @@ def max_over_ranks(x, world, device):
     return float(t.item())
 
 
+def gather_over_ranks(x, world, device):
+    """[x of rank 0, x of rank 1, ...] (floats; None is sent as NaN)."""
+    if world == 1:
+        return [x]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([math.nan if x is None else float(x)], dtype=torch.float64, device=device)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [None if math.isnan(v.item()) else v.item() for v in out]
+
+
 def relaunch_distributed(n):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr", "127.0.0.1", "--master-port", os.environ.get("MASTER_PORT", "29531"), *sys.argv]
@@ -190,7 +212,7 @@ def relaunch_distributed(n):
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the reference loops (oracle restatement) on the host cores
+# CPU side: the reference loops (oracle restatement) on the host cores
 
 _TABLES = {}
 
@@ -215,8 +237,9 @@ def _cpu_tables(shape):
 class CpuChainSample:
     """The chain for `n_tok` tokens of `shape` on the host cores, through the
     oracle's C restatement of the reference loops: embed for those tokens,
-    then per layer residual+LN, the softmax rows of those tokens for every
-    head, residual+LN and bias+GELU.  Inputs are generated once."""
+    then for every layer of the shape residual+LN, the softmax rows of those
+    tokens for every head, residual+LN and bias+GELU, then the final LN of
+    the tokens' rows.  Inputs are generated once."""
 
     def __init__(self, shape, n_tok, seed=0):
         import numpy as np
@@ -240,124 +263,223 @@ class CpuChainSample:
         self.bias = (0.02 * rng.standard_normal(F)).astype(np.float32)
         self.scores = normal(n_tok * H, L)
 
-    def run(self, layers, nthreads):
-        """Seconds for embed + `layers` layers, and the per-token seconds of
-        the full chain (embed + shape.layers layers) extrapolated from them."""
+    def run(self, nthreads, layers=None):
+        """Seconds for embed + `layers` layers (default: all of the shape's)
+        + the final LayerNorm of the sample's rows."""
         import oracle
         s = self.shape
+        layers = s.layers if layers is None else layers
         t0 = time.perf_counter()
         oracle.embed(self.ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, s.d, s.vocab, s.n_ctx,
                      seq=s.seq, pos_off=s.pos_off, nthreads=nthreads)
-        t_embed = time.perf_counter() - t0
-        t0 = time.perf_counter()
         for _ in range(layers):
             oracle.residual_layernorm(self.x, self.r, self.g, self.b, nthreads=nthreads)
             oracle.softmax_rows(self.scores, nthreads=nthreads)
             oracle.residual_layernorm(self.x, self.r, self.g, self.b, nthreads=nthreads)
             oracle.bias_gelu(self.pre, self.bias, nthreads=nthreads)
-        t_layer = (time.perf_counter() - t0) / max(layers, 1)
-        return t_embed + layers * t_layer, (t_embed + s.layers * t_layer) / self.n_tok
+        oracle.residual_layernorm(self.x[:max(1, self.n_tok // s.seq)], self.r[:max(1, self.n_tok // s.seq)],
+                                  self.g, self.b, nthreads=nthreads)
+        return time.perf_counter() - t0
 
 
 def cpu_sample_tokens(shape, cores, target_s):
-    """Tokens whose one-layer chain takes about target_s on `cores` threads,
-    from a short timed probe (at least 64 tokens per thread; at most the
-    workload's own tokens, and at most 64M softmax entries)."""
+    """Tokens whose whole chain (every layer) takes about target_s on `cores`
+    threads, from a short one-layer probe (at least 64 tokens per thread; at
+    most the workload's own tokens and 64M softmax entries)."""
     cap = max(1, (64 << 20) // (shape.heads * shape.L))   # score sample <= 64M floats
-    probe_n = min(max(64 * cores, 256), cap)
+    probe_n = min(max(64 * cores, 256), cap, shape.tokens)
     probe = CpuChainSample(shape, probe_n, seed=7)
-    probe.run(1, cores)
-    secs, _ = probe.run(1, cores)
-    n = int(probe_n * target_s / max(secs, 1e-6))
-    return max(1, min(max(n, probe_n), shape.tokens, cap))
+    probe.run(cores, layers=1)
+    one = probe.run(cores, layers=1)
+    per_tok = one * shape.layers / probe_n          # a layer dominates the embed
+    n = int(target_s / max(per_tok, 1e-9))
+    return max(1, min(n, shape.tokens, cap))
 
 
 def cpu_baseline(shape, target_s=12.0):
-    """The reference loops on all host cores: a bounded token sample run
-    through enough layers of the chain for about target_s of CPU work."""
+    """The reference loops on all host cores: one bounded token sample run
+    through the whole chain (every layer), about target_s of CPU work."""
     import oracle
     cores = oracle.max_threads()
-    n_tok = cpu_sample_tokens(shape, cores, 1.0)
+    n_tok = cpu_sample_tokens(shape, cores, target_s / 2)
     sample = CpuChainSample(shape, n_tok, seed=1)
-    sample.run(1, cores)                     # first touch of the sample's pages
-    one, _ = sample.run(1, cores)
-    layers = int(max(1, min(shape.layers, target_s / max(one, 1e-3))))
-    spent, per_tok = sample.run(layers, cores)
-    return {"value": 1.0 / per_tok, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{n_tok} tokens x {layers} layers of the chain (embed + residual+LN, their {shape.heads} "
-                      f"softmax rows of length {shape.L} each, residual+LN, bias+GELU), extrapolated to "
-                      f"{shape.layers} layers; oracle C restatement of the reference loops, gcc -O3, "
-                      f"{cores} threads", "seconds": round(spent, 2)}
+    sample.run(cores, layers=1)              # first touch of the sample's pages
+    spent = sample.run(cores)
+    return {"value": n_tok / spent, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n_tok} tokens through embed + all {shape.layers} layers of the chain (residual+LN, their "
+                      f"{shape.heads} softmax rows of length {shape.L} each, residual+LN, bias+GELU) + final LN; "
+                      f"oracle C restatement of the reference loops, gcc -O3, {cores} threads",
+            "seconds": round(spent, 2)}
 
 
 # ---------------------------------------------------------------------------
+# our side
 
-def run_ours(args, shape, desc, chain_kw, scaling):
+def _new_chain(shape, device, chain_kw, seed):
+    chain_mod = importlib.import_module(PKG + ".chain")
+    return chain_mod.Chain(shape, device, seed=seed, **chain_kw)
+
+
+def _free(*objs):
+    import torch
+    for o in objs:
+        if o is not None and getattr(o, "graph", None) is not None:
+            o.graph = None
+    del objs
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+def _timed_steps(fn, steps, world, device, stream, sample_clocks=True):
+    """Barrier, sync, `steps` calls of fn between two events on `stream`, sync,
+    barrier: (ms per step, max over ranks; clock summary of this rank)."""
+    import torch
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(device.index if device.index is not None else 0, enabled=sample_clocks) as clk:
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world, device) / steps
+    return ms, clk.summary()
+
+
+def kernel_table(timers, peak, peak_kind):
+    """Per kernel: launches, average event time, algorithmic bytes per launch
+    and the bandwidth they give."""
+    out = {}
+    for name, recs in timers.items():
+        us = [1000.0 * a.elapsed_time(b) for a, b, _ in recs]
+        nbytes = [n for _, _, n in recs]
+        tot_us, tot_b = sum(us), sum(nbytes)
+        out[name] = {"launches": len(us), "avg_us": tot_us / len(us), "bytes_per_launch": tot_b // len(us),
+                     "gbs": tot_b / (tot_us * 1e-6) / 1e9, "frac_of_" + peak_kind: tot_b / (tot_us * 1e-6) / 1e9 / peak}
+    return out
+
+
+def strong_1m(args, rank, world, device, stream, peak, peak_kind):
+    """The 1,048,576-token workload (512 sequences x 2048, d 4096) split
+    across the ranks by whole sequences: each rank runs its share in passes
+    of at most 64 sequences and copies its final LayerNorm rows to pinned
+    host memory (the host gather) inside the timed region."""
     import dataclasses
     import torch
-    rank, world, local = dist_setup(args.gpus)
+    shard = importlib.import_module(PKG + ".shard")
+    w = WORKLOADS["tokens-1m-sharded"]
+    full = WL.ChainShape(**w.shape)
+    first, count = shard.shard_sequences(full.batch, rank, world)
+    shape = dataclasses.replace(full, batch=count)
+    chain = _new_chain(shape, device, w.chain, seed=2000 + rank)
+    host = torch.empty(chain.out.shape, dtype=torch.float32).pin_memory()
+
+    def step():
+        chain.step(stream)
+        host.copy_(chain.out, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(device)
+    assert int(chain.err.item()) == 0, "embed reported out-of-range ids"
+    steps = max(3, min(args.steps, 10))
+    ms, clk = _timed_steps(step, steps, world, device, stream)
+    ms_local_mhz = clk.get("sm_mhz")
+    mhz = gather_over_ranks(ms_local_mhz, world, device)
+    bytes_rank = shape.bytes_per_step()
+    res = {"workload": "tokens-1m-sharded", "description": w.description, "scaling": "strong",
+           "tokens": full.tokens, "n_gpus": world, "sequences_per_gpu": count, "passes_per_gpu": shape.n_chunks,
+           "steps": steps, "warmup": 3, "ms_per_step": ms, "tokens_per_s": full.tokens / (ms * 1e-3),
+           "tokens_per_s_per_gpu": full.tokens / (ms * 1e-3) / world,
+           "hbm": {"bytes_per_step_per_gpu": bytes_rank, "gbs_per_gpu": bytes_rank / (ms * 1e-3) / 1e9,
+                   "frac": bytes_rank / (ms * 1e-3) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},
+           "clocks": clk, "sm_mhz_median_per_rank": mhz,
+           "ms_x_sm_mhz": ms * statistics.median([m for m in mhz if m]) if any(mhz) else None,
+           "host_gather": f"each rank copies its [{count}, {full.d}] final LayerNorm rows to pinned host memory in "
+                          "the timed region (the only exchange; no collective on the data path)",
+           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": int(host.numel() * 4)}
+    _free(chain)
+    return res
+
+
+def launch_bound(name, args, rank, world, device, stream, peak, peak_kind, pdl=True):
+    """A launch-bound workload replayed as one CUDA graph per step (the row
+    kernels launched with programmatic dependent launch): tokens/s, us per
+    step and the step's byte floor at the measured copy bandwidth."""
+    import torch
+    G = importlib.import_module(PKG)
+    w = WORKLOADS[name]
+    shape = WL.ChainShape(**w.shape)
+    prev = G.set_pdl(pdl)
+    try:
+        chain = _new_chain(shape, device, w.chain, seed=3000 + rank)
+        chain.step(stream)
+        torch.cuda.synchronize(device)
+        chain.capture_graph()
+        for _ in range(5):
+            chain.replay()
+        torch.cuda.synchronize(device)
+        assert int(chain.err.item()) == 0, "embed reported out-of-range ids"
+        steps = max(20, args.steps * 5)
+        ms, clk = _timed_steps(chain.replay, steps, world, device, stream)
+    finally:
+        G.set_pdl(prev)
+    nbytes = shape.bytes_per_step()
+    floor_us = nbytes / (peak * 1e9) * 1e6
+    res = {"workload": name, "description": w.description, "tokens_per_step": shape.tokens,
+           "tokens_per_s": shape.tokens / (ms * 1e-3) * world, "us_per_step": ms * 1e3,
+           "launches_per_step": shape.launches_per_step(), "bytes_per_step": nbytes,
+           "byte_floor_us": floor_us, "frac_of_floor": floor_us / (ms * 1e3), "steps": steps,
+           "cuda_graph": True, "programmatic_dependent_launch": pdl, "clocks": clk,
+           "l2": chain.l2_note()}
+    _free(chain)
+    return res
+
+
+def run_ours(args):
+    import dataclasses
+    import torch
+    rank, world, local = dist_setup()
     assert torch.cuda.is_available(), "bench.py needs a CUDA device"
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    from importlib import import_module
-    chain_mod = import_module("glassboxai-transformer_b200.chain")
-    shard = import_module("glassboxai-transformer_b200.shard")
-    global_batch = shape.batch * (world if scaling == "weak" else 1)
-    if scaling == "strong":
-        first, count = shard.shard_sequences(shape.batch, rank, world)
+    G = importlib.import_module(PKG)
+    shard = importlib.import_module(PKG + ".shard")
+    w = WORKLOADS[args.workload]
+    shape = WL.ChainShape(**w.shape)
+    global_batch = shape.batch * (world if w.scaling == "weak" else 1)
+    if w.scaling == "strong":
+        _, count = shard.shard_sequences(shape.batch, rank, world)
         shape = dataclasses.replace(shape, batch=count)
     if args.pdl:
-        import_module("glassboxai-transformer_b200").set_pdl(True)
-    chain = chain_mod.Chain(shape, device, seed=1000 + rank, **chain_kw)
+        G.set_pdl(True)
+    chain = _new_chain(shape, device, w.chain, seed=1000 + rank)
     stream = torch.cuda.current_stream(device)
     torch.cuda.synchronize(device)
+    peak, peak_kind = load_peak()
 
     for _ in range(args.warmup):
         chain.step(stream)
     torch.cuda.synchronize(device)
     assert int(chain.err.item()) == 0, "embed reported out-of-range ids"
-
-    timers = {}
     if args.graph:
         chain.capture_graph()
         chain.replay()
         torch.cuda.synchronize(device)
+    step = chain.replay if args.graph else (lambda: chain.step(stream))
 
-    # --- device-resident timing -------------------------------------------------
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(device)
-    with ClockSampler(device.index if device.index is not None else 0) as clk:
-        start.record(stream)
-        for _ in range(args.steps):
-            if args.graph:
-                chain.replay()
-            else:
-                chain.step(stream, timers=timers)
-        end.record(stream)
-        torch.cuda.synchronize(device)
-    barrier(world)
-    ms_local = start.elapsed_time(end)
-    ms = max_over_ranks(ms_local, world, device)
-    ms_per_step = ms / args.steps
-    if args.graph:
-        # events cannot be timed inside a replayed graph: per-kernel times
-        # come from one eager step after the timed region
+    # --- device-resident timing, no per-launch instrumentation ------------------
+    ms_per_step, clocks = _timed_steps(step, args.steps, world, device, stream)
+
+    # --- per-kernel times: a separate instrumented pass ---------------------------
+    timers = {}
+    k_steps = max(1, min(3, args.steps))
+    for _ in range(k_steps):
         chain.step(stream, timers=timers)
-        torch.cuda.synchronize(device)
-
-    kernels = {}
-    for name, pairs in timers.items():
-        durs = [a.elapsed_time(b) for a, b in pairs]
-        kernels[name] = {"launches": len(durs), "avg_us": 1000.0 * sum(durs) / len(durs)}
-    byte_of = {"embed": shape.bytes_embed(), "layernorm": shape.bytes_ln(),
-               "residual_layernorm": shape.bytes_residual_ln(), "softmax_rows": shape.bytes_softmax(),
-               "bias_gelu": shape.bytes_gelu(), "final_layernorm": shape.bytes_final()}
-    peak, peak_kind = load_peak()
-    for name, k in kernels.items():
-        k["bytes_per_launch"] = byte_of[name]
-        k["gbs"] = byte_of[name] / (k["avg_us"] * 1e-6) / 1e9
-        k["frac_of_" + peak_kind] = k["gbs"] / peak
+    torch.cuda.synchronize(device)
+    kernels = kernel_table(timers, peak, peak_kind)
 
     # --- end to end through the API with host buffers -----------------------------
     ids_host = chain.ids.cpu().pin_memory()
@@ -365,29 +487,18 @@ def run_ours(args, shape, desc, chain_kw, scaling):
 
     def e2e_step():
         chain.ids.copy_(ids_host, non_blocking=True)      # H2D of the step's token ids
-        if args.graph:
-            chain.replay()
-        else:
-            chain.step(stream)
+        step()
         out_host.copy_(chain.out, non_blocking=True)      # D2H of the step's result
         stream.synchronize()                              # the caller reads the result
 
     for _ in range(2):
         e2e_step()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(device)
-    e_start.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e_end.record(stream)
-    torch.cuda.synchronize(device)
-    barrier(world)
-    e_ms = max_over_ranks(e_start.elapsed_time(e_end), world, device) / args.steps
+    e_ms, _ = _timed_steps(e2e_step, args.steps, world, device, stream, sample_clocks=False)
 
     tokens_total = global_batch * shape.seq
     top = "softmax_rows" if "softmax_rows" in kernels else max(kernels, key=lambda k: kernels[k]["avg_us"])
     sm = kernels[top]
+    bytes_step = shape.bytes_per_step()
     result = {
         "metric": METRIC,
         "value": tokens_total / (ms_per_step * 1e-3),
@@ -397,48 +508,66 @@ def run_ours(args, shape, desc, chain_kw, scaling):
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": scaling,
+        "scaling": w.scaling,
         "vs_baseline": None,
-        "dtype": "f32 (activations; tables " + {0: "f32", 1: "f16", 30: "bf16"}[shape.table_dtype] + ")",
+        "dtype": "f32 (activations; tables " + DTYPE_NAME[shape.table_dtype] + ")",
         "data": "synthetic (seeded torch.randn / randint on device; random-init tables)",
-        "config": {"workload": args.workload, "description": desc, "tokens_per_gpu": shape.tokens,
+        "config": {"workload": args.workload, "description": w.description, "tokens_per_gpu": shape.tokens,
                    "global_batch": global_batch, "seq_len": shape.seq, "layers": shape.layers,
-                   "chunks_per_step": shape.n_chunks, "cuda_graph": bool(args.graph),
+                   "passes_per_step": shape.n_chunks, "cuda_graph": bool(args.graph),
                    "programmatic_dependent_launch": bool(args.pdl),
                    "parallelism": f"row shards of whole sequences over {world} GPU(s), no collective",
                    "l2": chain.l2_note()},
-        "hbm": {"bytes_per_step": shape.bytes_per_step(),
-                "gbs": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
-                "frac": shape.bytes_per_step() / (ms_per_step * 1e-3) / 1e9 / peak,
-                "peak": peak, "peak_kind": peak_kind},
+        "hbm": {"bytes_per_step": bytes_step, "gbs": bytes_step / (ms_per_step * 1e-3) / 1e9,
+                "frac": bytes_step / (ms_per_step * 1e-3) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},
         "roofline": {"kernel": top, "bound": "hbm", "achieved": sm["gbs"], "peak": peak,
                      "unit": "GB/s", "frac": sm["gbs"] / peak, "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_launch": byte_of[top],
-                     "traffic": traffic_from_profiles(top, args.workload)},
+                     "algorithmic_bytes_per_launch": sm["bytes_per_launch"],
+                     "traffic": traffic_from_profiles(top, args.workload),
+                     "traffic_source": f"dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed "
+                                       f"ncu summary profiles/{top}_{args.workload}.md (not measured in this run)"},
         "kernels": kernels,
-        "kernel_timing": "one eager step after the timed region (graph replay is timed as a whole)" if args.graph
-                         else "every launch of the timed region",
+        "kernel_timing": f"{k_steps} instrumented step(s) after the timed region, CUDA events around every launch "
+                         "on the launching stream (the timed region itself has none)",
         "gpu_launches": shape.launches_per_step() * args.steps,
-        "clocks": clk.summary(),
+        "clocks": clocks,
         "e2e": {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(chain.ids.numel() * 4), "d2h_bytes_per_step": int(chain.out.numel() * 4),
                 "ms_per_step": e_ms,
                 "path": "C ABI launches with pinned host token ids in, final LayerNorm rows out"
                         + (" (step replayed as a CUDA graph)" if args.graph else "")},
     }
+    _free(chain)
+    del chain
+    if args.workload == DEFAULT_WORKLOAD and not args.no_extras:
+        result["strong_1m"] = strong_1m(args, rank, world, device, stream, peak, peak_kind)
+        result["decode"] = launch_bound("gpt2-xl-decode", args, rank, world, device, stream, peak, peak_kind)
+        result["small"] = launch_bound("gpt2-small-chain", args, rank, world, device, stream, peak, peak_kind)
+        if world == 1:
+            try:
+                result["model_forward"] = run_model_forward(args, WL.ChainShape(**WORKLOADS["gpt2-medium-prefill"].shape),
+                                                            "gpt2-medium-prefill",
+                                                            WORKLOADS["gpt2-medium-prefill"].description, "ours",
+                                                            emit=False)
+            except Exception as e:   # report, never lose the headline line
+                result["model_forward"] = {"unavailable": f"{type(e).__name__}: {e}"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(shape)
+        result["cpu_baseline"] = cpu_baseline(WL.ChainShape(**w.shape))
     if rank == 0:
         print(json.dumps(result), flush=True)
-    chain.graph = None
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# the reference's side (never loads the product library)
+
 def reference_gpu_kernels(shape):
     """The reference's own kernels (its transformer.cu compiled unmodified) on
-    one GPU for one layer of the chain, with its launch shapes."""
+    one GPU for one layer of the chain, with its launch shapes: per layer LN
+    x2, residual add x2, softmax once per head of each sequence, GELU in
+    place; the chain's time is layers x that (its embed when d <= 1024)."""
     import torch
     import oracle
     if not oracle.ref_available():
@@ -500,34 +629,38 @@ def reference_gpu_kernels(shape):
                     "chain = layers x that"}
 
 
-def run_reference(args, shape, desc):
+def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import oracle
+    w = WORKLOADS[args.workload]
+    shape = WL.ChainShape(**w.shape)
     cores = oracle.max_threads()
-    # bounded sample per step: n_s tokens through embed + one layer of the
-    # chain on all host cores (about 2 s of work), extrapolated to the layer count
-    n_s = cpu_sample_tokens(shape, cores, 2.0)
+    # one bounded token sample per step, through every layer of the chain, on
+    # all host cores (about 1.5 s of work per step)
+    n_s = cpu_sample_tokens(shape, cores, 1.5)
     sample = CpuChainSample(shape, n_s, seed=3)
     for _ in range(args.warmup):
-        sample.run(1, cores)
-    per_tok = []
-    for _ in range(args.steps):
-        per_tok.append(sample.run(1, cores)[1])
-    sec_per_tok = statistics.mean(per_tok)
-    value = 1.0 / sec_per_tok
+        sample.run(cores)
+    secs = [sample.run(cores) for _ in range(args.steps)]
+    step_s = statistics.mean(secs)
+    value = n_s / step_s
     out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec_per_tok * shape.tokens * 1e3,
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+           "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": "f32",
            "data": "synthetic (seeded numpy)",
-           "config": {"workload": args.workload, "description": desc, "sample_tokens_per_step": n_s},
+           "config": {"workload": args.workload, "description": w.description,
+                      "step": f"{n_s} of the workload's {shape.tokens} tokens per GPU through embed + all "
+                              f"{shape.layers} layers + final LN",
+                      "sample_tokens_per_step": n_s},
+           "ms_per_full_workload_step_extrapolated": step_s * 1e3 * shape.tokens / n_s,
            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                            "sample": f"{n_s} tokens per step through embed + 1 layer of the chain (all "
-                                      f"{shape.heads} softmax rows of length {shape.L} per token), extrapolated "
-                                      f"to {shape.layers} layers; the reference's loops restated in C "
-                                      f"(oracle/gbx_oracle.c) on {cores} host threads"},
+                            "sample": f"{n_s} tokens per step through embed + all {shape.layers} layers of the chain "
+                                      f"({shape.heads} softmax rows of length {shape.L} per token per layer) + "
+                                      f"final LN; the reference's loops restated in C (oracle/gbx_oracle.c) on "
+                                      f"{cores} host threads"},
            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     try:
         import torch
@@ -537,6 +670,9 @@ def run_reference(args, shape, desc):
         out["reference_gpu_kernels"] = {"unavailable": f"{type(e).__name__}: {e}"}
     print(json.dumps(out), flush=True)
 
+
+# ---------------------------------------------------------------------------
+# single kernels, contractions, attention products, model forward
 
 def run_kernel(args, shape):
     """One hot-path kernel alone on `--rows` rows of the workload's shape
@@ -843,7 +979,7 @@ def forward_flops(shape, tokens, seq):
     return weights + attn + 2.0 * (tokens // seq) * d * shape.vocab
 
 
-def run_model_forward(args, shape, desc, impl):
+def run_model_forward(args, shape, workload, desc, impl, emit=True):
     """The drop-in TransformerModel::forward end to end through its C ABI
     (libgbx_model.so: token ids from host memory in, last-row logits to host
     memory out), wall-clock per call on a random-init GGUF of the workload's
@@ -853,8 +989,8 @@ def run_model_forward(args, shape, desc, impl):
     import numpy as np
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
-        return
-    path = bench_gguf(shape, args.workload)
+        return None
+    path = bench_gguf(shape, workload)
     ids = np.random.default_rng(1).integers(0, shape.vocab, shape.batch * shape.seq).astype(np.int32)
     one = ids[:shape.seq].copy()
 
@@ -868,7 +1004,7 @@ def run_model_forward(args, shape, desc, impl):
             ts.append(time.perf_counter() - t0)
         return statistics.median(ts)
 
-    out = {"mode": "model-forward", "impl": impl, "workload": args.workload, "description": desc,
+    out = {"mode": "model-forward", "impl": impl, "workload": workload, "description": desc,
            "weights": {0: "f32", 1: "f16", 30: "bf16"}[shape.table_dtype],
            "data": "synthetic (random-init weights in a GGUF file, seeded token ids)", "warmup": args.warmup,
            "steps": args.steps}
@@ -894,7 +1030,10 @@ def run_model_forward(args, shape, desc, impl):
                     "single_sequence_ms": s1 * 1e3, "single_sequence_tokens_per_s": shape.seq / s1,
                     "single_sequence_tflops": forward_flops(shape, shape.seq, shape.seq) / s1 / 1e12,
                     "h2d_bytes_per_forward": 4 * N, "d2h_bytes_per_forward": 4 * shape.batch * shape.vocab})
-    print(json.dumps(out), flush=True)
+        m.close()
+    if emit:
+        print(json.dumps(out), flush=True)
+    return out
 
 
 def main():
@@ -906,6 +1045,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the strong_1m / decode / small / model_forward records of the default line")
     ap.add_argument("--kernel", choices=["embed", "layernorm", "residual_layernorm", "softmax_rows", "attn_softmax_rows",
                                          "bias_gelu"] + sorted(LINEAR_KERNELS) + ATTN_KERNELS,
                     help="time one kernel alone on --rows rows of the workload's shape")
@@ -921,17 +1062,16 @@ def main():
         ap.error("--warmup must be >= 3")
     if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
         relaunch_distributed(args.gpus)
-    shape_kw, desc, chain_kw, scaling = WORKLOADS[args.workload]
-    chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
-    shape = chain_mod.ChainShape(**shape_kw)
+    w = WORKLOADS[args.workload]
+    shape = WL.ChainShape(**w.shape)
     if args.model_forward:
-        run_model_forward(args, shape, desc, args.impl)
+        run_model_forward(args, shape, args.workload, w.description, args.impl)
+    elif args.impl == "reference":
+        run_reference(args)
     elif args.kernel:
         run_kernel(args, shape)
-    elif args.impl == "reference":
-        run_reference(args, shape, desc)
     else:
-        run_ours(args, shape, desc, chain_kw, scaling)
+        run_ours(args)
 
 
 if __name__ == "__main__":

@@ -44,11 +44,13 @@ SIGNATURES = {
     "gbx_status_string": [_int],
     "gbx_last_error": [],
     "gbx_set_pdl": [_int],
+    "gbx_set_first_wait_limit": [ctypes.c_uint64],
     "gbx_dequant": [_vp, _int, _vp, _i64, _vp],
     "gbx_embed": [_vp, _vp, _int, _vp, _int, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, _vp],
     "gbx_layernorm": [_vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
     "gbx_layernorm_pair": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
     "gbx_residual_layernorm": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
+    "gbx_final_layernorm": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _f, _vp],
     "gbx_bias_gelu": [_vp, _vp, _vp, _i64, _int, _vp],
     "gbx_softmax_rows": [_vp, _vp, _i64, _int, _vp],
     "gbx_attn_softmax_rows": [_vp, _vp, _i64, _int, _int, _int, _f, _int, _vp],
@@ -60,11 +62,13 @@ SIGNATURES = {
     "gbx_logits": [_vp, _i64, _vp, _int, _vp, _int, _int, _vp],
     "gbx_select_tokens": [_vp, _i64, _int, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
     "gbx_split_tf32": [_vp, _vp, _vp, _i64, _vp],
+    "gbx_linear_set_tiles": [_int, _int, _vp, _vp],
     "gbx_linear": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp],
     "gbx_linear_splitk": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _vp, _i64, _vp, _vp],
     "gbx_linear_splitk_noalloc": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp],
 }
-_RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p}
+_RESTYPES = {"gbx_status_string": ctypes.c_char_p, "gbx_last_error": ctypes.c_char_p,
+             "gbx_set_first_wait_limit": ctypes.c_uint64}
 
 _lib = None
 
@@ -124,6 +128,16 @@ def set_pdl(enable: bool) -> bool:
     return bool(lib().gbx_set_pdl(1 if enable else 0))
 
 
+DEFAULT_WAIT_NS = 1_000_000_000
+
+
+def set_first_wait_limit(ns: int) -> int:
+    """Limit of the first consumer wait of the staged embedding and the
+    tensor-core contractions (0: give up at once; for timeout tests).
+    Returns the previous limit."""
+    return int(lib().gbx_set_first_wait_limit(int(ns)))
+
+
 def dequant(src, dtype: int, dst, n: int, stream=None):
     _check(lib().gbx_dequant(_p(src), dtype, _p(dst), n, _stream(stream)))
 
@@ -147,6 +161,12 @@ def layernorm_pair(x, y_hi, y_lo, gamma, beta, *, rows, d, eps=1e-5, stream=None
 def residual_layernorm(x, r, h_out, y, gamma, beta, *, rows, d, eps=1e-5, xbias=None, stream=None):
     _check(lib().gbx_residual_layernorm(_p(x), _p(r), _p(xbias), _p(h_out), _p(y), _p(gamma), _p(beta),
                                         rows, d, eps, _stream(stream)))
+
+
+def final_layernorm(x, r, y, gamma, beta, *, n_seq, seq, d, eps=1e-5, stream=None):
+    """y[b] = LayerNorm(r[t] + x[t]) for t = b*seq + seq - 1, the last row of
+    each of n_seq sequences (x may be None)."""
+    _check(lib().gbx_final_layernorm(_p(x), _p(r), _p(y), _p(gamma), _p(beta), n_seq, seq, d, eps, _stream(stream)))
 
 
 def bias_gelu(x, out, bias, *, rows, F, stream=None):
@@ -179,6 +199,15 @@ LINEAR_TIMEOUT = 4
 def split_tf32(x, hi, lo, *, n, stream=None):
     """hi = tf32(x), lo = tf32(x - hi): the operand pair gbx_linear reads."""
     _check(lib().gbx_split_tf32(_p(x), _p(hi), _p(lo), n, _stream(stream)))
+
+
+def linear_set_tiles(k_block: int, pair_mode: int):
+    """Tile form of the tensor-core contractions (process-wide): k_block 16 or
+    32, pair_mode -1 auto / 0 never / 1 always CTA pairs.  Returns the
+    previous (k_block, pair_mode)."""
+    pk, pp = ctypes.c_int(0), ctypes.c_int(0)
+    _check(lib().gbx_linear_set_tiles(k_block, pair_mode, ctypes.byref(pk), ctypes.byref(pp)))
+    return pk.value, pp.value
 
 
 def linear(x_hi, x_lo, w_hi, w_lo, y, *, M, N, K, bias=None, resid=None, y_lo=None, act=ACT_NONE, err_flag=None,

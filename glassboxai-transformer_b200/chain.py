@@ -18,14 +18,16 @@ kernels would:
             softmax(scores)               -> probs     (softmax_rows, all heads, all sequences)
             h += attn_out; LN2(h)         -> ln        (residual_layernorm)
             bias + GELU(ffn_pre)          -> ffn_act   (bias_gelu)
-  final:    h_last += ffn_out_last; LN_f  -> out [B, d] (residual_layernorm on each
+  final:    h_last += ffn_out_last; LN_f  -> out [B, d] (final_layernorm: each
                                                         sequence's last row)
 
 Rows are independent, so a batch of B whole sequences is one call per
 kernel (the reference launches per head and has no batch dimension).  When
 the batch needs more device memory than one pass should hold, it runs in
-chunks of ``chunk`` sequences through the same buffers, one chain pass per
-chunk (each chunk's token ids are its own slice).
+passes of at most ``chunk`` sequences through the same buffers
+(``ChainShape.passes()``); every launch of a pass is sized to that pass's own
+sequences, token ids and output rows, so a short last pass reads and writes
+only its own rows.
 
 ``capture_graph`` records one step into a CUDA graph; ``replay`` launches it
 (the decode-sized chains are launch-bound without it).
@@ -40,98 +42,18 @@ uses anyway.
 from __future__ import annotations
 
 import importlib
-from dataclasses import dataclass
+
+from .workloads import ChainShape  # noqa: F401  (re-exported: the shapes chains are built from)
 
 _gbx = importlib.import_module(__package__)
-
-
-@dataclass
-class ChainShape:
-    batch: int          # sequences
-    seq: int            # query rows per sequence
-    d: int              # d_model
-    ff: int             # feed-forward width
-    heads: int
-    layers: int
-    vocab: int = 50257
-    n_ctx: int = 1024
-    table_dtype: int = 30     # GGUF dtype of wte / wpe
-    kv_len: int | None = None  # softmax row length (defaults to seq: causal prefill)
-    pos_off: int = 0
-    chunk: int | None = None   # sequences per pass (default: the whole batch)
-
-    @property
-    def tokens(self):
-        return self.batch * self.seq
-
-    @property
-    def chunk_seqs(self):
-        return min(self.batch, self.chunk or self.batch)
-
-    @property
-    def n_chunks(self):
-        return -(-self.batch // self.chunk_seqs)
-
-    @property
-    def chunk_tokens(self):
-        return self.chunk_seqs * self.seq
-
-    @property
-    def L(self):
-        return self.kv_len if self.kv_len is not None else self.seq
-
-    @property
-    def softmax_rows(self):
-        return self.chunk_seqs * self.heads * self.seq
-
-    def table_es(self):
-        return 4 if self.table_dtype == 0 else 2
-
-    # Algorithmic bytes per launch (each input read once, each output written
-    # once), for one chunk.
-    def bytes_embed(self):
-        # ids + gathered wte rows + distinct wpe rows + output
-        distinct_pos = min(self.seq, self.n_ctx)
-        t = self.chunk_tokens
-        return 4 * t + t * self.d * self.table_es() + distinct_pos * self.d * self.table_es() + 4 * t * self.d
-
-    def bytes_ln(self, rows=None):
-        rows = self.chunk_tokens if rows is None else rows
-        return 8 * rows * self.d + 8 * self.d
-
-    def bytes_residual_ln(self, rows=None):
-        rows = self.chunk_tokens if rows is None else rows
-        return 16 * rows * self.d + 8 * self.d
-
-    def bytes_gelu(self):
-        return 8 * self.chunk_tokens * self.ff + 4 * self.ff
-
-    def bytes_softmax(self):
-        return 8 * self.softmax_rows * self.L
-
-    def bytes_final(self):
-        return 16 * self.chunk_seqs * self.d + 8 * self.d
-
-    def launches_per_chunk(self):
-        return 1 + 1 + 4 * self.layers - 1 + 1
-
-    def launches_per_step(self):
-        return self.n_chunks * self.launches_per_chunk()
-
-    def bytes_per_chunk(self):
-        return (self.bytes_embed() + self.bytes_ln() + (2 * self.layers - 1) * self.bytes_residual_ln()
-                + self.layers * (self.bytes_softmax() + self.bytes_gelu()) + self.bytes_final())
-
-    def bytes_per_step(self):
-        return self.n_chunks * self.bytes_per_chunk()
 
 
 class Chain:
     """Device buffers for one shard and the launch sequence of one step.
 
-    ``timers``: optional dict kernel-name -> list, into which (start, end)
-    CUDA event pairs are appended around every launch (events recorded on the
-    launching stream).
+    ``timers``: optional dict kernel-name -> list, into which
+    (start, end, algorithmic bytes) are appended around every launch (CUDA
+    events recorded on the launching stream).
     """
 
     def __init__(self, shape: ChainShape, device, seed=0, act_std=1.0, table_std=0.02, score_std=1.0,
@@ -183,9 +105,6 @@ class Chain:
         self.up_bias = normal((s.layers, F), 0.02)
         self.gf = normal((d,), 0.1, 1.0)
         self.bf = normal((d,), 0.02)
-        B = s.chunk_seqs
-        self.last_h = torch.empty((B, d), **f32)
-        self.last_f = torch.empty((B, d), **f32)
         self.out = torch.empty((s.batch, d), **f32)
         self.graph = None
 
@@ -220,42 +139,39 @@ class Chain:
                 ", ".join(f"{k} x{c}" for k, c in multi.items()) + "), cycling through up to 1 GB each, so each "
                 "layer's kernels read their inputs from HBM")
 
-    def _chunk(self, c, st, run):
-        import torch
+    def _pass(self, first, B, st, run):
+        """One chain pass over sequences [first, first + B) of the batch."""
         s, G = self.s, _gbx
-        N, d, B = s.chunk_tokens, s.d, s.chunk_seqs
-        ids = self.ids[c * N:(c + 1) * N]
-        run("embed", lambda: G.embed(ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, self.h, n_tok=N,
-                                     d=d, vocab=s.vocab, n_ctx=s.n_ctx, seq=s.seq, pos_off=s.pos_off,
-                                     err_flag=self.err, stream=st))
+        N, d = B * s.seq, s.d
+        ids = self.ids[first * s.seq:(first + B) * s.seq]
+        run("embed", B, lambda: G.embed(ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, self.h, n_tok=N,
+                                        d=d, vocab=s.vocab, n_ctx=s.n_ctx, seq=s.seq, pos_off=s.pos_off,
+                                        err_flag=self.err, stream=st))
         for l in range(s.layers):
             if l == 0:
-                run("layernorm", lambda: G.layernorm(self.h, self.ln, self.g1[0], self.b1[0], rows=N, d=d,
-                                                     stream=st))
+                run("layernorm", B, lambda: G.layernorm(self.h, self.ln, self.g1[0], self.b1[0], rows=N, d=d,
+                                                        stream=st))
             else:
-                run("residual_layernorm",
+                run("residual_layernorm", B,
                     lambda: G.residual_layernorm(self.ffn_out(l - 1), self.h, self.h, self.ln, self.g1[l],
                                                  self.b1[l], rows=N, d=d, stream=st))
-            run("softmax_rows", lambda: G.softmax_rows(self.scores(l), self.probs, rows=s.softmax_rows, L=s.L,
-                                                       stream=st))
-            run("residual_layernorm",
+            run("softmax_rows", B, lambda: G.softmax_rows(self.scores(l), self.probs, rows=s.softmax_rows_of(B),
+                                                          L=s.L, stream=st))
+            run("residual_layernorm", B,
                 lambda: G.residual_layernorm(self.attn_out(l), self.h, self.h, self.ln, self.g2[l], self.b2[l],
                                              rows=N, d=d, stream=st))
-            run("bias_gelu", lambda: G.bias_gelu(self.ffn_pre(l), self.ffn_act, self.up_bias[l], rows=N, F=s.ff,
-                                                 stream=st))
-        # final residual add + ln_f on each sequence's last row (transformer.cu:890-896)
-        with torch.cuda.stream(st):
-            self.last_h.copy_(self.h.view(B, s.seq, d)[:, -1])
-            self.last_f.copy_(self.ffn_out(s.layers - 1).view(B, s.seq, d)[:, -1])
-        out = self.out[c * B:(c + 1) * B]
-        run("final_layernorm", lambda: G.residual_layernorm(self.last_f, self.last_h, None, out, self.gf,
-                                                            self.bf, rows=B, d=d, stream=st))
+            run("bias_gelu", B, lambda: G.bias_gelu(self.ffn_pre(l), self.ffn_act, self.up_bias[l], rows=N, F=s.ff,
+                                                    stream=st))
+        # final residual add + ln_f on each sequence's last row (transformer.cu:883-896)
+        run("final_layernorm", B, lambda: G.final_layernorm(self.ffn_out(s.layers - 1), self.h,
+                                                            self.out[first:first + B], self.gf, self.bf, n_seq=B,
+                                                            seq=s.seq, d=d, stream=st))
 
     def step(self, stream=None, timers=None):
         import torch
         st = stream if stream is not None else torch.cuda.current_stream(self.device)
 
-        def run(name, fn):
+        def run(name, seqs, fn):
             if timers is None:
                 fn()
                 return
@@ -264,10 +180,10 @@ class Chain:
             a.record(st)
             fn()
             b.record(st)
-            timers.setdefault(name, []).append((a, b))
+            timers.setdefault(name, []).append((a, b, self.s.bytes_of(name, seqs)))
 
-        for c in range(self.s.n_chunks):
-            self._chunk(c, st, run)
+        for first, n in self.s.passes():
+            self._pass(first, n, st, run)
         return self.out
 
     def capture_graph(self, timers=None):

@@ -637,6 +637,20 @@ extern "C" int gbx_attn_fused(const float* q_hi, const float* q_lo, const float*
     if (ld < (int64_t)H * hd || ld_out < (int64_t)H * hd)
         return set_error(GBX_EINVAL, "gbx_attn_fused: ld=%lld ld_out=%lld < H*hd", (long long)ld, (long long)ld_out);
     if (out_lo == out) return set_error(GBX_EINVAL, "gbx_attn_fused: out_lo aliases out");
+    {
+        // CTAs store their output rows while other CTAs still read Q, K and V:
+        // no output may overlap an operand's extent
+        const int64_t in_n = ((int64_t)B * S - 1) * ld + (int64_t)H * hd;
+        const int64_t out_n = ((int64_t)B * S - 1) * ld_out + (int64_t)H * hd;
+        auto overlaps = [](const float* a, int64_t na, const float* b, int64_t nb) {
+            return a && b && b < a + na && a < b + nb;
+        };
+        for (const float* o : {(const float*)out, (const float*)out_lo})
+            for (const float* in : {q_hi, q_lo, k_hi, k_lo, v_hi, v_lo})
+                if (overlaps(o, out_n, in, in_n))
+                    return set_error(GBX_EINVAL, "gbx_attn_fused: an output overlaps an operand");
+        if (overlaps(out, out_n, out_lo, out_n)) return set_error(GBX_EINVAL, "gbx_attn_fused: out and out_lo overlap");
+    }
     // the tensor maps: 16-byte bases and strides; the vector output stores
     const bool al = aligned16(q_hi) && aligned16(q_lo) && aligned16(k_hi) && aligned16(k_lo) && aligned16(v_hi) &&
                     aligned16(v_lo) && aligned16(out) && (!out_lo || aligned16(out_lo));

@@ -96,14 +96,15 @@ embed_vec4_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte,
 constexpr int kStageThreads = 256;
 constexpr int kStageMaxTok = 32;          // tokens per CTA: one copying lane each
 constexpr uint32_t kStageBytes = 32768;   // shared-memory bytes per CTA aimed at
-constexpr uint64_t kStageWaitNs = 1000000000ull;
+constexpr uint64_t kStageWaitNs = kDeviceWaitNs;
 constexpr int64_t kStageMinElems = 1 << 20;   // smaller launches take the register path
 
 template <int WT, int PT>
 __global__ void __launch_bounds__(kStageThreads)
 embed_staged_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, const void* __restrict__ wpe,
                     const int32_t* __restrict__ pos_ids, float* __restrict__ out, int64_t n_tok, int tpc,
-                    FastDiv div_n4, int seq, int pos_off, int d, int vocab, int n_ctx, int32_t* __restrict__ err)
+                    FastDiv div_n4, int seq, int pos_off, int d, int vocab, int n_ctx, int32_t* __restrict__ err,
+                    uint64_t first_wait_ns)
 {
     extern __shared__ __align__(128) unsigned char stage[];
     __shared__ __align__(8) uint64_t bar;
@@ -143,7 +144,8 @@ embed_staged_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wt
         bad_s[j] = bad;
     }
     __syncthreads();
-    if (!tc::mbar_wait(bar_a, 0, nullptr, kStageWaitNs)) {
+    // first_wait_ns is kStageWaitNs unless a test shortens it (0: give up at once)
+    if (!(first_wait_ns && tc::mbar_wait(bar_a, 0, nullptr, first_wait_ns))) {
         // the copies did not land within the limit: flag it, give the copies
         // in flight one more limit before the shared memory is released, and
         // leave this CTA's rows unwritten
@@ -243,7 +245,8 @@ static int launch_embed(const int32_t* ids, const void* wte, const void* wpe, co
         if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return check_launch("gbx_embed");
         launch_row_kernel(k, dim3((unsigned)grid_s), dim3(kStageThreads), (size_t)smem, stream, ids, wte, wpe, pos_ids,
-                          out, n_tok, tpc, make_fastdiv((uint32_t)n4), seq, pos_off, d, vocab, n_ctx, err);
+                          out, n_tok, tpc, make_fastdiv((uint32_t)n4), seq, pos_off, d, vocab, n_ctx, err,
+                          first_wait_limit_ns());
     } else if (vec) {
         const int64_t per_cta = (int64_t)kEmbedThreads * kEmbedU;
         const int64_t grid = (total + per_cta - 1) / per_cta;

@@ -57,6 +57,16 @@ inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 // without the attribute.
 bool pdl_enabled();
 
+// Device waits (a CTA waiting on its own copies or its own pipeline) give up
+// after kDeviceWaitNs of %globaltimer time and report a timeout status.  The
+// first consumer wait of the staged embedding and of the tensor-core
+// contractions takes its limit from first_wait_limit_ns() instead
+// (gbx_set_first_wait_limit; kDeviceWaitNs unless a test shortens it; 0 =
+// give up without waiting).  Every drain of copies or MMAs in flight keeps
+// kDeviceWaitNs.
+constexpr uint64_t kDeviceWaitNs = 1000000000ull;
+uint64_t first_wait_limit_ns();
+
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -27,7 +27,8 @@ __device__ __forceinline__ float4 f4add(float4 a, float4 b)
 template <int TPR, int V4, bool RESID>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads)
 ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out, float* y, float* y_lo,
-              const float* __restrict__ gamma, const float* __restrict__ beta, int64_t rows, int d, float eps)
+              const float* __restrict__ gamma, const float* __restrict__ beta, int64_t rows, int d, int64_t ld,
+              float eps)
 {
     grid_dependency_wait();   // see launch_row_kernel
     allow_dependents();
@@ -36,28 +37,29 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
     const int lane = threadIdx.x & (TPR - 1);
     const int64_t row = (int64_t)blockIdx.x * RowCTA<TPR>::rows + threadIdx.x / TPR;
     const bool valid = row < rows;
-    const int64_t off = row * d;
+    const int64_t in_off = row * ld;   // x, r, h_out
+    const int64_t off = row * d;       // y, y_lo
     const float fd = (float)d;
 
     float4 v[V4];
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
         const int c = k * TPR + lane;
-        v[k] = (valid && c < n4) ? ld_stream(x + off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[k] = (valid && c < n4) ? ld_stream(x + in_off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if constexpr (RESID) {
         float4 rv[V4];
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
             const int c = k * TPR + lane;
-            rv[k] = (valid && c < n4) ? ld_stream(r + off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            rv[k] = (valid && c < n4) ? ld_stream(r + in_off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
             const int c = k * TPR + lane;
             if (xbias && c < n4) v[k] = f4add(v[k], ld_param4(xbias + 4 * c));
             v[k] = f4add(rv[k], v[k]);
-            if (h_out && valid && c < n4) st_stream(h_out + off + 4 * c, v[k]);
+            if (h_out && valid && c < n4) st_stream(h_out + in_off + 4 * c, v[k]);
         }
     }
 
@@ -114,22 +116,23 @@ template <bool RESID>
 __global__ void __launch_bounds__(kGeneralCTA)
 ln_general_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out,
                   float* y, float* y_lo, const float* __restrict__ gamma, const float* __restrict__ beta,
-                  int64_t rows, int d, float eps)
+                  int64_t rows, int d, int64_t ld, float eps)
 {
     __shared__ float red[2][kGeneralCTA / 32];
     const float fd = (float)d;
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-        const int64_t off = row * d;
+        const int64_t in_off = row * ld;   // x, r, h_out
+        const int64_t off = row * d;       // y, y_lo
         auto hval = [&](int i) -> float {
-            if (!RESID) return x[off + i];
-            if (h_out) return h_out[off + i];
-            const float xv = xbias ? x[off + i] + xbias[i] : x[off + i];
-            return r[off + i] + xv;
+            if (!RESID) return x[in_off + i];
+            if (h_out) return h_out[in_off + i];
+            const float xv = xbias ? x[in_off + i] + xbias[i] : x[in_off + i];
+            return r[in_off + i] + xv;
         };
         if (RESID && h_out) {
             for (int i = threadIdx.x; i < d; i += kGeneralCTA) {
-                const float xv = xbias ? x[off + i] + xbias[i] : x[off + i];
-                h_out[off + i] = r[off + i] + xv;
+                const float xv = xbias ? x[in_off + i] + xbias[i] : x[in_off + i];
+                h_out[in_off + i] = r[in_off + i] + xv;
             }
             __syncthreads();
         }
@@ -161,25 +164,29 @@ ln_general_kernel(const float* x, const float* r, const float* __restrict__ xbia
 
 template <int TPR, int V4, bool RESID>
 static int launch_ln_vec(const float* x, const float* r, const float* xbias, float* h_out, float* y, float* y_lo,
-                         const float* g, const float* b, int64_t rows, int d, float eps, cudaStream_t stream)
+                         const float* g, const float* b, int64_t rows, int d, int64_t ld, float eps,
+                         cudaStream_t stream)
 {
     const int64_t grid = row_grid<TPR>(rows);
     if (grid < 0) return GBX_ERANGE;
     launch_row_kernel(ln_vec_kernel<TPR, V4, RESID>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads), 0, stream, x,
-                      r, xbias, h_out, y, y_lo, g, b, rows, d, eps);
+                      r, xbias, h_out, y, y_lo, g, b, rows, d, ld, eps);
     return GBX_OK;
 }
 
+// ld: row stride of x, r and h_out in floats (d for contiguous rows); y and
+// y_lo rows are always contiguous.
 template <bool RESID>
 static int launch_ln(const char* what, const float* x, const float* r, const float* xbias, float* h_out, float* y,
-                     float* y_lo, const float* g, const float* b, int64_t rows, int d, float eps, cudaStream_t stream)
+                     float* y_lo, const float* g, const float* b, int64_t rows, int d, int64_t ld, float eps,
+                     cudaStream_t stream)
 {
     RowShape shape;
-    const bool vec = d % 4 == 0 && row_shape(d / 4, &shape) && aligned16(x) && aligned16(y) &&
+    const bool vec = d % 4 == 0 && ld % 4 == 0 && row_shape(d / 4, &shape) && aligned16(x) && aligned16(y) &&
                      (!y_lo || aligned16(y_lo)) && (!RESID || aligned16(r)) && (!h_out || aligned16(h_out)) &&
                      (!xbias || aligned16(xbias)) && (!g || aligned16(g)) && (!b || aligned16(b));
     if (vec) {
-#define GBX_LN_CALL(T, V) launch_ln_vec<T, V, RESID>(x, r, xbias, h_out, y, y_lo, g, b, rows, d, eps, stream)
+#define GBX_LN_CALL(T, V) launch_ln_vec<T, V, RESID>(x, r, xbias, h_out, y, y_lo, g, b, rows, d, ld, eps, stream)
         const int rc = GBX_ROW_DISPATCH(shape, GBX_LN_CALL, GBX_ERANGE);
 #undef GBX_LN_CALL
         if (rc != GBX_OK) return set_error(rc, "%s: rows=%lld d=%d out of range", what, (long long)rows, d);
@@ -187,7 +194,7 @@ static int launch_ln(const char* what, const float* x, const float* r, const flo
         auto k = ln_general_kernel<RESID>;
         const int grid = persistent_grid(k, kGeneralCTA, 0, rows, 4);
         if (grid < 1) return GBX_ECUDA;
-        k<<<grid, kGeneralCTA, 0, stream>>>(x, r, xbias, h_out, y, y_lo, g, b, rows, d, eps);
+        k<<<grid, kGeneralCTA, 0, stream>>>(x, r, xbias, h_out, y, y_lo, g, b, rows, d, ld, eps);
     }
     return check_launch(what);
 }
@@ -202,7 +209,7 @@ extern "C" int gbx_layernorm(const float* x, float* y, const float* gamma, const
     if (rows < 0 || d <= 0) return set_error(GBX_EINVAL, "gbx_layernorm: rows=%lld d=%d", (long long)rows, d);
     if (rows == 0) return GBX_OK;
     if (!x || !y) return set_error(GBX_EINVAL, "gbx_layernorm: null pointer");
-    return launch_ln<false>("gbx_layernorm", x, nullptr, nullptr, nullptr, y, nullptr, gamma, beta, rows, d, eps,
+    return launch_ln<false>("gbx_layernorm", x, nullptr, nullptr, nullptr, y, nullptr, gamma, beta, rows, d, d, eps,
                             reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -214,7 +221,7 @@ extern "C" int gbx_layernorm_pair(const float* x, float* y_hi, float* y_lo, cons
     if (!x || !y_hi || !y_lo) return set_error(GBX_EINVAL, "gbx_layernorm_pair: null pointer");
     if (y_lo == x || y_lo == y_hi) return set_error(GBX_EINVAL, "gbx_layernorm_pair: y_lo must not alias x or y_hi");
     return launch_ln<false>("gbx_layernorm_pair", x, nullptr, nullptr, nullptr, y_hi, y_lo, gamma, beta, rows, d,
-                            eps, reinterpret_cast<cudaStream_t>(stream));
+                            d, eps, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gbx_residual_layernorm(const float* x, const float* r, const float* xbias, float* h_out,
@@ -226,6 +233,33 @@ extern "C" int gbx_residual_layernorm(const float* x, const float* r, const floa
     if (rows == 0) return GBX_OK;
     if (!x || !r || !y) return set_error(GBX_EINVAL, "gbx_residual_layernorm: null pointer");
     if (h_out && h_out == y) return set_error(GBX_EINVAL, "gbx_residual_layernorm: h_out and y must differ");
-    return launch_ln<true>("gbx_residual_layernorm", x, r, xbias, h_out, y, nullptr, gamma, beta, rows, d, eps,
+    return launch_ln<true>("gbx_residual_layernorm", x, r, xbias, h_out, y, nullptr, gamma, beta, rows, d, d, eps,
                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gbx_final_layernorm(const float* x, const float* r, float* y, const float* gamma, const float* beta,
+                                   int64_t n_seq, int seq, int d, float eps, gbx_stream_t stream)
+{
+    if (n_seq < 0 || seq <= 0 || d <= 0)
+        return set_error(GBX_EINVAL, "gbx_final_layernorm: n_seq=%lld seq=%d d=%d", (long long)n_seq, seq, d);
+    if (n_seq == 0) return GBX_OK;
+    if (!r || !y) return set_error(GBX_EINVAL, "gbx_final_layernorm: null pointer");
+    const int64_t ld = (int64_t)seq * d;      // from one sequence's last row to the next's
+    const int64_t first = (int64_t)(seq - 1) * d;
+    if (seq > 1) {
+        // y rows are packed, the input rows are strided: another CTA's input
+        // row could lie under this CTA's output row.
+        const uintptr_t y0 = (uintptr_t)y, y1 = (uintptr_t)(y + n_seq * d);
+        for (const float* in : {x, r}) {
+            if (!in) continue;
+            const uintptr_t a0 = (uintptr_t)in, a1 = (uintptr_t)(in + n_seq * ld);
+            if (a0 < y1 && y0 < a1) return set_error(GBX_EINVAL, "gbx_final_layernorm: y overlaps an input");
+        }
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (x)
+        return launch_ln<true>("gbx_final_layernorm", x + first, r + first, nullptr, nullptr, y, nullptr, gamma, beta,
+                               n_seq, d, ld, eps, st);
+    return launch_ln<false>("gbx_final_layernorm", r + first, nullptr, nullptr, nullptr, y, nullptr, gamma, beta, n_seq,
+                            d, ld, eps, st);
 }

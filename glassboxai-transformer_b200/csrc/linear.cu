@@ -36,6 +36,7 @@
 // (bounded) for its loads in flight, the MMA thread for its MMAs, TMEM is
 // freed, and GBX_LINEAR_TIMEOUT is OR-ed into err_flag.  No cluster
 // multicast: every TMA load fills this CTA's own shared memory.
+#include <atomic>
 #include <cuda.h>
 #include <stdlib.h>
 
@@ -61,7 +62,7 @@ constexpr int kLinTmemCols = kLinBuffers * kLinBN;
 #define GBX_LINEAR_CHUNK_K 128
 #endif
 constexpr int kLinChunkK = GBX_LINEAR_CHUNK_K;   // K elements summed in TMEM before each fp32 promotion
-constexpr uint64_t kLinWaitNs = 1000000000ull;
+constexpr uint64_t kLinWaitNs = kDeviceWaitNs;
 // Heads mode: per epilogue warp, a 32-row x 16-column staging block in
 // shared memory (after the barriers) for coalesced output stores.
 constexpr int kLinStageFloats = 32 * 16;
@@ -121,6 +122,7 @@ struct LinearArgs {
     int x_head_major;   // 1: x's map orders its dimensions (k, head, row, sequence)
     int w_head_major;
     int w_box_rows;     // w rows per TMA box: the tile's, or fewer when N is narrow
+    uint64_t first_wait_ns;   // limit of the MMA thread's first wait (first_wait_limit_ns)
 };
 
 struct TileInfo {
@@ -412,6 +414,7 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
             int buf = 0;
             uint32_t buf_phase = 0;
             bool ok = true;
+            bool first = true;   // the first wait on a load takes a.first_wait_ns (0: give up at once)
             for (int t = unit; t < a.tiles && ok; t += units) {
                 // the last column tile runs only as wide as N needs (a multiple of 16)
                 const TileInfo ti = tile_info<BK, PAIR, HEADS>(t, a);
@@ -430,7 +433,10 @@ linear_tf32x3_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_co
                     const int kb0 = c * C::chunk_blocks;
                     const int kb1 = kb0 + C::chunk_blocks < ti.kb_end ? kb0 + C::chunk_blocks : ti.kb_end;
                     for (int kb = kb0; kb < kb1; ++kb) {
-                        if (!tc::mbar_wait(full0 + 8 * stage, phase, abort, kLinWaitNs)) {
+                        const uint64_t limit = first ? a.first_wait_ns : kLinWaitNs;
+                        first = false;
+                        if (limit == 0) *abort = 1;
+                        if (limit == 0 || !tc::mbar_wait(full0 + 8 * stage, phase, abort, limit)) {
                             ok = false;
                             break;
                         }
@@ -837,6 +843,7 @@ static int launch_linear(const float* x_hi, const float* x_lo, const float* w_hi
     a.tiles = (int)(m_blocks * a.n_blocks * zs);
     a.k_blocks = (a.K + BK - 1) / BK;
     a.w_box_rows = C::b_rows;
+    a.first_wait_ns = first_wait_limit_ns();
     if (HEADS && a.n_blocks == 1) {   // a narrow N (a head's width): load only the rows the MMA reads
         const int n16 = (a.N + 15) & ~15;
         const int rows = PAIR ? n16 / 2 : n16;
@@ -921,29 +928,28 @@ extern "C" int gbx_split_tf32(const float* x, float* hi, float* lo, int64_t n, g
     return check_launch("gbx_split_tf32");
 }
 
-// Tile K width: 16 (64-byte rows, 4 pipeline stages; 6 in CTA pairs)
-// unless GBX_LINEAR_BK=32 (128-byte rows) is set in the environment.  CTA
-// pairs (M 256 tiles over two SMs) for M >= kLinPairMinRows unless
-// GBX_LINEAR_PAIR=0; GBX_LINEAR_PAIR=1 forces them.  Read once.
+// Tile K width: 16 (64-byte rows, 4 pipeline stages; 6 in CTA pairs) unless
+// gbx_linear_set_tiles selects 32 (128-byte rows).  CTA pairs (M 256 tiles
+// over two SMs) for M >= kLinPairMinRows unless gbx_linear_set_tiles turns
+// them off (0) or on for every shape (1).  Process-wide, read at each launch.
 constexpr int64_t kLinPairMinRows = 1024;
 constexpr int kLinMaxSplit = 16;   // K slices of gbx_linear_splitk
 
-static int env_int(const char* name, int dflt)
-{
-    const char* e = getenv(name);
-    return (e && *e) ? atoi(e) : dflt;
-}
+static std::atomic<int> g_lin_bk{16};
+static std::atomic<int> g_lin_pair{-1};   // -1 auto, 0 never, 1 always
 
-static int linear_bk()
-{
-    static int bk = env_int("GBX_LINEAR_BK", 16) == 32 ? 32 : 16;
-    return bk;
-}
+static int linear_bk() { return g_lin_bk.load(std::memory_order_relaxed); }
+static int linear_pair_mode() { return g_lin_pair.load(std::memory_order_relaxed); }
 
-static int linear_pair_mode()   // -1 auto, 0 never, 1 always
+extern "C" int gbx_linear_set_tiles(int k_block, int pair_mode, int* prev_k_block, int* prev_pair_mode)
 {
-    static int mode = env_int("GBX_LINEAR_PAIR", -1);
-    return mode;
+    if (k_block != 16 && k_block != 32) return set_error(GBX_EINVAL, "gbx_linear_set_tiles: k_block=%d", k_block);
+    if (pair_mode < -1 || pair_mode > 1)
+        return set_error(GBX_EINVAL, "gbx_linear_set_tiles: pair_mode=%d", pair_mode);
+    const int pk = g_lin_bk.exchange(k_block), pp = g_lin_pair.exchange(pair_mode);
+    if (prev_k_block) *prev_k_block = pk;
+    if (prev_pair_mode) *prev_pair_mode = pp;
+    return GBX_OK;
 }
 
 extern "C" int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,

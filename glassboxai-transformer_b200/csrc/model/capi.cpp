@@ -129,6 +129,30 @@ int gbx_model_forward(gbx_model* m, const int32_t* ids_host, int64_t n_ids, int 
     return GBX_OK;
 }
 
+int gbx_model_forward_hidden(gbx_model* m, const int32_t* ids_host, int64_t n_ids, int batch, float* hidden_host,
+                             int64_t cap)
+{
+    if (!m || !ids_host || !hidden_host || n_ids <= 0 || batch <= 0)
+        return gbx::set_error(GBX_EINVAL, "gbx_model_forward_hidden: bad argument");
+    const int64_t need = (int64_t)(m->model.getNumLayers() + 1) * n_ids * m->model.getEmbedDim();
+    if (cap < need)
+        return gbx::set_error(GBX_ERANGE, "gbx_model_forward_hidden: %lld floats needed, %lld given", (long long)need,
+                              (long long)cap);
+    std::vector<int> ids(ids_host, ids_host + n_ids);
+    std::vector<float> out = m->model.forwardHidden(ids, batch);
+    if (out.empty()) return gbx::set_error(GBX_EINVAL, "%s", m->model.lastError().c_str());
+    std::memcpy(hidden_host, out.data(), out.size() * sizeof(float));
+    return GBX_OK;
+}
+
+int gbx_model_set_fused_attention(gbx_model* m, int on)
+{
+    if (!m) return gbx::set_error(GBX_EINVAL, "gbx_model_set_fused_attention: null model");
+    const int prev = m->model.fusedAttention() ? 1 : 0;
+    m->model.setFusedAttention(on != 0);
+    return prev;
+}
+
 int gbx_model_next_token(gbx_model* m, const int32_t* ids_host, int64_t n_ids, double temperature, double u,
                          int32_t* out_id, int32_t* best, float* best_logit)
 {

@@ -106,10 +106,11 @@ struct TransformerModel::Impl {
     int device = -1;
     // activations (ln, qkv, scores (as probabilities), vt, attn and up hold
     // the hi half of a tf32 pair, *_lo the low half)
-    DevBuf h, ln, ln_lo, qkv, qkv_lo, scores, probs_lo, vt, vt_lo, attn, attn_lo, up, up_lo, last_h, last_y, logits;
+    DevBuf h, ln, ln_lo, qkv, qkv_lo, scores, probs_lo, vt, vt_lo, attn, attn_lo, up, up_lo, last_y, logits;
     DevBuf splitk_ws;      // partial sums of the K-split contractions
     int score_group = 1;   // sequences per attention launch (unfused path)
     bool fused = false;    // attention in one gbx_attn_fused launch (head width 64)
+    bool want_fused = true;   // setFusedAttention
     int sm_count = 148;
     int32_t* ids = nullptr;
     size_t ids_n = 0;
@@ -143,7 +144,7 @@ struct TransformerModel::Impl {
     ~Impl()
     {
         for (DevBuf* b : {&h, &ln, &ln_lo, &qkv, &qkv_lo, &scores, &probs_lo, &vt, &vt_lo, &attn, &attn_lo, &up, &up_lo,
-                          &last_h, &last_y, &logits, &splitk_ws})
+                          &last_y, &logits, &splitk_ws})
             b->release();
         for (float* p : owned) cudaFree(p);
         if (ids) cudaFree(ids);
@@ -273,13 +274,8 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
     int64_t G = kScoreGroupFloats / per_seq;
     G = G < 1 ? 1 : (G > B ? B : G);
     m.score_group = (int)G;
-    // the fused attention needs no score buffers and transposes V of every
-    // sequence at once
-    static const bool unfused_env = [] {
-        const char* e = getenv("GBX_ATTN_UNFUSED");
-        return e && *e && *e != '0';
-    }();
-    m.fused = !unfused_env && headDim_ == 64 && d % 4 == 0;
+    // the fused attention needs no score buffers
+    m.fused = m.want_fused && headDim_ == 64 && d % 4 == 0;
     const int64_t score_floats = m.fused ? 1 : G * per_seq;
     const int64_t vt_floats = m.fused ? 1 : G * seq * d;
     // the largest split-K workspace of the four contractions
@@ -294,7 +290,7 @@ bool TransformerModel::ensureBuffers(int64_t tokens, int seq)
                     m.scores.ensure((size_t)score_floats) && m.probs_lo.ensure((size_t)score_floats) &&
                     m.vt.ensure((size_t)vt_floats) && m.vt_lo.ensure((size_t)vt_floats) &&
                     m.attn.ensure(tokens * d) && m.attn_lo.ensure(tokens * d) && m.up.ensure(tokens * F) &&
-                    m.up_lo.ensure(tokens * F) && m.splitk_ws.ensure(ws) && m.last_h.ensure(B * d) &&
+                    m.up_lo.ensure(tokens * F) && m.splitk_ws.ensure(ws) &&
                     m.last_y.ensure(B * d) &&
                     m.logits.ensure((size_t)B * vocab_);
     if (!ok) return fail("cudaMalloc of activation buffers failed");
@@ -372,7 +368,26 @@ int TransformerModel::nextTokenWithDraw(const std::vector<int>& tokenIDs, double
     return selected;
 }
 
-bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
+void TransformerModel::setFusedAttention(bool on) { impl_->want_fused = on; }
+
+bool TransformerModel::fusedAttention() const { return impl_->want_fused; }
+
+std::vector<float> TransformerModel::forwardHidden(const std::vector<int>& tokenIDs, int batch)
+{
+    if (!loader_.isLoaded() || batch <= 0 || tokenIDs.empty()) {
+        fail("forwardHidden: model not loaded or empty input");
+        return {};
+    }
+    std::vector<float> hidden((size_t)(numLayers_ + 1) * tokenIDs.size() * embedDim_);
+    int cur = -1;
+    cudaGetDevice(&cur);
+    const bool ok = runForward(tokenIDs, batch, hidden.data());
+    if (cur >= 0 && cur != impl_->device) cudaSetDevice(cur);
+    if (!ok) return {};
+    return hidden;
+}
+
+bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch, float* hidden_host)
 {
     Impl& m = *impl_;
     err_.clear();
@@ -413,6 +428,14 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
         cudaMemsetAsync(m.err, 0, sizeof(int32_t), st) != cudaSuccess)
         return fail("host-to-device copy of token ids failed");
     check(gbx_embed(m.ids, m.wte, m.wte_dt, m.wpe, m.wpe_dt, nullptr, m.h.p, N, S, 0, d, V, nCtx_, m.err, gs));
+    // forwardHidden: the residual stream after the embedding and after each layer
+    auto keep_hidden = [&](int slot) {
+        if (hidden_host && rc == GBX_OK &&
+            cudaMemcpyAsync(hidden_host + (size_t)slot * N * d, m.h.p, (size_t)N * d * sizeof(float),
+                            cudaMemcpyDeviceToHost, st) != cudaSuccess)
+            check(GBX_ECUDA);
+    };
+    keep_hidden(0);
 
     const float scale = sqrtf((float)hd);   // transformer.cu:836
     for (int l = 0; l < numLayers_ && rc == GBX_OK; ++l) {
@@ -444,15 +467,11 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
         check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln2_g, L.ln2_b, N, d, 1e-5f, gs));
         linear(m.ln.p, m.ln_lo.p, W.up, L.up_b, nullptr, m.up.p, m.up_lo.p, N, F, d, GBX_ACT_GELU);
         linear(m.up.p, m.up_lo.p, W.down, L.down_b, m.h.p, m.h.p, nullptr, N, d, F, GBX_ACT_NONE);
+        keep_hidden(l + 1);
     }
     if (rc == GBX_OK) {
-        // each sequence's last row of h, then ln_f
-        const size_t pitch = (size_t)S * d * sizeof(float);
-        const size_t row = (size_t)d * sizeof(float);
-        if (cudaMemcpy2DAsync(m.last_h.p, row, m.h.p + (int64_t)(S - 1) * d, pitch, row, batch,
-                              cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-            check(GBX_ECUDA);
-        check(gbx_layernorm(m.last_h.p, m.last_y.p, m.lnf_g, m.lnf_b, batch, d, 1e-5f, gs));
+        // ln_f of each sequence's last row of h (transformer.cu:883-896)
+        check(gbx_final_layernorm(nullptr, m.h.p, m.last_y.p, m.lnf_g, m.lnf_b, batch, S, d, 1e-5f, gs));
         check(gbx_logits(m.last_y.p, batch, m.wte, m.wte_dt, m.logits.p, V, d, gs));
     }
     int32_t err_host = 0;
@@ -460,7 +479,10 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch)
         rc = GBX_ECUDA;
     if (cudaStreamSynchronize(st) != cudaSuccess && rc == GBX_OK) rc = GBX_ECUDA;
     if (rc != GBX_OK) return fail(std::string(gbx_status_string(rc)) + ": " + gbx_last_error());
-    if (err_host & GBX_LINEAR_TIMEOUT) return fail("a tensor-core contraction timed out (its output is incomplete)");
+    // GBX_LINEAR_TIMEOUT and GBX_EMBED_TIMEOUT are the same bit of the shared flag
+    if (err_host & GBX_LINEAR_TIMEOUT)
+        return fail("a device wait timed out (a tensor-core contraction or the staged embedding): the forward's "
+                    "outputs are incomplete");
     if (err_host) return fail("embedding reported out-of-range ids or positions");
     return true;
 }

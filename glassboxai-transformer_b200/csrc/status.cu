@@ -56,11 +56,17 @@ static std::atomic<int> g_pdl{0};
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
+static std::atomic<uint64_t> g_first_wait_ns{kDeviceWaitNs};
+
+uint64_t first_wait_limit_ns() { return g_first_wait_ns.load(std::memory_order_relaxed); }
+
 }  // namespace gbx
 
 extern "C" {
 
 int gbx_set_pdl(int enable) { return gbx::g_pdl.exchange(enable ? 1 : 0); }
+
+uint64_t gbx_set_first_wait_limit(uint64_t ns) { return gbx::g_first_wait_ns.exchange(ns); }
 
 int gbx_version(void) { return 100; }
 

@@ -41,6 +41,8 @@ SIGNATURES = {
     "gbx_model_close": ([_vp], None),
     "gbx_model_config": ([_vp, _vp], _int),
     "gbx_model_forward": ([_vp, _vp, _i64, _int, _vp], _int),
+    "gbx_model_forward_hidden": ([_vp, _vp, _i64, _int, _vp, _i64], _int),
+    "gbx_model_set_fused_attention": ([_vp, _int], _int),
     "gbx_model_next_token": ([_vp, _vp, _i64, ctypes.c_double, ctypes.c_double, _vp, _vp, _vp], _int),
     "gbx_sharded_open": ([_cp, _vp, _int], _vp),
     "gbx_sharded_close": ([_vp], None),
@@ -159,6 +161,23 @@ class Model:
         if rc != 0:
             raise _err(rc)
         return out[0] if batch == 1 else out
+
+    def forward_hidden(self, ids, batch: int = 1) -> np.ndarray:
+        """The residual stream after the embedding and after each layer:
+        [layers + 1, tokens, embed_dim]."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32).ravel()
+        out = np.empty((self.config["num_layers"] + 1, ids.size, self.config["embed_dim"]), dtype=np.float32)
+        rc = lib().gbx_model_forward_hidden(self.h, _np_ptr(ids), ids.size, batch, _np_ptr(out), out.size)
+        if rc != 0:
+            raise _err(rc)
+        return out
+
+    def set_fused_attention(self, on: bool) -> bool:
+        """Fused attention (default) or the per-head products; returns the previous setting."""
+        rc = lib().gbx_model_set_fused_attention(self.h, 1 if on else 0)
+        if rc < 0 or rc > 1:
+            raise _err(rc)
+        return bool(rc)
 
     def next_token(self, ids, temperature=0.0, u=0.0):
         """(selected, best, best_logit) of one generate step with draw u."""

@@ -74,6 +74,20 @@ const char* gbx_last_error(void);
 int gbx_set_pdl(int enable);
 
 /*
+ * Limit of the first consumer wait of the staged embedding (the CTA waiting
+ * for its table rows' bulk copies) and of the tensor-core contractions (the
+ * MMA thread waiting for its first tile loads), process-wide, in ns of
+ * %globaltimer time; 1 s by default, like every other device wait here.  0
+ * makes that wait give up at once, so a test can drive the timeout path:
+ * the kernel sets GBX_EMBED_TIMEOUT / GBX_LINEAR_TIMEOUT in *err_flag, waits
+ * (with the full 1 s limit) for the copies or MMAs it already started,
+ * frees what it holds and returns, leaving its outputs unwritten.  No
+ * counterpart in the reference (whose CUDA_CHECK exits the process,
+ * transformer.cu:24-32).  Returns the previous limit.  For tests only.
+ */
+uint64_t gbx_set_first_wait_limit(uint64_t ns);
+
+/*
  * GGUF tensor decode to fp32 on the device, bit-identical to the reference's
  * host dequant GGUFLoader::loadTensorByIndex (transformer.cu:635-650) with
  * float16ToFloat32 (:508-527: -0 -> +0, every NaN -> 0x7fc00000, subnormals
@@ -133,6 +147,21 @@ int gbx_layernorm_pair(const float* x, float* y_hi, float* y_lo, const float* ga
 int gbx_residual_layernorm(const float* x, const float* r, const float* xbias, float* h_out,
                            float* y, const float* gamma, const float* beta, int64_t rows, int d,
                            float eps, gbx_stream_t stream);
+
+/*
+ * Final LayerNorm of each sequence's last row, replacing the last-row copy
+ * and layerNormKernel launch of TransformerModel::computeLogits
+ * (transformer.cu:883-896) together with the residual epilogue of the last
+ * ffnDownKernel (:292), for n_seq sequences of seq rows in one launch:
+ *   t = b*seq + seq - 1
+ *   y[b*d + i] = LayerNorm(r[t*d + .] + x[t*d + .])[i]    (b < n_seq)
+ * with gbx_layernorm's arithmetic (the add is one fp32 add, as
+ * gbx_residual_layernorm's).  x may be NULL: y = LayerNorm of r's last rows.
+ * x, r: [n_seq*seq, d]; y: [n_seq, d], overlapping neither input when
+ * seq > 1 (GBX_EINVAL).  No row other than each sequence's last is read.
+ */
+int gbx_final_layernorm(const float* x, const float* r, float* y, const float* gamma, const float* beta,
+                        int64_t n_seq, int seq, int d, float eps, gbx_stream_t stream);
 
 /*
  * Bias + GELU(tanh), replacing the ffnUpKernel epilogue
@@ -265,6 +294,20 @@ int gbx_linear(const float* x_hi, const float* x_lo, const float* w_hi, const fl
                gbx_stream_t stream);
 
 /*
+ * Tile configuration of the tensor-core contractions (gbx_linear, its split-K
+ * forms and the attention products), process-wide; no counterpart in the
+ * reference.  k_block: 16 (default; 64-byte swizzled rows) or 32 (128-byte
+ * rows).  pair_mode: -1 (default) CTA pairs (cta_group::2, an M 256 tile on
+ * two SMs) for M >= 1024, 0 never, 1 for every shape.  Every form computes
+ * the same three product terms with fp32 accumulation (results within the
+ * bound stated below, not necessarily bit-identical); it exists so that tests
+ * can run every tile form on any shape, and for tuning.  The previous values
+ * go to prev_* (may be NULL).  Not to be changed while another host thread
+ * launches contractions.
+ */
+int gbx_linear_set_tiles(int k_block, int pair_mode, int* prev_k_block, int* prev_pair_mode);
+
+/*
  * gbx_linear with K cut into ksplit slices of K / ksplit (1 <= ksplit <= 16),
  * for contractions with too few output tiles to fill the GPU (one sequence
  * of 1024 tokens against a d x d projection: 16 CTA-pair tiles for 74 SM
@@ -297,7 +340,10 @@ int gbx_linear_splitk(const float* x_hi, const float* x_lo, const float* w_hi, c
  * first call before any stream capture.  All calls share the one array:
  * calls that can overlap on the GPU (other streams, other host threads)
  * race on it and must be serialised by the caller.  Results are those of
- * gbx_linear_splitk; ksplit 1 or an unsliceable shape runs gbx_linear.
+ * gbx_linear_splitk; ksplit 1 or an unsliceable shape runs gbx_linear, which
+ * needs no scratch, so the size limit applies only to calls that split K.
+ * The cached address assumes the device's primary context (the one the CUDA
+ * runtime uses) and does not survive cudaDeviceReset.
  */
 int gbx_linear_splitk_noalloc(const float* x_hi, const float* x_lo, const float* w_hi, const float* w_lo,
                               const float* bias, const float* resid, float* y, float* y_lo, int64_t M, int N, int K,
@@ -364,7 +410,9 @@ int gbx_attn_values(const float* p_hi, const float* p_lo, const float* vt_hi, co
  * weigh exactly 0.  hd must be 64 (every GPT-2 size); ld and ld_out
  * multiples of 4; operands 16-byte aligned; any S >= 1.  Other shapes return
  * GBX_EINVAL: use gbx_attn_scores, gbx_attn_softmax_rows_pair and
- * gbx_attn_values.  err_flag: as gbx_linear (GBX_LINEAR_TIMEOUT).
+ * gbx_attn_values.  out and out_lo must overlap neither each other nor any
+ * of q, k, v (GBX_EINVAL): no in-place attention over the QKV block.
+ * err_flag: as gbx_linear (GBX_LINEAR_TIMEOUT).
  */
 int gbx_attn_fused(const float* q_hi, const float* q_lo, const float* k_hi, const float* k_lo, int64_t ld,
                    const float* v_hi, const float* v_lo, float* out, float* out_lo, int64_t ld_out, int B, int S,

@@ -49,6 +49,19 @@ int gbx_model_config(gbx_model* m, int32_t out6[6]);
  * logits of each sequence's last token. */
 int gbx_model_forward(gbx_model* m, const int32_t* ids_host, int64_t n_ids, int batch, float* logits_host);
 
+/* The residual stream of gbx_model_forward's sequences after the embedding
+ * and after each layer (no counterpart in the reference; for inspecting a
+ * forward layer by layer): hidden_host receives (num_layers + 1) blocks of
+ * n_ids x embed_dim floats; cap is its capacity in floats (GBX_ERANGE when
+ * too small). */
+int gbx_model_forward_hidden(gbx_model* m, const int32_t* ids_host, int64_t n_ids, int batch, float* hidden_host,
+                             int64_t cap);
+
+/* Attention of head width 64 in one fused launch (on != 0, the default) or as
+ * the per-head products; returns the previous setting (or a GBX_E* code for
+ * a NULL model).  The two differ only in rounding. */
+int gbx_model_set_fused_attention(gbx_model* m, int on);
+
 /* One step of generate's loop without the tokenizer (transformer.cu:986-1028):
  * forward, then the reference's argmax / temperature sampling on the device
  * with the caller's uniform draw u in [0, 1) (used when temperature > 0.01).

@@ -160,6 +160,16 @@ public:
     int nextTokenWithDraw(const std::vector<int>& tokenIDs, double temperature, double u, int* bestID = nullptr,
                           float* bestLogit = nullptr);
 
+    // New (inspection): the residual stream h after the embedding and after
+    // each layer of forwardBatch(tokenIDs, batch): (layers + 1) blocks of
+    // tokens x embedDim floats, layer by layer; empty on failure.
+    std::vector<float> forwardHidden(const std::vector<int>& tokenIDs, int batch = 1);
+    // New: the attention of head width 64 as one fused launch (gbx_attn_fused,
+    // the default) or as the per-head products (gbx_attn_scores, the score
+    // softmax, gbx_attn_values); the results differ only in rounding.
+    void setFusedAttention(bool on);
+    bool fusedAttention() const;
+
     bool isModelLoaded() const { return loader_.isLoaded(); }
     void printTensorNames() { loader_.printAllTensorNames(); }
     GGUFLoader& getLoader() { return loader_; }
@@ -179,7 +189,8 @@ private:
     std::string err_;
     bool fail(const std::string& msg);
     bool ensureBuffers(int64_t tokens, int seq);
-    bool runForward(const std::vector<int>& tokenIDs, int batch);   // logits stay on the device
+    // logits stay on the device; hidden_host (optional) receives forwardHidden's blocks
+    bool runForward(const std::vector<int>& tokenIDs, int batch, float* hidden_host = nullptr);
 };
 
 // Row sharding across GPUs with one host thread per device: a replica of

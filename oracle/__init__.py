@@ -214,6 +214,8 @@ def ref():
         R.ref_model_close.argtypes = [_vp]
         R.ref_model_forward.argtypes = [_vp, _vp, _c_int, _vp, _c_i64]
         R.ref_model_forward.restype = _c_i64
+        R.ref_model_forward_hidden.argtypes = [_vp, _vp, _c_int, _vp, _c_i64, _vp, _c_i64]
+        R.ref_model_forward_hidden.restype = _c_i64
         for name, args in (("ref_launch_embed", [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp]),
                            ("ref_launch_layernorm", [_vp, _vp, _vp, _vp, _c_int, _c_int, _vp]),
                            ("ref_launch_softmax", [_vp, _c_int, _c_int, _vp]),
@@ -279,6 +281,19 @@ class RefModel:
         if n < 0:
             raise ValueError("reference logits larger than expected")
         return out[:n].copy()
+
+    def forward_hidden(self, ids, layers: int, d: int):
+        """(hidden [layers + 1, n, d]: the residual stream after the embedding
+        and after each layer, logits of the last token), from the reference's
+        own forward steps."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        hidden = np.empty((layers + 1, ids.size, d), dtype=np.float32)
+        logits = np.empty(50257, dtype=np.float32)
+        n = ref().ref_model_forward_hidden(self.h, _ptr(ids), ids.size, _ptr(hidden), hidden.size, _ptr(logits),
+                                           logits.size)
+        if n != layers + 1:
+            raise ValueError(f"reference forward_hidden returned {n}")
+        return hidden, logits
 
     def close(self):
         if self.h:

@@ -18,7 +18,9 @@
 //   ref_launch_add        addResidualKernel (1 thread per element, block 256)
 //   ref_model_*           TransformerModel::loadModel / forward (transformer.cu:
 //                         913-949): the reference's whole GPU forward, for the
-//                         end-to-end parity test of the drop-in TransformerModel.
+//                         end-to-end parity test of the drop-in TransformerModel;
+//                         ref_model_forward_hidden runs the same steps and also
+//                         returns the residual stream after every layer.
 //                         forward is a private member there, so the reference's
 //                         source is compiled with `private` spelled `public`;
 //                         that changes access checking only, not code.
@@ -143,6 +145,33 @@ int64_t ref_model_forward(void* m, const int* ids, int n, float* logits, int64_t
     if ((int64_t)out.size() > cap) return -1;
     std::memcpy(logits, out.data(), out.size() * sizeof(float));
     return (int64_t)out.size();
+}
+
+// TransformerModel::forward (transformer.cu:913-927) step by step through the
+// reference's own member functions, in forward's order (embedTokens, then
+// attentionBlock and ffnBlock per layer, then computeLogits; only the progress
+// print is left out), copying its residual stream d_hidden to the host after
+// the embedding and after each layer: hidden receives (numLayers + 1) blocks
+// of n x embedDim floats, logits the last token's logits.  Returns the block
+// count, or -1 when a capacity is too small.
+int64_t ref_model_forward_hidden(void* mp, const int* ids, int n, float* hidden, int64_t cap, float* logits,
+                                 int64_t lcap)
+{
+    TransformerModel* m = static_cast<TransformerModel*>(mp);
+    const int64_t per = (int64_t)n * m->embedDim;
+    if (cap < per * (m->numLayers + 1) || lcap < m->vocabSize) return -1;
+    std::vector<int> v(ids, ids + n);
+    m->allocateBuffers(n);
+    m->embedTokens(v, n);
+    cudaMemcpy(hidden, m->d_hidden, per * sizeof(float), cudaMemcpyDeviceToHost);
+    for (int l = 0; l < m->numLayers; l++) {
+        m->attentionBlock(n, l);
+        m->ffnBlock(n, l);
+        cudaMemcpy(hidden + (l + 1) * per, m->d_hidden, per * sizeof(float), cudaMemcpyDeviceToHost);
+    }
+    std::vector<float> out = m->computeLogits(n);
+    std::memcpy(logits, out.data(), out.size() * sizeof(float));
+    return m->numLayers + 1;
 }
 
 }  // extern "C"

@@ -75,3 +75,44 @@ def assert_bits_equal(got, ref, what=""):
     bad = np.flatnonzero(got.ravel() != ref.ravel())
     assert bad.size == 0, (f"{what}: {bad.size} of {got.size} words differ; first at {bad[0]}: "
                            f"{got.ravel()[bad[0]]:08x} vs {ref.ravel()[bad[0]]:08x}")
+
+
+def assert_close_dev(got, ref, atol=1e-6, rtol=1e-5, what=""):
+    """assert_close for device tensors, evaluated on the device in float64
+    chunks (for outputs too large to copy to the host comfortably)."""
+    import torch
+    assert got.shape == ref.shape, (tuple(got.shape), tuple(ref.shape))
+    g, r = got.reshape(-1), ref.reshape(-1)
+    chunk = 1 << 26
+    bad_total, worst = 0, None
+    for s in range(0, g.numel(), chunk):
+        gc, rc = g[s:s + chunk].double(), r[s:s + chunk].double()
+        nan_r = torch.isnan(rc)
+        assert torch.equal(torch.isnan(gc), nan_r), f"{what}: NaN pattern differs"
+        inf_r = torch.isinf(rc)
+        assert torch.equal(gc[inf_r], rc[inf_r]), f"{what}: inf mismatch"
+        fin = ~(nan_r | inf_r)
+        err = torch.where(fin, (gc - rc).abs(), torch.zeros_like(gc))
+        tol = atol + rtol * rc.abs()
+        over = err > tol
+        n = int(over.sum().item())
+        if n:
+            i = int(torch.argmax(torch.where(fin, err - tol, torch.full_like(err, -1e300))).item())
+            worst = (gc[i].item(), rc[i].item(), err[i].item(), tol[i].item())
+            bad_total += n
+    assert bad_total == 0, (f"{what}: {bad_total} of {g.numel()} beyond tolerance; worst |{worst[0]} - {worst[1]}| "
+                            f"= {worst[2]:.3g} > {worst[3]:.3g}")
+
+
+def assert_bits_equal_dev(got, ref, what=""):
+    """Bit-for-bit equality of two fp32 device tensors."""
+    import torch
+    assert got.shape == ref.shape, (tuple(got.shape), tuple(ref.shape))
+    a = got.contiguous().view(torch.int32).reshape(-1)
+    b = ref.contiguous().view(torch.int32).reshape(-1)
+    ne = a != b
+    n = int(ne.sum().item())
+    if n:
+        i = int(torch.nonzero(ne)[0].item())
+        raise AssertionError(f"{what}: {n} of {a.numel()} words differ; first at {i}: "
+                             f"{a[i].item() & 0xffffffff:08x} vs {b[i].item() & 0xffffffff:08x}")

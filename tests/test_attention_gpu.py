@@ -277,6 +277,21 @@ def test_attn_fused_rejects_other_shapes(gbx, cuda):
             gbx.attn_fused(x, x, x, x, x, x, x[1024:], **args)
 
 
+def test_attn_fused_rejects_outputs_over_operands(gbx, cuda):
+    """An output written over the QKV block (in place) or over its own lo
+    plane is refused on the host: other CTAs would still read what one CTA's
+    stores overwrite."""
+    import torch
+    B, S, H, d = 1, 8, 2, 128
+    qkv = torch.zeros((B * S, 3 * d), dtype=torch.float32, device="cuda")
+    lo = torch.zeros_like(qkv)
+    out = torch.zeros((B * S, d), dtype=torch.float32, device="cuda")
+    args = dict(ld=3 * d, ld_out=d, B=B, S=S, H=H, hd=64, scale=8.0)
+    for o, o_lo in ((qkv, None), (qkv[:, d:], None), (out, lo), (out, out.view(-1)[4:]), (lo[:, 2 * d:], None)):
+        with pytest.raises(gbx.GbxError):
+            gbx.attn_fused(qkv, lo, qkv[:, d:], lo[:, d:], qkv[:, 2 * d:], lo[:, 2 * d:], o, out_lo=o_lo, **args)
+
+
 def test_attn_products_reject_bad_arguments(gbx, cuda):
     import torch
     x = torch.zeros(4096, dtype=torch.float32, device="cuda")
@@ -299,6 +314,7 @@ import importlib, sys
 import torch
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
 gbx = importlib.import_module("glassboxai-transformer_b200")
+gbx.linear_set_tiles(int(sys.argv[3]), int(sys.argv[4]))
 import test_attention_gpu as t
 for B, S, H, hd in ((2, 64, 3, 64), (1, 300, 2, 64), (3, 17, 2, 64), (1, 36, 2, 12), (1, 1024, 1, 64)):
     for causal in (True, False):
@@ -308,19 +324,20 @@ print("ok")
 """
 
 
-def _run_cases(env_extra):
+def _run_cases(k_block, pair_mode):
+    """The cases in a fresh process with the contractions' tile form set by
+    gbx_linear_set_tiles (k_block 16 / 32; pair_mode -1 auto, 0 never, 1 always)."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, **env_extra)
-    out = subprocess.run([sys.executable, "-c", _SUBPROCESS_CASES, root, os.path.join(root, "tests")], env=env,
-                         capture_output=True, text=True, timeout=600)
+    out = subprocess.run([sys.executable, "-c", _SUBPROCESS_CASES, root, os.path.join(root, "tests"), str(k_block),
+                          str(pair_mode)], capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stdout + out.stderr
 
 
 def test_attn_products_cta_pairs_forced(cuda):
     """The heads mode on CTA pairs for every shape (a 256-row pair tile over
     fewer rows than a head holds)."""
-    _run_cases({"GBX_LINEAR_PAIR": "1"})
+    _run_cases(16, 1)
 
 
 def test_attn_products_single_cta_forced(cuda):
-    _run_cases({"GBX_LINEAR_PAIR": "0"})
+    _run_cases(16, 0)

@@ -431,6 +431,7 @@ import importlib, sys
 import numpy as np, torch
 sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
 gbx = importlib.import_module("glassboxai-transformer_b200")
+gbx.linear_set_tiles(int(sys.argv[3]), int(sys.argv[4]))
 import test_linear_gpu as t
 for M, N, K, act, res in ((1, 8, 4, 0, 0), (37, 100, 20, 1, 0), (129, 257, 52, 0, 1), (300, 1600, 1600, 0, 1),
                           (257, 2304, 768, 0, 0), (64, 768, 3072, 1, 0), (520, 6400, 1600, 1, 0)):
@@ -454,11 +455,12 @@ print("ok")
 """
 
 
-def _run_cases(env_extra):
+def _run_cases(k_block, pair_mode):
+    """The cases in a fresh process with the contractions' tile form set by
+    gbx_linear_set_tiles (k_block 16 / 32; pair_mode -1 auto, 0 never, 1 always)."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, **env_extra)
-    out = subprocess.run([sys.executable, "-c", _SUBPROCESS_CASES, root, os.path.join(root, "tests")], env=env,
-                         capture_output=True, text=True, timeout=600)
+    out = subprocess.run([sys.executable, "-c", _SUBPROCESS_CASES, root, os.path.join(root, "tests"), str(k_block),
+                          str(pair_mode)], capture_output=True, text=True, timeout=600)
     assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stdout + out.stderr
 
 
@@ -466,12 +468,12 @@ def test_linear_cta_pairs_every_shape(cuda):
     """The CTA-pair kernel (two SMs per M 256 tile, cta_group::2) forced on
     for every shape, M = 1 included: tails in M (a whole second CTA of
     out-of-range rows), N and K, and each epilogue."""
-    _run_cases({"GBX_LINEAR_PAIR": "1"})
+    _run_cases(16, 1)
 
 
 def test_linear_cta_pairs_kblock_32(cuda):
-    _run_cases({"GBX_LINEAR_PAIR": "1", "GBX_LINEAR_BK": "32"})
+    _run_cases(32, 1)
 
 
 def test_linear_single_cta_kblock_32(cuda):
-    _run_cases({"GBX_LINEAR_PAIR": "0", "GBX_LINEAR_BK": "32"})
+    _run_cases(32, 0)

@@ -47,6 +47,8 @@ SIGNATURES = {
     "gbx_set_first_wait_limit": [ctypes.c_uint64],
     "gbx_dequant": [_vp, _int, _vp, _i64, _vp],
     "gbx_embed": [_vp, _vp, _int, _vp, _int, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, _vp],
+    "gbx_embed_layernorm": [_vp, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int,
+                            _int, _f, _vp, _vp],
     "gbx_layernorm": [_vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
     "gbx_layernorm_pair": [_vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
     "gbx_residual_layernorm": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _f, _vp],
@@ -147,6 +149,16 @@ def embed(ids, wte, wte_dtype, wpe, wpe_dtype, out, *, n_tok, d, vocab, n_ctx, s
     seq = n_tok if seq is None else seq
     _check(lib().gbx_embed(_p(ids), _p(wte), wte_dtype, _p(wpe), wpe_dtype, _p(pos_ids), _p(out), n_tok,
                            seq, pos_off, d, vocab, n_ctx, _p(err_flag), _stream(stream)))
+
+
+def embed_layernorm(ids, wte, wte_dtype, wpe, wpe_dtype, h_out, y, gamma, beta, *, n_tok, d, vocab, n_ctx, seq=None,
+                    pos_off=0, pos_ids=None, y_lo=None, eps=1e-5, err_flag=None, stream=None):
+    """embed (into h_out, may be None) and the LayerNorm of its rows (into y;
+    with y_lo, as a tf32 pair) in one pass."""
+    seq = n_tok if seq is None else seq
+    _check(lib().gbx_embed_layernorm(_p(ids), _p(wte), wte_dtype, _p(wpe), wpe_dtype, _p(pos_ids), _p(h_out), _p(y),
+                                     _p(y_lo), _p(gamma), _p(beta), n_tok, seq, pos_off, d, vocab, n_ctx, eps,
+                                     _p(err_flag), _stream(stream)))
 
 
 def layernorm(x, y, gamma, beta, *, rows, d, eps=1e-5, stream=None):

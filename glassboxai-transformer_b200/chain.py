@@ -12,8 +12,7 @@ output, ``ffn_pre``: ffn-up pre-activation, ``ffn_out``: ffn-down output,
 convention), and the hot path consumes them exactly as the reference's
 kernels would:
 
-  embed                                   -> h
-  layer 0:  LN1(h)                        -> ln        (layernorm)
+  embed; layer 0: LN1(h)                  -> h, ln     (embed_layernorm: one pass)
   layer l:  h += ffn_out(l-1); LN1(h)     -> ln        (residual_layernorm)
             softmax(scores)               -> probs     (softmax_rows, all heads, all sequences)
             h += attn_out; LN2(h)         -> ln        (residual_layernorm)
@@ -144,14 +143,13 @@ class Chain:
         s, G = self.s, _gbx
         N, d = B * s.seq, s.d
         ids = self.ids[first * s.seq:(first + B) * s.seq]
-        run("embed", B, lambda: G.embed(ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, self.h, n_tok=N,
-                                        d=d, vocab=s.vocab, n_ctx=s.n_ctx, seq=s.seq, pos_off=s.pos_off,
-                                        err_flag=self.err, stream=st))
+        # embed fused with layer 0's LayerNorm: h written once, never re-read
+        run("embed_layernorm", B, lambda: G.embed_layernorm(ids, self.wte, s.table_dtype, self.wpe, s.table_dtype,
+                                                            self.h, self.ln, self.g1[0], self.b1[0], n_tok=N, d=d,
+                                                            vocab=s.vocab, n_ctx=s.n_ctx, seq=s.seq,
+                                                            pos_off=s.pos_off, err_flag=self.err, stream=st))
         for l in range(s.layers):
-            if l == 0:
-                run("layernorm", B, lambda: G.layernorm(self.h, self.ln, self.g1[0], self.b1[0], rows=N, d=d,
-                                                        stream=st))
-            else:
+            if l > 0:
                 run("residual_layernorm", B,
                     lambda: G.residual_layernorm(self.ffn_out(l - 1), self.h, self.h, self.ln, self.g1[l],
                                                  self.b1[l], rows=N, d=d, stream=st))

@@ -5,9 +5,11 @@
 // Per forward of B sequences of S tokens (N = B*S rows, hidden d, H heads of
 // hd = d/H, feed-forward F, vocab V):
 //
-//   gbx_embed                              h = wte[ids] + wpe[pos]          (:805-815)
+//   gbx_embed_layernorm                    h = wte[ids] + wpe[pos]          (:805-815)
+//                                          and layer 0's ln = LN1(h) as a tf32 pair,
+//                                          one pass                        (:827-828)
 //   for each layer l:
-//     gbx_layernorm_pair                   ln = LN1(h), as a tf32 pair     (:827-828)
+//     gbx_layernorm_pair (l > 0)           ln = LN1(h), as a tf32 pair     (:827-828)
 //     gbx_linear                           qkv = ln . Wqkv^T + b_qkv, as a tf32 pair (:830-832)
 //     head width 64 (every GPT-2 size):
 //       gbx_attn_fused                     attn = softmax(mask(Q K^T / sqrt(hd))) V, every
@@ -28,8 +30,8 @@
 //     gbx_linear                           up = GELU(ln . Wup^T + b_up), as a tf32 pair
 //                                                                          (:870-872)
 //     gbx_linear                           h += up . Wdown^T + b_down      (:874-878)
-//   gbx_layernorm on each sequence's last row
-//                                          last = LN_f(h)                  (:890-896)
+//   gbx_final_layernorm                    last = LN_f(h) of each sequence's last row
+//                                                                          (:883-896)
 //   gbx_logits                             logits = last . wte^T           (:898-900)
 //   (nextToken) gbx_select_tokens          argmax / temperature sampling   (:994-1028)
 //
@@ -427,7 +429,10 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch, f
     if (cudaMemcpyAsync(m.ids, tokenIDs.data(), N * sizeof(int32_t), cudaMemcpyHostToDevice, st) != cudaSuccess ||
         cudaMemsetAsync(m.err, 0, sizeof(int32_t), st) != cudaSuccess)
         return fail("host-to-device copy of token ids failed");
-    check(gbx_embed(m.ids, m.wte, m.wte_dt, m.wpe, m.wpe_dt, nullptr, m.h.p, N, S, 0, d, V, nCtx_, m.err, gs));
+    // the embedding and layer 0's attention LayerNorm in one pass (h written once, not re-read)
+    check(gbx_embed_layernorm(m.ids, m.wte, m.wte_dt, m.wpe, m.wpe_dt, nullptr, m.h.p, m.ln.p, m.ln_lo.p,
+                              numLayers_ > 0 ? m.layers[0].ln1_g : nullptr, numLayers_ > 0 ? m.layers[0].ln1_b : nullptr,
+                              N, S, 0, d, V, nCtx_, 1e-5f, m.err, gs));
     // forwardHidden: the residual stream after the embedding and after each layer
     auto keep_hidden = [&](int slot) {
         if (hidden_host && rc == GBX_OK &&
@@ -441,7 +446,7 @@ bool TransformerModel::runForward(const std::vector<int>& tokenIDs, int batch, f
     for (int l = 0; l < numLayers_ && rc == GBX_OK; ++l) {
         const Impl::Layer& L = m.layers[l];
         const Impl::LayerW& W = m.wpairs[l];
-        check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
+        if (l > 0) check(gbx_layernorm_pair(m.h.p, m.ln.p, m.ln_lo.p, L.ln1_g, L.ln1_b, N, d, 1e-5f, gs));
         linear(m.ln.p, m.ln_lo.p, W.qkv, L.qkv_b, nullptr, m.qkv.p, m.qkv_lo.p, N, 3 * d, d, GBX_ACT_NONE);
         if (m.fused) {
             // attn = softmax(mask(Q K^T / sqrt(hd))) V for every head of every

@@ -90,6 +90,10 @@ class ChainShape:
         distinct_pos = min(self.seq, self.n_ctx)
         return 4 * t + t * self.d * self.table_es() + distinct_pos * self.d * self.table_es() + 4 * t * self.d
 
+    def bytes_embed_ln(self, seqs=None):
+        # the embedding's bytes + the LayerNorm output row and gamma / beta (h is not re-read)
+        return self.bytes_embed(seqs) + 4 * self._seqs(seqs) * self.seq * self.d + 8 * self.d
+
     def bytes_ln(self, seqs=None):
         return 8 * self._seqs(seqs) * self.seq * self.d + 8 * self.d
 
@@ -106,19 +110,21 @@ class ChainShape:
         return 16 * self._seqs(seqs) * self.d + 8 * self.d
 
     def bytes_of(self, kernel, seqs=None):
-        return {"embed": self.bytes_embed, "layernorm": self.bytes_ln, "residual_layernorm": self.bytes_residual_ln,
+        return {"embed": self.bytes_embed, "embed_layernorm": self.bytes_embed_ln, "layernorm": self.bytes_ln,
+                "residual_layernorm": self.bytes_residual_ln,
                 "softmax_rows": self.bytes_softmax, "bias_gelu": self.bytes_gelu,
                 "final_layernorm": self.bytes_final}[kernel](seqs)
 
     def launches_per_chunk(self):
-        # embed, LN, (layers-1) x residual+LN, layers x (softmax, residual+LN, bias+GELU), final LN
-        return 1 + 1 + 4 * self.layers - 1 + 1
+        # embed + LN (one fused launch), (layers-1) x residual+LN, layers x (softmax, residual+LN,
+        # bias+GELU), final LN
+        return 1 + 4 * self.layers - 1 + 1
 
     def launches_per_step(self):
         return self.n_chunks * self.launches_per_chunk()
 
     def bytes_per_pass(self, seqs=None):
-        return (self.bytes_embed(seqs) + self.bytes_ln(seqs) + (2 * self.layers - 1) * self.bytes_residual_ln(seqs)
+        return (self.bytes_embed_ln(seqs) + (2 * self.layers - 1) * self.bytes_residual_ln(seqs)
                 + self.layers * (self.bytes_softmax(seqs) + self.bytes_gelu(seqs)) + self.bytes_final(seqs))
 
     def bytes_per_chunk(self):

@@ -116,6 +116,26 @@ int gbx_embed(const int32_t* ids, const void* wte, int wte_dtype, const void* wp
               int vocab, int n_ctx, int32_t* err_flag, gbx_stream_t stream);
 
 /*
+ * Embedding fused with the first LayerNorm: gbx_embed followed by
+ * gbx_layernorm (or gbx_layernorm_pair when y_lo is given) in one pass,
+ * replacing embedTokensKernel (transformer.cu:175-185) and the layer-0
+ * layerNormKernel launch of attentionBlock (:828):
+ *   h = gbx_embed(ids, wte, wpe, ...)         into h_out (may be NULL: not stored)
+ *   y = LayerNorm(h) with gamma, beta, eps   (y_lo non-NULL: y, y_lo its tf32 pair)
+ * h is bit-identical to gbx_embed's, err_flag receives the same GBX_EMBED_*
+ * bits, and a rejected token's h row is zeros (its y row is then beta, as
+ * gbx_layernorm of a zero row).  y is within the LayerNorm tolerance of
+ * gbx_layernorm(h) (the row sums are taken in another order).  h is never
+ * re-read from memory.  Fused for wte_dtype == wpe_dtype, d a multiple of 4
+ * up to 16384 and 16-byte aligned rows; other cases run the two calls.
+ * h_out, y and y_lo must be distinct, non-overlapping [n_tok, d] buffers.
+ */
+int gbx_embed_layernorm(const int32_t* ids, const void* wte, int wte_dtype, const void* wpe, int wpe_dtype,
+                        const int32_t* pos_ids, float* h_out, float* y, float* y_lo, const float* gamma,
+                        const float* beta, int64_t n_tok, int seq, int pos_off, int d, int vocab, int n_ctx, float eps,
+                        int32_t* err_flag, gbx_stream_t stream);
+
+/*
  * LayerNorm over rows of length d, replacing layerNormKernel
  * (transformer.cu:77-124, launched at :828, :868, :896):
  *   mean = sum(x)/d; var = sum((x-mean)^2)/d; inv = rsqrtf(var + eps);

@@ -187,10 +187,11 @@ def test_forward_layers_match_reference_at_medium_shape(gm, orc, cuda, tmp_path)
     computeLogits, transformer.cu:805-927), and the logits.
 
     The embedding is bit-exact.  Each later layer's hidden state must agree
-    normwise: max |h - h_ref| <= 2e-5 * l * max |h_ref| after layer l (l from
-    1), i.e. the differences of summation order may grow at most linearly
-    with depth, at about 100 times fp32's unit roundoff per layer; the
-    largest observed ratio is reported on failure."""
+    normwise: max |h - h_ref| <= 1.5e-5 * max |h_ref| after every layer, about
+    250 times fp32's unit roundoff (2^-24) of the row's largest entry.  On
+    B200 the ratio measured 2.6e-6 to 3.6e-6 at every one of the 24 layers:
+    the summation-order differences do not grow with depth.  The ratios are
+    reported on failure."""
     orc = _ref_or_skip(orc)
     path = str(tmp_path / "medium.gguf")
     d, layers = 1024, 24
@@ -210,10 +211,9 @@ def test_forward_layers_match_reference_at_medium_shape(gm, orc, cuda, tmp_path)
         scale = float(np.abs(want_h[l]).max())
         err = float(np.abs(got_h[l].astype(np.float64) - want_h[l]).max())
         ratios.append(err / scale)
-    worst = max(range(layers), key=lambda i: ratios[i] / (2e-5 * (i + 1)))
-    assert all(r <= 2e-5 * (i + 1) for i, r in enumerate(ratios)), (
-        f"layer {worst + 1}: max|dh|/max|h| = {ratios[worst]:.3g} > {2e-5 * (worst + 1):.3g}; "
-        f"per layer: {[f'{r:.2g}' for r in ratios]}")
+    worst = max(range(layers), key=lambda i: ratios[i])
+    assert ratios[worst] <= 1.5e-5, (
+        f"layer {worst + 1}: max|dh|/max|h| = {ratios[worst]:.3g} > 1.5e-5; per layer: {[f'{r:.2g}' for r in ratios]}")
     err = np.abs(got_logits.astype(np.float64) - want_logits)
     assert np.all(err <= 1e-5 + 1e-3 * np.abs(want_logits)), f"logits: max abs err {err.max():.3g}"
     assert int(np.argmax(got_logits)) == int(np.argmax(want_logits))

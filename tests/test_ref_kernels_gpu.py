@@ -196,3 +196,30 @@ def test_embed_vs_reference_kernel(gbx, R, orc, cuda, cfg):
         return
     assert rc == 0
     assert_bits_equal_dev(got, ref, what=f"{name}: embed")
+
+
+@pytest.mark.parametrize("cfg", CONFIGS[:2], ids=IDS[:2])
+def test_embed_layernorm_vs_reference_kernels(gbx, R, orc, cuda, cfg):
+    """The fused embedding + first LayerNorm against the reference's
+    embedTokensKernel then layerNormKernel (transformer.cu:811-813, :828) on
+    one sequence (the widths the reference embed can launch): h bit-exact,
+    y within the LayerNorm tolerance."""
+    import torch
+    name, S, d, dtype = cfg[0], cfg[5], cfg[2], cfg[9]
+    V, C = 50257, max(S, 1024)
+    raw_te, raw_pe, dec_te, dec_pe = _tables(orc, V, C, d, dtype, seed=8)
+    ids = np.random.default_rng(9).integers(0, V, S).astype(np.int32)
+    g = _gen(10)
+    gam, bet = _ln_params(d, g)
+    t_ids = _dev(ids)
+    h_ref = torch.empty((S, d), device=cuda)
+    y_ref = torch.empty((S, d), device=cuda)
+    assert R.ref_launch_embed(t_ids.data_ptr(), _dev(dec_te).data_ptr(), _dev(dec_pe).data_ptr(), h_ref.data_ptr(), S,
+                              d, None) == 0
+    assert R.ref_launch_layernorm(h_ref.data_ptr(), y_ref.data_ptr(), gam.data_ptr(), bet.data_ptr(), S, d, None) == 0
+    h, y = torch.empty((S, d), device=cuda), torch.empty((S, d), device=cuda)
+    gbx.embed_layernorm(t_ids, _dev(raw_te), dtype, _dev(raw_pe), dtype, h, y, gam, bet, n_tok=S, d=d, vocab=V,
+                        n_ctx=C, seq=S)
+    torch.cuda.synchronize()
+    assert_bits_equal_dev(h, h_ref, what=f"{name}: fused embed h")
+    assert_close_dev(y, y_ref, what=f"{name}: fused embed + LayerNorm")

@@ -22,8 +22,17 @@
 
 namespace gbx {
 
+// Resident CTAs per SM the one-warp-per-token form is compiled for (its
+// register budget: 65536 / (256 x this)).  4 (64 registers, a few bytes of
+// spill) measured on B200 against the compiler's free choice (80 registers,
+// 3 CTAs): 49.5 vs 53.7 us at d 768 (f32 tables), 94.6 vs 96.0 us at d 1600
+// (bf16), equal at d 1024 (f16), 32,768 tokens each.
+#ifndef GBX_EMBED_LN_WARP_MIN_CTAS
+#define GBX_EMBED_LN_WARP_MIN_CTAS 4
+#endif
+
 template <int T, int TPR, int V4>
-__global__ void __launch_bounds__(RowCTA<TPR>::threads)
+__global__ void __launch_bounds__(RowCTA<TPR>::threads, TPR == 32 && V4 > 4 ? GBX_EMBED_LN_WARP_MIN_CTAS : 1)
 embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, const void* __restrict__ wpe,
                 const int32_t* __restrict__ pos_ids, float* __restrict__ h_out, float* __restrict__ y,
                 float* __restrict__ y_lo, const float* __restrict__ gamma, const float* __restrict__ beta,

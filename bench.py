@@ -19,10 +19,13 @@ default line also carries, measured in the same run:
   strong_1m      the 1,048,576-token workload split across the N ranks
                  (strong scaling), each rank's final rows copied to host
                  memory inside the timed region (the host gather)
+  medium         the GPT-2 medium prefill chain (8 x 1024 tokens, 24 layers)
   decode, small  the launch-bound GPT-2 XL decode step and GPT-2 small chain,
                  replayed as CUDA graphs
   model_forward  (N = 1) the drop-in TransformerModel forward end to end on a
                  random-init GPT-2 medium GGUF file
+  sharded_forward (N > 1) the same forward through gbx::ShardedModel, one
+                 host thread per GPU over the job's N GPUs, 8 sequences per GPU
   cpu_baseline   (N = 1) the reference's loops on the host cores
 
 ``--impl reference`` runs the reference's side only (rank 0; the product
@@ -438,6 +441,64 @@ def launch_bound(name, args, rank, world, device, stream, peak, peak_kind, pdl=T
     return res
 
 
+def chain_record(name, args, rank, world, device, stream, peak, peak_kind):
+    """Another configuration's chain, eager and uninstrumented like `value`
+    (weak: every rank runs the whole batch): tokens/s, ms per step and the
+    fraction of the measured copy rate."""
+    import torch
+    w = WORKLOADS[name]
+    shape = WL.ChainShape(**w.shape)
+    chain = _new_chain(shape, device, w.chain, seed=4000 + rank)
+    for _ in range(3):
+        chain.step(stream)
+    torch.cuda.synchronize(device)
+    assert int(chain.err.item()) == 0, "embed reported out-of-range ids"
+    steps = max(5, args.steps)
+    ms, clk = _timed_steps(lambda: chain.step(stream), steps, world, device, stream)
+    nbytes = shape.bytes_per_step()
+    res = {"workload": name, "description": w.description, "tokens_per_step": shape.tokens,
+           "tokens_per_s": shape.tokens / (ms * 1e-3) * world, "ms_per_step": ms, "steps": steps,
+           "launches_per_step": shape.launches_per_step(), "bytes_per_step": nbytes,
+           "hbm": {"gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / peak, "peak": peak,
+                   "peak_kind": peak_kind},
+           "clocks": clk, "l2": chain.l2_note()}
+    _free(chain)
+    return res
+
+
+def sharded_record(args, world):
+    """(rank 0, N > 1) the C++ multi-GPU runtime, gbx::ShardedModel, over the
+    job's N GPUs: a TransformerModel replica per GPU, one host thread per GPU,
+    8 sequences of 1024 tokens per GPU (GPT-2 medium, random-init f16 GGUF),
+    split into whole-sequence shards, logits gathered on the host: wall clock
+    per forwardBatch, ids from host memory in, logits to host memory out."""
+    import numpy as np
+    gm = importlib.import_module(PKG + ".model")
+    name = "gpt2-medium-prefill"
+    shape = WL.ChainShape(**WORKLOADS[name].shape)
+    path = bench_gguf(shape, name)
+    B = shape.batch * world
+    ids = np.random.default_rng(2).integers(0, shape.vocab, B * shape.seq).astype(np.int32)
+    sm = gm.ShardedModel(path, list(range(world)), vocab=shape.vocab)
+    try:
+        for _ in range(2):
+            sm.forward(ids, batch=B)
+        ts = []
+        for _ in range(max(3, min(args.steps, 10))):
+            t0 = time.perf_counter()
+            sm.forward(ids, batch=B)
+            ts.append(time.perf_counter() - t0)
+    finally:
+        sm.close()
+    sec = statistics.median(ts)
+    return {"workload": name, "api": "gbx::ShardedModel::forwardBatch (C ABI gbx_sharded_forward)",
+            "gpus": world, "sequences": B, "seq_len": shape.seq, "forward_ms": sec * 1e3,
+            "tokens_per_s": B * shape.seq / sec, "per_gpu_tokens_per_s": B * shape.seq / sec / world,
+            "steps": len(ts), "timing": "wall clock, median", "h2d_bytes_per_forward": int(ids.nbytes),
+            "d2h_bytes_per_forward": 4 * B * shape.vocab,
+            "note": "compare with model_forward of an N = 1 run: the same 8 sequences per GPU on one GPU"}
+
+
 def run_ours(args):
     import dataclasses
     import torch
@@ -544,6 +605,7 @@ def run_ours(args):
     del chain
     if args.workload == DEFAULT_WORKLOAD and not args.no_extras:
         result["strong_1m"] = strong_1m(args, rank, world, device, stream, peak, peak_kind)
+        result["medium"] = chain_record("gpt2-medium-prefill", args, rank, world, device, stream, peak, peak_kind)
         result["decode"] = launch_bound("gpt2-xl-decode", args, rank, world, device, stream, peak, peak_kind)
         result["small"] = launch_bound("gpt2-small-chain", args, rank, world, device, stream, peak, peak_kind)
         if world == 1:
@@ -554,6 +616,19 @@ def run_ours(args):
                                                             emit=False)
             except Exception as e:   # report, never lose the headline line
                 result["model_forward"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    if args.workload == DEFAULT_WORKLOAD and not args.no_extras and world > 1:
+        # every rank's GPU work is done; ranks other than 0 wait on the CPU
+        # (a gloo group: no NCCL kernel waits on a GPU that rank 0 now uses)
+        import datetime
+        import torch.distributed as dist
+        cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=600))
+        if rank == 0:
+            try:
+                result["sharded_forward"] = sharded_record(args, world)
+            except Exception as e:   # report, never lose the headline line
+                result["sharded_forward"] = {"unavailable": f"{type(e).__name__}: {e}"}
+        dist.barrier(group=cpu_group)
+        dist.destroy_process_group(cpu_group)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(WL.ChainShape(**w.shape))
     if rank == 0:
@@ -1064,7 +1139,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the strong_1m / decode / small / model_forward records of the default line")
+                    help="skip the strong_1m / medium / decode / small / model_forward records of the default line")
     ap.add_argument("--kernel", choices=["embed", "embed_layernorm", "layernorm", "residual_layernorm", "softmax_rows",
                                          "attn_softmax_rows", "bias_gelu"] + sorted(LINEAR_KERNELS) + ATTN_KERNELS,
                     help="time one kernel alone on --rows rows of the workload's shape")

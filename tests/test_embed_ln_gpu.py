@@ -132,3 +132,38 @@ def test_embed_layernorm_rejects_bad_arguments(gbx, cuda):
         gbx.embed_layernorm(ids, x, 2, x, 0, None, x, None, None, **kw)
     with pytest.raises(gbx.GbxError):        # positions past n_ctx
         gbx.embed_layernorm(ids, x, 0, x, 0, None, x, None, None, **dict(kw, seq=9, n_tok=9))
+
+
+@pytest.mark.parametrize("dt", [1, 30])
+@pytest.mark.parametrize("d,n_tok", [(1600, 703), (1024, 1029), (768, 1367), (2048, 515)])
+def test_embed_layernorm_large_launches(gbx, orc, cuda, dt, d, n_tok):
+    """Launches of more than 2^20 elements with 16-bit tables, one warp per
+    token: the token counts leave a ragged last CTA, rejected ids are mixed
+    in, and the tf32 pair output is exactly gbx_split_tf32 of the fp32 one."""
+    import torch
+    assert n_tok * d >= 1 << 20
+    seq = 512
+    V, C, wte, wpe, ids, g, b = _case(orc, dt, dt, d, n_tok, seq, 2, seed=3 * d + dt)
+    ids[5], ids[n_tok - 1] = V + 3, -1
+    fh, h = _guarded((n_tok, d), torch)
+    fy, y = _guarded((n_tok, d), torch)
+    flo, lo = _guarded((n_tok, d), torch)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = (_t(ids, torch), _t(wte, torch), dt, _t(wpe, torch), dt)
+    kw = dict(n_tok=n_tok, d=d, vocab=V, n_ctx=C, seq=seq, pos_off=2, err_flag=err)
+    gbx.embed_layernorm(*args, h, y, _t(g, torch), _t(b, torch), **kw)
+    h_ref, bad = orc.embed(ids, wte, dt, wpe, dt, d, V, C, seq=seq, pos_off=2)
+    assert bad == 2 and int(err.item()) == gbx.EMBED_BAD_ID
+    assert_bits_equal(h.cpu().numpy(), h_ref, f"embed_layernorm h dt={dt} d={d}")
+    y_ref = orc.layernorm(h_ref, g, b)
+    assert_close(y.cpu().numpy(), y_ref, what=f"embed_layernorm y dt={dt} d={d}")
+    # the tf32 pair output, without h: exactly gbx_split_tf32 of the fp32 output
+    fhi, hi = _guarded((n_tok, d), torch)
+    gbx.embed_layernorm(*args, None, hi, _t(g, torch), _t(b, torch), y_lo=lo, **kw)
+    shi, slo = torch.empty_like(h), torch.empty_like(h)
+    gbx.split_tf32(y, shi, slo, n=h.numel())
+    torch.cuda.synchronize()
+    assert_bits_equal(hi.cpu().numpy(), shi.cpu().numpy(), "pair hi")
+    assert_bits_equal(lo.cpu().numpy(), slo.cpu().numpy(), "pair lo")
+    for f in (fh, fy, flo, fhi):
+        _check_guards(f)

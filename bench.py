@@ -544,6 +544,22 @@ def run_ours(args):
         chain.step(stream, timers=timers)
     torch.cuda.synchronize(device)
     kernels = kernel_table(timers, peak, peak_kind)
+    # each kernel alone: 10 back-to-back launches on the chain's own buffers
+    # between one event pair (steady state, no neighbour's L2 write-back)
+    for name, k in kernels.items():
+        fn = chain.launch_of(name, stream)
+        for _ in range(2):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(10):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        us = 1000.0 * a.elapsed_time(b) / 10
+        nb = shape.bytes_of(name, shape.passes()[0][1])
+        k["alone_us"] = us
+        k["alone_frac_of_" + peak_kind] = nb / (us * 1e-6) / 1e9 / peak
 
     # --- end to end through the API with host buffers -----------------------------
     ids_host = chain.ids.cpu().pin_memory()
@@ -592,7 +608,8 @@ def run_ours(args):
                                        f"ncu summary profiles/{top}_{args.workload}.md (not measured in this run)"},
         "kernels": kernels,
         "kernel_timing": f"{k_steps} instrumented step(s) after the timed region (and one uncounted before them), "
-                         "CUDA events around every launch on the launching stream (the timed region itself has none)",
+                         "CUDA events around every launch on the launching stream (the timed region itself has none); "
+                         "alone_*: 10 back-to-back launches of the kernel on the chain's buffers between one event pair",
         "gpu_launches": shape.launches_per_step() * args.steps,
         "clocks": clocks,
         "e2e": {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s",

@@ -184,6 +184,32 @@ class Chain:
             self._pass(first, n, st, run)
         return self.out
 
+    def launch_of(self, name, stream=None):
+        """A zero-argument callable issuing one launch of kernel `name` with the
+        chain's own buffers and the first pass's sizes (layer 0's inputs): for
+        timing one kernel back to back outside the chain's order."""
+        import torch
+        s, G = self.s, _gbx
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        B = s.passes()[0][1]
+        N, d = B * s.seq, s.d
+        ids = self.ids[:N]
+        fns = {
+            "embed_layernorm": lambda: G.embed_layernorm(ids, self.wte, s.table_dtype, self.wpe, s.table_dtype, self.h,
+                                                         self.ln, self.g1[0], self.b1[0], n_tok=N, d=d, vocab=s.vocab,
+                                                         n_ctx=s.n_ctx, seq=s.seq, pos_off=s.pos_off,
+                                                         err_flag=self.err, stream=st),
+            "residual_layernorm": lambda: G.residual_layernorm(self.attn_out(0), self.h, self.h, self.ln, self.g2[0],
+                                                               self.b2[0], rows=N, d=d, stream=st),
+            "softmax_rows": lambda: G.softmax_rows(self.scores(0), self.probs, rows=s.softmax_rows_of(B), L=s.L,
+                                                   stream=st),
+            "bias_gelu": lambda: G.bias_gelu(self.ffn_pre(0), self.ffn_act, self.up_bias[0], rows=N, F=s.ff,
+                                             stream=st),
+            "final_layernorm": lambda: G.final_layernorm(self.ffn_out(0), self.h, self.out[:B], self.gf, self.bf,
+                                                         n_seq=B, seq=s.seq, d=d, stream=st),
+        }
+        return fns[name]
+
     def capture_graph(self, timers=None):
         """Record one step into a CUDA graph (launches on the capture stream).
         With ``timers``, the graph also records an event pair around every

@@ -116,3 +116,26 @@ def test_reference_arm_does_not_load_the_product_library():
     assert line["ms_per_step"] * line["steps"] < 60e3
     assert not loaded["pkg"]
     assert not any(p.endswith("/libgbx.so") or p.endswith("/libgbx_model.so") for p in loaded["so"]), loaded["so"]
+
+
+def test_launch_of_uses_the_first_pass_sizes(monkeypatch):
+    """Chain.launch_of (the bench's back-to-back timing of one kernel) issues
+    the kernel on the chain's own buffers with the first pass's sizes."""
+    import torch
+    chain_mod = importlib.import_module("glassboxai-transformer_b200.chain")
+    s = chain_mod.ChainShape(batch=5, seq=4, d=8, ff=16, heads=2, layers=2, vocab=50, n_ctx=8, table_dtype=0, chunk=2)
+    c = chain_mod.Chain(s, torch.device("cpu"), seed=0)
+    rec = _Recorder()
+    monkeypatch.setattr(chain_mod, "_gbx", rec)
+    names = ["embed_layernorm", "residual_layernorm", "softmax_rows", "bias_gelu", "final_layernorm"]
+    for n in names:
+        c.launch_of(n, stream="st")()
+    assert [name for name, _, _ in rec.calls] == names
+    kw = {name: k for name, _, k in rec.calls}
+    assert kw["embed_layernorm"]["n_tok"] == 2 * s.seq
+    assert kw["residual_layernorm"]["rows"] == 2 * s.seq
+    assert kw["softmax_rows"]["rows"] == 2 * s.heads * s.seq
+    assert kw["bias_gelu"]["rows"] == 2 * s.seq
+    assert kw["final_layernorm"]["n_seq"] == 2
+    with pytest.raises(KeyError):
+        c.launch_of("nothing", stream="st")

@@ -53,13 +53,19 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
                     ((uint32_t)pos >= (uint32_t)n_ctx ? GBX_EMBED_BAD_POS : 0);
     const bool live = valid && !bad;
 
-    typename Raw4<T>::type a[V4], b[V4];
+    // Every lane walks its row through base pointers with compile-time
+    // offsets (k * TPR units), and "float4 k * TPR + lane exists" is one
+    // compare against lim: the loops below carry no per-element index math.
+    using R = typename Raw4<T>::type;
+    const int lim = n4 - lane;
+    const R* const wrow = reinterpret_cast<const R*>(wte) + (int64_t)(live ? id : 0) * n4 + lane;
+    const R* const prow = reinterpret_cast<const R*>(wpe) + (int64_t)(live ? pos : 0) * n4 + lane;
+    R a[V4], b[V4];
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
-        const int c = k * TPR + lane;
-        if (live && c < n4) {
-            a[k] = load_raw4<T>(wte, (int64_t)id * d + 4 * c);
-            b[k] = load_raw4<T>(wpe, (int64_t)pos * d + 4 * c);
+        if (live && k * TPR < lim) {
+            a[k] = __ldg(wrow + k * TPR);
+            b[k] = __ldg(prow + k * TPR);
         } else {
             a[k] = zero_raw4<T>();
             b[k] = zero_raw4<T>();
@@ -79,8 +85,12 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
         if constexpr (T == TF16)
             o = make_float4(__fadd_rn(o.x, 0.0f), __fadd_rn(o.y, 0.0f), __fadd_rn(o.z, 0.0f), __fadd_rn(o.w, 0.0f));
         v[k] = o;
-        const int c = k * TPR + lane;
-        if (h_out && valid && c < n4) st_stream(h_out + off + 4 * c, o);
+    }
+    if (h_out && valid) {
+        float* const hrow = h_out + off + 4 * lane;
+#pragma unroll
+        for (int k = 0; k < V4; ++k)
+            if (k * TPR < lim) st_stream(hrow + 4 * k * TPR, v[k]);
     }
 
     // LayerNorm of h, the arithmetic of ln_vec_kernel (layernorm.cu)
@@ -93,7 +103,7 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
     float qs = 0.0f;
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
-        if (k * TPR + lane < n4) {
+        if (k * TPR < lim) {
             const float e0 = v[k].x - mean, e1 = v[k].y - mean, e2 = v[k].z - mean, e3 = v[k].w - mean;
             qs = fmaf(e0, e0, qs);
             qs = fmaf(e1, e1, qs);
@@ -104,10 +114,29 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
     qs = row_sum<TPR>(qs, red[1]);
     const float inv = rsqrtf(qs / fd + eps);
     if (!valid) return;
+    float* const yrow = y + off + 4 * lane;
+    if (gamma && beta && !y_lo) {
+        // the common case, with no per-element pointer tests
+        const float* const grow = gamma + 4 * lane;
+        const float* const brow = beta + 4 * lane;
+#pragma unroll
+        for (int k = 0; k < V4; ++k) {
+            if (k * TPR < lim) {
+                const float4 g = ld_param4(grow + 4 * k * TPR), bb = ld_param4(brow + 4 * k * TPR);
+                float4 o;
+                o.x = fmaf((v[k].x - mean) * inv, g.x, bb.x);
+                o.y = fmaf((v[k].y - mean) * inv, g.y, bb.y);
+                o.z = fmaf((v[k].z - mean) * inv, g.z, bb.z);
+                o.w = fmaf((v[k].w - mean) * inv, g.w, bb.w);
+                st_stream(yrow + 4 * k * TPR, o);
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
         const int c = k * TPR + lane;
-        if (c < n4) {
+        if (k * TPR < lim) {
             const float4 g = gamma ? ld_param4(gamma + 4 * c) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
             const float4 bb = beta ? ld_param4(beta + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             float4 o;
@@ -118,10 +147,10 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
             if (y_lo) {
                 float4 hi, lo;
                 split4(o, hi, lo);
-                st_stream(y + off + 4 * c, hi);
+                st_stream(yrow + 4 * k * TPR, hi);
                 st_stream(y_lo + off + 4 * c, lo);
             } else {
-                st_stream(y + off + 4 * c, o);
+                st_stream(yrow + 4 * k * TPR, o);
             }
         }
     }

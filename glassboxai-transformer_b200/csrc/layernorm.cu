@@ -41,25 +41,34 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
     const int64_t off = row * d;       // y, y_lo
     const float fd = (float)d;
 
+    // Per-lane base pointers with compile-time offsets (k * TPR float4s), and
+    // "float4 k * TPR + lane exists" as one compare against lim: no
+    // per-element index math or pointer tests inside the unrolled loops.
+    const int lim = n4 - lane;
+    const float* const xrow = x + in_off + 4 * lane;
     float4 v[V4];
 #pragma unroll
-    for (int k = 0; k < V4; ++k) {
-        const int c = k * TPR + lane;
-        v[k] = (valid && c < n4) ? ld_stream(x + in_off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int k = 0; k < V4; ++k)
+        v[k] = (valid && k * TPR < lim) ? ld_stream(xrow + 4 * k * TPR) : make_float4(0.f, 0.f, 0.f, 0.f);
     if constexpr (RESID) {
+        const float* const rrow = r + in_off + 4 * lane;
         float4 rv[V4];
 #pragma unroll
-        for (int k = 0; k < V4; ++k) {
-            const int c = k * TPR + lane;
-            rv[k] = (valid && c < n4) ? ld_stream(r + in_off + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < V4; ++k)
+            rv[k] = (valid && k * TPR < lim) ? ld_stream(rrow + 4 * k * TPR) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (xbias) {
+            const float* const brow = xbias + 4 * lane;
+#pragma unroll
+            for (int k = 0; k < V4; ++k)
+                if (k * TPR < lim) v[k] = f4add(v[k], ld_param4(brow + 4 * k * TPR));
         }
 #pragma unroll
-        for (int k = 0; k < V4; ++k) {
-            const int c = k * TPR + lane;
-            if (xbias && c < n4) v[k] = f4add(v[k], ld_param4(xbias + 4 * c));
-            v[k] = f4add(rv[k], v[k]);
-            if (h_out && valid && c < n4) st_stream(h_out + in_off + 4 * c, v[k]);
+        for (int k = 0; k < V4; ++k) v[k] = f4add(rv[k], v[k]);
+        if (h_out && valid) {
+            float* const hrow = h_out + in_off + 4 * lane;
+#pragma unroll
+            for (int k = 0; k < V4; ++k)
+                if (k * TPR < lim) st_stream(hrow + 4 * k * TPR, v[k]);
         }
     }
 
@@ -72,7 +81,7 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
     float q = 0.0f;
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
-        if (k * TPR + lane < n4) {
+        if (k * TPR < lim) {
             const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, e = v[k].w - mean;
             q = fmaf(a, a, q);
             q = fmaf(b, b, q);
@@ -83,26 +92,44 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
     q = row_sum<TPR>(q, red[1]);
     const float inv = rsqrtf(q / fd + eps);
 
-    if (valid) {
+    if (!valid) return;
+    float* const yrow = y + off + 4 * lane;
+    if (gamma && beta && !y_lo) {
+        // the common case, with no per-element pointer tests
+        const float* const grow = gamma + 4 * lane;
+        const float* const brow = beta + 4 * lane;
 #pragma unroll
         for (int k = 0; k < V4; ++k) {
-            const int c = k * TPR + lane;
-            if (c < n4) {
-                const float4 g = gamma ? ld_param4(gamma + 4 * c) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-                const float4 b = beta ? ld_param4(beta + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (k * TPR < lim) {
+                const float4 g = ld_param4(grow + 4 * k * TPR), b = ld_param4(brow + 4 * k * TPR);
                 float4 o;
                 o.x = fmaf((v[k].x - mean) * inv, g.x, b.x);
                 o.y = fmaf((v[k].y - mean) * inv, g.y, b.y);
                 o.z = fmaf((v[k].z - mean) * inv, g.z, b.z);
                 o.w = fmaf((v[k].w - mean) * inv, g.w, b.w);
-                if (y_lo) {
-                    float4 hi, lo;
-                    split4(o, hi, lo);
-                    st_stream(y + off + 4 * c, hi);
-                    st_stream(y_lo + off + 4 * c, lo);
-                } else {
-                    st_stream(y + off + 4 * c, o);
-                }
+                st_stream(yrow + 4 * k * TPR, o);
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        const int c = k * TPR + lane;
+        if (k * TPR < lim) {
+            const float4 g = gamma ? ld_param4(gamma + 4 * c) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+            const float4 b = beta ? ld_param4(beta + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float4 o;
+            o.x = fmaf((v[k].x - mean) * inv, g.x, b.x);
+            o.y = fmaf((v[k].y - mean) * inv, g.y, b.y);
+            o.z = fmaf((v[k].z - mean) * inv, g.z, b.z);
+            o.w = fmaf((v[k].w - mean) * inv, g.w, b.w);
+            if (y_lo) {
+                float4 hi, lo;
+                split4(o, hi, lo);
+                st_stream(yrow + 4 * k * TPR, hi);
+                st_stream(y_lo + off + 4 * c, lo);
+            } else {
+                st_stream(yrow + 4 * k * TPR, o);
             }
         }
     }

@@ -611,3 +611,45 @@ def test_embed_negative_zero_sums(gbx, orc, cuda, wdt, pdt, want_bits):
     got = out.cpu().numpy()
     assert_bits_equal(got, ref, f"-0 sums {wdt}/{pdt}")
     assert np.all(got.view(np.uint32) == want_bits)
+
+
+# ---------------------------------------------------------------------------
+# final LayerNorm of each sequence's last row
+
+@pytest.mark.parametrize("n_seq,seq,d", [(1, 1, 768), (1, 64, 768), (32, 1024, 1600), (7, 33, 1028), (3, 5, 12),
+                                         (256, 1, 1600), (5, 17, 4096)])
+@pytest.mark.parametrize("with_x", [True, False])
+def test_final_layernorm_last_rows(gbx, orc, cuda, n_seq, seq, d, with_x):
+    """y[b] = LayerNorm(r[t] + x[t]) for t = b*seq + seq - 1 (the reference's
+    last-row copy + layerNormKernel of computeLogits, transformer.cu:883-896,
+    with the last ffnDownKernel's residual add, :292), or of r[t] alone.
+    Every row but the last of each sequence holds NaN: none of them may be
+    read."""
+    import torch
+    rng = np.random.default_rng(n_seq * 1000 + seq + d)
+    x = np.full((n_seq * seq, d), np.nan, np.float32)
+    r = np.full((n_seq * seq, d), np.nan, np.float32)
+    last = np.arange(n_seq) * seq + seq - 1
+    x[last] = rng.standard_normal((n_seq, d)).astype(np.float32)
+    r[last] = rng.standard_normal((n_seq, d)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.02 * rng.standard_normal(d)).astype(np.float32)
+    full, y = _guarded((n_seq, d), torch)
+    gbx.final_layernorm(_t(x, torch) if with_x else None, _t(r, torch), y, _t(g, torch), _t(b, torch), n_seq=n_seq,
+                        seq=seq, d=d)
+    if with_x:
+        ref = orc.residual_layernorm(x[last], r[last], g, b)[1]
+    else:
+        ref = orc.layernorm(r[last], g, b)
+    assert_close(y.cpu().numpy(), ref, what=f"final LN n_seq={n_seq} seq={seq} d={d}")
+    _check_guards(full)
+
+
+def test_final_layernorm_rejects_overlap(gbx, cuda):
+    import torch
+    buf = torch.zeros((4 * 8, 64), device="cuda")
+    g = torch.ones(64, device="cuda")
+    with pytest.raises(gbx.GbxError):   # y over the strided input rows
+        gbx.final_layernorm(None, buf, buf[4:8], g, g, n_seq=4, seq=8, d=64)
+    with pytest.raises(gbx.GbxError):
+        gbx.final_layernorm(None, buf, buf[:1], g, g, n_seq=4, seq=0, d=64)

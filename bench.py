@@ -392,7 +392,7 @@ def strong_1m(args, rank, world, device, stream, peak, peak_kind):
     ms_local_mhz = clk.get("sm_mhz")
     mhz = gather_over_ranks(ms_local_mhz, world, device)
     bytes_rank = shape.bytes_per_step()
-    res = {"workload": "tokens-1m-sharded", "description": w.description, "scaling": "strong",
+    res = {"workload": "tokens-1m-sharded", "scaling": "strong",
            "tokens": full.tokens, "n_gpus": world, "sequences_per_gpu": count, "passes_per_gpu": shape.n_chunks,
            "steps": steps, "warmup": 3, "ms_per_step": ms, "tokens_per_s": full.tokens / (ms * 1e-3),
            "tokens_per_s_per_gpu": full.tokens / (ms * 1e-3) / world,
@@ -400,8 +400,7 @@ def strong_1m(args, rank, world, device, stream, peak, peak_kind):
                    "frac": bytes_rank / (ms * 1e-3) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},
            "clocks": clk, "sm_mhz_median_per_rank": mhz,
            "ms_x_sm_mhz": ms * statistics.median([m for m in mhz if m]) if any(mhz) else None,
-           "host_gather": f"each rank copies its [{count}, {full.d}] final LayerNorm rows to pinned host memory in "
-                          "the timed region (the only exchange; no collective on the data path)",
+           "host_gather": f"[{count}, {full.d}] final rows per rank to pinned host memory, in the timed region",
            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": int(host.numel() * 4)}
     _free(chain)
     return res
@@ -431,12 +430,11 @@ def launch_bound(name, args, rank, world, device, stream, peak, peak_kind, pdl=T
         G.set_pdl(prev)
     nbytes = shape.bytes_per_step()
     floor_us = nbytes / (peak * 1e9) * 1e6
-    res = {"workload": name, "description": w.description, "tokens_per_step": shape.tokens,
+    res = {"workload": name, "tokens_per_step": shape.tokens,
            "tokens_per_s": shape.tokens / (ms * 1e-3) * world, "us_per_step": ms * 1e3,
            "launches_per_step": shape.launches_per_step(), "bytes_per_step": nbytes,
            "byte_floor_us": floor_us, "frac_of_floor": floor_us / (ms * 1e3), "steps": steps,
-           "cuda_graph": True, "programmatic_dependent_launch": pdl, "clocks": clk,
-           "l2": chain.l2_note()}
+           "cuda_graph": True, "programmatic_dependent_launch": pdl, "clocks": clk}
     _free(chain)
     return res
 
@@ -456,12 +454,12 @@ def chain_record(name, args, rank, world, device, stream, peak, peak_kind):
     steps = max(5, args.steps)
     ms, clk = _timed_steps(lambda: chain.step(stream), steps, world, device, stream)
     nbytes = shape.bytes_per_step()
-    res = {"workload": name, "description": w.description, "tokens_per_step": shape.tokens,
+    res = {"workload": name, "tokens_per_step": shape.tokens,
            "tokens_per_s": shape.tokens / (ms * 1e-3) * world, "ms_per_step": ms, "steps": steps,
            "launches_per_step": shape.launches_per_step(), "bytes_per_step": nbytes,
            "hbm": {"gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / peak, "peak": peak,
                    "peak_kind": peak_kind},
-           "clocks": clk, "l2": chain.l2_note()}
+           "clocks": clk}
     _free(chain)
     return res
 
@@ -1114,7 +1112,7 @@ def run_model_forward(args, shape, workload, desc, impl, emit=True):
             ts.append(time.perf_counter() - t0)
         return statistics.median(ts)
 
-    out = {"mode": "model-forward", "impl": impl, "workload": workload, "description": desc,
+    out = {"mode": "model-forward", "impl": impl, "workload": workload, **({"description": desc} if emit else {}),
            "weights": {0: "f32", 1: "f16", 30: "bf16"}[shape.table_dtype],
            "data": "synthetic (random-init weights in a GGUF file, seeded token ids)", "warmup": args.warmup,
            "steps": args.steps}

@@ -4,7 +4,9 @@
 // installed headers and libraries:
 //   api_check loader <file.gguf> <tensor>   -> config, hasTensor, getTensor checksum
 //   api_check model  <file.gguf> <id...>    -> forward logits checksum, argmax,
-//                                              nextToken at T=0 and T=0.8 (mt19937 seed 1234)
+//                                              nextToken at T=0 and T=0.8 (mt19937 seed 1234),
+//                                              forwardHidden (block count, last block's checksum),
+//                                              the argmax with the per-head attention products
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -63,5 +65,22 @@ int main(int argc, char** argv)
     const int greedy = model.nextToken(ids, 0.0, rng, &b0, &l0);
     const int sampled = model.nextToken(ids, 0.8, rng, &b1, &l1);
     std::printf("next %d %d %d %d\n", greedy, b0, sampled, b1);
-    return greedy < 0 || sampled < 0 ? 1 : 0;
+    // inspection: the residual stream after the embedding and after every layer
+    const std::vector<float> hidden = model.forwardHidden(ids);
+    const size_t block = ids.size() * (size_t)model.getEmbedDim();
+    if (hidden.size() != (size_t)(model.getNumLayers() + 1) * block) {
+        std::printf("error forwardHidden returned %zu floats\n", hidden.size());
+        return 1;
+    }
+    const std::vector<float> last(hidden.end() - block, hidden.end());
+    std::printf("hidden %d %.17g\n", model.getNumLayers() + 1, checksum(last));
+    // the same forward on the per-head attention products
+    model.setFusedAttention(false);
+    const std::vector<float> unfused = model.forward(ids);
+    model.setFusedAttention(true);
+    int ubest = 0;
+    for (size_t j = 1; j < unfused.size(); ++j)
+        if (unfused[j] > unfused[ubest]) ubest = (int)j;
+    std::printf("unfused %zu %d %d\n", unfused.size(), ubest, (int)model.fusedAttention());
+    return greedy < 0 || sampled < 0 || unfused.empty() ? 1 : 0;
 }

@@ -69,6 +69,17 @@ def test_cpp_model_matches_c_abi(api_check, cuda, tmp_path):
     orc = importlib.import_module("oracle")
     want, _, _ = orc.select_tokens(logits[None, :], 0.8, [draw])
     assert sampled == int(want[0])
+    # forwardHidden and setFusedAttention from C++ agree with the C ABI binding
+    m = gm.Model(path)
+    hidden = m.forward_hidden(np.array(ids, np.int32))
+    assert int(out["hidden"][0]) == hidden.shape[0] == m.config["num_layers"] + 1
+    assert float(out["hidden"][1]) == pytest.approx(_checksum(hidden[-1].ravel()), rel=1e-9)
+    m.set_fused_attention(False)
+    unfused = m.forward(np.array(ids, np.int32))
+    m.close()
+    assert int(out["unfused"][0]) == unfused.size
+    assert int(out["unfused"][1]) == int(np.argmax(unfused)) == int(np.argmax(logits))
+    assert out["unfused"][2] == "1"          # the setting was restored
 
 
 def _mt19937_uniform(seed):

@@ -383,18 +383,24 @@ def strong_1m(args, rank, world, device, stream, peak, peak_kind):
         chain.step(stream)
         host.copy_(chain.out, non_blocking=True)
 
-    for _ in range(3):
+    # warm-up and timed steps scale with the rank count, so that every N times
+    # about the same wall-clock window (about 1.2 s): a shorter window at
+    # large N would run above the clock the power cap settles to, and the
+    # ratio between N would measure the clock, not the scaling
+    warm = 3 * world
+    for _ in range(warm):
         step()
     torch.cuda.synchronize(device)
     assert int(chain.err.item()) == 0, "embed reported out-of-range ids"
-    steps = max(3, min(args.steps, 10))
+    steps = max(3, min(args.steps, 10)) * world
     ms, clk = _timed_steps(step, steps, world, device, stream)
     ms_local_mhz = clk.get("sm_mhz")
     mhz = gather_over_ranks(ms_local_mhz, world, device)
     bytes_rank = shape.bytes_per_step()
     res = {"workload": "tokens-1m-sharded", "scaling": "strong",
            "tokens": full.tokens, "n_gpus": world, "sequences_per_gpu": count, "passes_per_gpu": shape.n_chunks,
-           "steps": steps, "warmup": 3, "ms_per_step": ms, "tokens_per_s": full.tokens / (ms * 1e-3),
+           "steps": steps, "warmup": warm, "timed_s": ms * steps * 1e-3, "ms_per_step": ms,
+           "tokens_per_s": full.tokens / (ms * 1e-3),
            "tokens_per_s_per_gpu": full.tokens / (ms * 1e-3) / world,
            "hbm": {"bytes_per_step_per_gpu": bytes_rank, "gbs_per_gpu": bytes_rank / (ms * 1e-3) / 1e9,
                    "frac": bytes_rank / (ms * 1e-3) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},

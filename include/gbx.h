@@ -9,7 +9,10 @@
  *     `_host`.  Callers own every buffer; nothing here allocates per call.
  *   - Work is enqueued asynchronously on `stream` (NULL = the legacy default
  *     stream, which is what the reference uses).  Entry points are stateless
- *     and safe to call from several host threads at once.
+ *     and safe to call from several host threads at once.  Three process-wide
+ *     settings exist, none needed for correct results: gbx_set_pdl,
+ *     gbx_linear_set_tiles and (for tests) gbx_set_first_wait_limit; change
+ *     them while no other host thread is launching.
  *   - Return GBX_OK (0) or a GBX_E* code; they never exit the process
  *     (the reference's CUDA_CHECK prints and calls exit(1),
  *     transformer.cu:24-32).  gbx_last_error() gives a one-line reason,

@@ -24,8 +24,21 @@ __device__ __forceinline__ float4 f4add(float4 a, float4 b)
 
 // y_lo non-null: y and y_lo receive the tf32 pair of the output (tf32.cuh)
 // instead of the fp32 output, for gbx_linear.
+// Resident CTAs per SM the row kernels are compiled for (a register budget of
+// 65536 / (CTA threads x this)); 1 leaves the compiler free.  Measured on
+// B200 (32,768 rows of 1600): the LayerNorm at 6 (40 registers) 70.1 us
+// against 80.2 us free (48 registers, 5 CTAs); residual + LayerNorm best free
+// (50 registers): capped at 6 it spills and takes 130 against 127.5 us.
+#ifndef GBX_LN_MIN_CTAS
+#define GBX_LN_MIN_CTAS 6
+#endif
+#ifndef GBX_RLN_MIN_CTAS
+#define GBX_RLN_MIN_CTAS 1
+#endif
+
 template <int TPR, int V4, bool RESID>
-__global__ void __launch_bounds__(RowCTA<TPR>::threads)
+__global__ void __launch_bounds__(RowCTA<TPR>::threads, RowCTA<TPR>::threads > 256 ? 1
+                                                        : (RESID ? GBX_RLN_MIN_CTAS : GBX_LN_MIN_CTAS))
 ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, float* h_out, float* y, float* y_lo,
               const float* __restrict__ gamma, const float* __restrict__ beta, int64_t rows, int d, int64_t ld,
               float eps)

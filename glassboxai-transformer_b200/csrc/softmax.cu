@@ -51,10 +51,18 @@ struct ScoreEpilogue {
 // round_up(p + 1, 256) are written: the rest are zero, and the
 // contraction, whose row tiles are 128 or 256 rows high, never reads them.
 // (PAIR_OUT held to 8 resident CTAs of 256 threads, 32 registers: 6%
-// faster on B200 than its unbounded 48 registers, a few bytes spilled)
+// faster on B200 than its unbounded 48 registers, a few bytes spilled.
+// The attention form without the pair, in CTAs of 256 threads, compiled for
+// GBX_ATTN_SM_MIN_CTAS resident CTAs:
+// at 6 (40 registers, no spill) 1032 us for 819,200 causal rows of 1024,
+// against 1137 us unbounded (47 registers, 5 CTAs) and 1033 us at 8.)
+#ifndef GBX_ATTN_SM_MIN_CTAS
+#define GBX_ATTN_SM_MIN_CTAS 6
+#endif
 template <int TPR, int V4, bool ATTN, bool POW2, bool PAIR_OUT>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads,
-                                  PAIR_OUT ? (2048 / RowCTA<TPR>::threads < 8 ? 2048 / RowCTA<TPR>::threads : 8) : 1)
+                                  PAIR_OUT ? (2048 / RowCTA<TPR>::threads < 8 ? 2048 / RowCTA<TPR>::threads : 8)
+                                  : (ATTN && RowCTA<TPR>::threads <= 256) ? GBX_ATTN_SM_MIN_CTAS : 1)
 softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep)
 {
     grid_dependency_wait();   // see launch_row_kernel

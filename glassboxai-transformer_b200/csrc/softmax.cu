@@ -55,14 +55,19 @@ struct ScoreEpilogue {
 // The attention form without the pair, in CTAs of 256 threads, compiled for
 // GBX_ATTN_SM_MIN_CTAS resident CTAs:
 // at 6 (40 registers, no spill) 1032 us for 819,200 causal rows of 1024,
-// against 1137 us unbounded (47 registers, 5 CTAs) and 1033 us at 8.)
+// against 1137 us unbounded (47 registers, 5 CTAs) and 1033 us at 8.  The
+// plain softmax is best left free, GBX_SM_MIN_CTAS 1 (40 registers, 6 CTAs):
+// 962 us against 968 us at 8 CTAs (32 registers) on the same rows.)
 #ifndef GBX_ATTN_SM_MIN_CTAS
 #define GBX_ATTN_SM_MIN_CTAS 6
+#endif
+#ifndef GBX_SM_MIN_CTAS
+#define GBX_SM_MIN_CTAS 1
 #endif
 template <int TPR, int V4, bool ATTN, bool POW2, bool PAIR_OUT>
 __global__ void __launch_bounds__(RowCTA<TPR>::threads,
                                   PAIR_OUT ? (2048 / RowCTA<TPR>::threads < 8 ? 2048 / RowCTA<TPR>::threads : 8)
-                                  : (ATTN && RowCTA<TPR>::threads <= 256) ? GBX_ATTN_SM_MIN_CTAS : 1)
+                                  : RowCTA<TPR>::threads > 256 ? 1 : ATTN ? GBX_ATTN_SM_MIN_CTAS : GBX_SM_MIN_CTAS)
 softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep)
 {
     grid_dependency_wait();   // see launch_row_kernel

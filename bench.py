@@ -299,20 +299,27 @@ def cpu_sample_tokens(shape, cores, target_s):
     return max(1, min(n, shape.tokens, cap))
 
 
-def cpu_baseline(shape, target_s=12.0):
+def cpu_baseline(shape, target_s=12.0, single_s=2.0):
     """The reference loops on all host cores: one bounded token sample run
-    through the whole chain (every layer), about target_s of CPU work."""
+    through the whole chain (every layer), about target_s of CPU work; and
+    the same loops on one thread, on a sample of about single_s."""
     import oracle
     cores = oracle.max_threads()
     n_tok = cpu_sample_tokens(shape, cores, target_s / 2)
     sample = CpuChainSample(shape, n_tok, seed=1)
     sample.run(cores, layers=1)              # first touch of the sample's pages
     spent = sample.run(cores)
+    n_one = cpu_sample_tokens(shape, 1, single_s)
+    one = CpuChainSample(shape, n_one, seed=4)
+    one.run(1, layers=1)
+    spent_one = one.run(1)
     return {"value": n_tok / spent, "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{n_tok} tokens through embed + all {shape.layers} layers of the chain (residual+LN, their "
                       f"{shape.heads} softmax rows of length {shape.L} each, residual+LN, bias+GELU) + final LN; "
                       f"oracle C restatement of the reference loops, gcc -O3, {cores} threads",
-            "seconds": round(spent, 2)}
+            "seconds": round(spent, 2), "nproc": os.cpu_count(),
+            "single_thread": {"value": n_one / spent_one, "unit": "tokens/s", "cores": 1,
+                              "sample": f"{n_one} tokens, the same chain", "seconds": round(spent_one, 2)}}
 
 
 # ---------------------------------------------------------------------------

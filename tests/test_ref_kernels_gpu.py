@@ -21,7 +21,9 @@ exported by oracle/ref_shim.cu) and launched with its own launch shapes:
 
 Shapes: configuration 0 in full; one whole sequence of configurations 1, 2
 and 4; the decode batch of configuration 3 (256 rows, 6400 softmax rows of
-2048).  The bar is the parity contract: embed and the residual sum bit for
+2048).  Special and extreme values (NaN, +-inf, rows of the -1e9 mask value,
++-1e30, subnormals, +-0, constant rows, overflowing variances) go through
+both sides at the configurations' widths as well.  The bar is the parity contract: embed and the residual sum bit for
 bit, everything else |a-b| <= 1e-6 + 1e-5|b| (b the reference's value),
 compared on the device."""
 import numpy as np
@@ -223,3 +225,97 @@ def test_embed_layernorm_vs_reference_kernels(gbx, R, orc, cuda, cfg):
     torch.cuda.synchronize()
     assert_bits_equal_dev(h, h_ref, what=f"{name}: fused embed h")
     assert_close_dev(y, y_ref, what=f"{name}: fused embed + LayerNorm")
+
+
+def _special_rows(n_cols, g, dev, for_layernorm=False):
+    """Rows of special and extreme fp32 values (one case per row) followed by
+    ordinary rows: NaN, +-inf, all -inf, the reference's -1e9 mask value on
+    every entry, +-1e30, +-88 (the ends of expf), subnormals, +-0, a constant
+    row and +-1e20.  For a LayerNorm, rows 4-6 stay ordinary: a row of
+    -1e9 / 1e30 entries has a mean whose last bits depend on the order of
+    the sum, and x - mean then cancels to a few significant bits in either
+    kernel (ill-conditioned, not a parity case)."""
+    import torch
+    base = torch.randn((16, n_cols), generator=g, dtype=torch.float32, device=dev)
+    base[0, 3] = float("nan")
+    base[1, 5] = float("inf")
+    base[2, 7] = float("-inf")
+    base[3, :] = float("-inf")
+    if not for_layernorm:
+        base[4, :] = -1e9
+        base[5, :] = -1e9
+        base[5, n_cols // 2] = 0.5
+        base[6, 0], base[6, 1:] = 1e30, -1e30
+    base[7, ::2], base[7, 1::2] = 88.0, -88.0
+    base[8, :] = 1e-40 * torch.sign(base[8, :])
+    base[9, :] = 0.0
+    base[9, 1::2] = -0.0
+    base[10, :] = 3.25
+    base[11, :] = 1e20 * torch.sign(base[11, :])
+    return base
+
+
+@pytest.mark.parametrize("d", [768, 1600])
+def test_layernorm_specials_vs_reference_kernel(gbx, R, cuda, d):
+    """NaN / inf / overflowing-variance / constant / subnormal rows through
+    layerNormKernel and gbx_layernorm / gbx_residual_layernorm on the same
+    buffers: the same NaN and inf positions, finite values within tolerance,
+    the residual sum bit for bit."""
+    import torch
+    g = _gen(11)
+    x = _special_rows(d, g, cuda, for_layernorm=True)
+    r = torch.randn_like(x)
+    r[12, 4] = float("-inf")           # inf + -inf in the residual sum
+    x[12, 4] = float("inf")
+    gam, bet = _ln_params(d, g)
+    rows = x.shape[0]
+    ref = torch.empty_like(x)
+    assert R.ref_launch_layernorm(x.data_ptr(), ref.data_ptr(), gam.data_ptr(), bet.data_ptr(), rows, d, None) == 0
+    y = torch.empty_like(x)
+    gbx.layernorm(x, y, gam, bet, rows=rows, d=d)
+    torch.cuda.synchronize()
+    assert_close_dev(y, ref, what=f"LayerNorm specials d={d}")
+    h_ref = x.clone()
+    assert R.ref_launch_add(h_ref.data_ptr(), r.data_ptr(), rows * d, None) == 0
+    y_ref = torch.empty_like(x)
+    assert R.ref_launch_layernorm(h_ref.data_ptr(), y_ref.data_ptr(), gam.data_ptr(), bet.data_ptr(), rows, d,
+                                  None) == 0
+    h, y2 = torch.empty_like(x), torch.empty_like(x)
+    gbx.residual_layernorm(x, r, h, y2, gam, bet, rows=rows, d=d)
+    torch.cuda.synchronize()
+    assert_bits_equal_dev(h, h_ref, what=f"residual sum specials d={d}")
+    assert_close_dev(y2, y_ref, what=f"residual + LayerNorm specials d={d}")
+
+
+@pytest.mark.parametrize("L", [64, 1024, 2048])
+def test_softmax_specials_vs_reference_kernel(gbx, R, cuda, L):
+    """The special rows through softmaxKernel (one launch over all rows) and
+    gbx_softmax_rows: NaN rows where the reference has them, a row of -1e9
+    (every entry masked) uniform, finite values within tolerance."""
+    import torch
+    x = _special_rows(L, _gen(12), cuda)
+    rows = x.shape[0]
+    ref = x.clone()
+    assert R.ref_launch_softmax(ref.data_ptr(), rows, L, None) == 0
+    got = torch.empty_like(x)
+    gbx.softmax_rows(x, got, rows=rows, L=L)
+    torch.cuda.synchronize()
+    assert_close_dev(got, ref, what=f"softmax specials L={L}")
+
+
+@pytest.mark.parametrize("F", [3072, 6400])
+def test_bias_gelu_specials_vs_reference_kernel(gbx, R, cuda, F):
+    """The special rows plus a sweep through the tanh saturation through
+    geluKernel (on pre + bias) and gbx_bias_gelu."""
+    import torch
+    g = _gen(13)
+    pre = _special_rows(F, g, cuda)
+    pre[13, :] = torch.linspace(-12.0, 12.0, F, device=cuda)
+    bias = 0.02 * torch.randn((F,), generator=g, dtype=torch.float32, device=cuda)
+    rows = pre.shape[0]
+    ref = pre + bias
+    assert R.ref_launch_gelu(ref.data_ptr(), rows * F, None) == 0
+    got = torch.empty_like(pre)
+    gbx.bias_gelu(pre, got, bias, rows=rows, F=F)
+    torch.cuda.synchronize()
+    assert_close_dev(got, ref, what=f"bias + GELU specials F={F}")

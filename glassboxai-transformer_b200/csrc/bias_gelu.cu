@@ -16,9 +16,13 @@ namespace gbx {
 
 constexpr int kGeluU = 4;
 
+// Two elements per packed instruction (gelu_tanh2, add4): bit-identical to
+// the scalar form, and on B200 12% fewer instructions per launch (96.3 M
+// against 109.2 M on 16,384 rows of 6400), so that under the power cap the
+// XL prefill's launch takes 249-250 us in the chain against 276 us.
 __device__ __forceinline__ float4 gelu4(float4 u)
 {
-    return make_float4(gelu_tanh(u.x), gelu_tanh(u.y), gelu_tanh(u.z), gelu_tanh(u.w));
+    return cat2(gelu_tanh2(lo2(u)), gelu_tanh2(hi2(u)));
 }
 
 // blockIdx.x = slab * bands + band.  At most 32 registers (4 CTAs of the
@@ -45,7 +49,7 @@ bias_gelu_vec_kernel(const float* in, float* out, const float* __restrict__ bias
     for (int u = 0; u < kGeluU; ++u) {
         if (r0 + u < rows) {
             float4 x = v[u];
-            if (BIAS) x = make_float4(x.x + b.x, x.y + b.y, x.z + b.z, x.w + b.w);
+            if (BIAS) x = add4(x, b);
             st_stream(out + (r0 + u) * F + 4 * c, gelu4(x));
         }
     }

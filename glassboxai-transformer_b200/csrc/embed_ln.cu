@@ -80,10 +80,8 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
     float4 v[V4];
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
-        const float4 p = decode4_arith<T>(a[k]), q = decode4_arith<T>(b[k]);
-        float4 o = make_float4(p.x + q.x, p.y + q.y, p.z + q.z, p.w + q.w);
-        if constexpr (T == TF16)
-            o = make_float4(__fadd_rn(o.x, 0.0f), __fadd_rn(o.y, 0.0f), __fadd_rn(o.z, 0.0f), __fadd_rn(o.w, 0.0f));
+        float4 o = add4(decode4_arith<T>(a[k]), decode4_arith<T>(b[k]));
+        if constexpr (T == TF16) o = add4(o, make_float4(0.0f, 0.0f, 0.0f, 0.0f));
         v[k] = o;
     }
     if (h_out && valid) {
@@ -104,11 +102,11 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
         if (k * TPR < lim) {
-            const float e0 = v[k].x - mean, e1 = v[k].y - mean, e2 = v[k].z - mean, e3 = v[k].w - mean;
-            qs = fmaf(e0, e0, qs);
-            qs = fmaf(e1, e1, qs);
-            qs = fmaf(e2, e2, qs);
-            qs = fmaf(e3, e3, qs);
+            const float4 dv = sub4s(v[k], mean);
+            qs = fmaf(dv.x, dv.x, qs);
+            qs = fmaf(dv.y, dv.y, qs);
+            qs = fmaf(dv.z, dv.z, qs);
+            qs = fmaf(dv.w, dv.w, qs);
         }
     }
     qs = row_sum<TPR>(qs, red[1]);
@@ -123,12 +121,7 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
         for (int k = 0; k < V4; ++k) {
             if (k * TPR < lim) {
                 const float4 g = ld_param4(grow + 4 * k * TPR), bb = ld_param4(brow + 4 * k * TPR);
-                float4 o;
-                o.x = fmaf((v[k].x - mean) * inv, g.x, bb.x);
-                o.y = fmaf((v[k].y - mean) * inv, g.y, bb.y);
-                o.z = fmaf((v[k].z - mean) * inv, g.z, bb.z);
-                o.w = fmaf((v[k].w - mean) * inv, g.w, bb.w);
-                st_stream(yrow + 4 * k * TPR, o);
+                st_stream(yrow + 4 * k * TPR, ln_affine4(v[k], mean, inv, g, bb));
             }
         }
         return;
@@ -139,11 +132,7 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
         if (k * TPR < lim) {
             const float4 g = gamma ? ld_param4(gamma + 4 * c) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
             const float4 bb = beta ? ld_param4(beta + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            float4 o;
-            o.x = fmaf((v[k].x - mean) * inv, g.x, bb.x);
-            o.y = fmaf((v[k].y - mean) * inv, g.y, bb.y);
-            o.z = fmaf((v[k].z - mean) * inv, g.z, bb.z);
-            o.w = fmaf((v[k].w - mean) * inv, g.w, bb.w);
+            const float4 o = ln_affine4(v[k], mean, inv, g, bb);
             if (y_lo) {
                 float4 hi, lo;
                 split4(o, hi, lo);

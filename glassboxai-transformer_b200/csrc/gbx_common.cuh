@@ -115,6 +115,53 @@ __device__ __forceinline__ void st_stream(float* p, float4 v)
 __device__ __forceinline__ float4 ld_param4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
 // ---------------------------------------------------------------------------
+// Elementwise fp32 on float4s, two lanes per instruction (sm_100's packed
+// FADD2 / FMUL2 / FFMA2 through __fadd2_rn / __fmul2_rn / __ffma2_rn).  Each
+// component is rounded exactly as the scalar __fadd_rn / __fmul_rn /
+// __fmaf_rn rounds it, so these are bit-identical to the scalar expressions
+// they stand for, in half the arithmetic instructions.
+__device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
+__device__ __forceinline__ float4 cat2(float2 a, float2 b) { return make_float4(a.x, a.y, b.x, b.y); }
+__device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
+
+// a + b
+__device__ __forceinline__ float4 add4(float4 a, float4 b)
+{
+    return cat2(__fadd2_rn(lo2(a), lo2(b)), __fadd2_rn(hi2(a), hi2(b)));
+}
+
+// a - s (IEEE a - s is a + (-s) exactly)
+__device__ __forceinline__ float4 sub4s(float4 a, float s)
+{
+    return cat2(__fadd2_rn(lo2(a), splat2(-s)), __fadd2_rn(hi2(a), splat2(-s)));
+}
+
+// a * s
+__device__ __forceinline__ float4 mul4s(float4 a, float s)
+{
+    return cat2(__fmul2_rn(lo2(a), splat2(s)), __fmul2_rn(hi2(a), splat2(s)));
+}
+
+// fmaf(a, b, c) per component
+__device__ __forceinline__ float4 fma4(float4 a, float4 b, float4 c)
+{
+    return cat2(__ffma2_rn(lo2(a), lo2(b), lo2(c)), __ffma2_rn(hi2(a), hi2(b), hi2(c)));
+}
+
+// fmaf(a, s, c) per component
+__device__ __forceinline__ float4 fma4s(float4 a, float s, float4 c)
+{
+    return cat2(__ffma2_rn(lo2(a), splat2(s), lo2(c)), __ffma2_rn(hi2(a), splat2(s), hi2(c)));
+}
+
+// The LayerNorm affine map fmaf((x - mean) * inv, g, b) per component.
+__device__ __forceinline__ float4 ln_affine4(float4 x, float mean, float inv, float4 g, float4 b)
+{
+    return fma4(mul4s(sub4s(x, mean), inv), g, b);
+}
+
+// ---------------------------------------------------------------------------
 // Division by a run-time constant without a hardware divide (Granlund-
 // Montgomery round-up method): for 0 <= n < 2^32 and 1 <= d < 2^31,
 // q = (umulhi(n, m) + n) >> s with s = ceil(log2 d), m = floor(2^32 (2^s - d) / d) + 1.

@@ -17,11 +17,6 @@
 
 namespace gbx {
 
-__device__ __forceinline__ float4 f4add(float4 a, float4 b)
-{
-    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
-}
-
 // y_lo non-null: y and y_lo receive the tf32 pair of the output (tf32.cuh)
 // instead of the fp32 output, for gbx_linear.
 // Resident CTAs per SM the row kernels are compiled for (a register budget of
@@ -73,10 +68,10 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
             const float* const brow = xbias + 4 * lane;
 #pragma unroll
             for (int k = 0; k < V4; ++k)
-                if (k * TPR < lim) v[k] = f4add(v[k], ld_param4(brow + 4 * k * TPR));
+                if (k * TPR < lim) v[k] = add4(v[k], ld_param4(brow + 4 * k * TPR));
         }
 #pragma unroll
-        for (int k = 0; k < V4; ++k) v[k] = f4add(rv[k], v[k]);
+        for (int k = 0; k < V4; ++k) v[k] = add4(rv[k], v[k]);
         if (h_out && valid) {
             float* const hrow = h_out + in_off + 4 * lane;
 #pragma unroll
@@ -95,11 +90,11 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
         if (k * TPR < lim) {
-            const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, e = v[k].w - mean;
-            q = fmaf(a, a, q);
-            q = fmaf(b, b, q);
-            q = fmaf(c, c, q);
-            q = fmaf(e, e, q);
+            const float4 dv = sub4s(v[k], mean);
+            q = fmaf(dv.x, dv.x, q);
+            q = fmaf(dv.y, dv.y, q);
+            q = fmaf(dv.z, dv.z, q);
+            q = fmaf(dv.w, dv.w, q);
         }
     }
     q = row_sum<TPR>(q, red[1]);
@@ -115,12 +110,7 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
         for (int k = 0; k < V4; ++k) {
             if (k * TPR < lim) {
                 const float4 g = ld_param4(grow + 4 * k * TPR), b = ld_param4(brow + 4 * k * TPR);
-                float4 o;
-                o.x = fmaf((v[k].x - mean) * inv, g.x, b.x);
-                o.y = fmaf((v[k].y - mean) * inv, g.y, b.y);
-                o.z = fmaf((v[k].z - mean) * inv, g.z, b.z);
-                o.w = fmaf((v[k].w - mean) * inv, g.w, b.w);
-                st_stream(yrow + 4 * k * TPR, o);
+                st_stream(yrow + 4 * k * TPR, ln_affine4(v[k], mean, inv, g, b));
             }
         }
         return;
@@ -131,11 +121,7 @@ ln_vec_kernel(const float* x, const float* r, const float* __restrict__ xbias, f
         if (k * TPR < lim) {
             const float4 g = gamma ? ld_param4(gamma + 4 * c) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
             const float4 b = beta ? ld_param4(beta + 4 * c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            float4 o;
-            o.x = fmaf((v[k].x - mean) * inv, g.x, b.x);
-            o.y = fmaf((v[k].y - mean) * inv, g.y, b.y);
-            o.z = fmaf((v[k].z - mean) * inv, g.z, b.z);
-            o.w = fmaf((v[k].w - mean) * inv, g.w, b.w);
+            const float4 o = ln_affine4(v[k], mean, inv, g, b);
             if (y_lo) {
                 float4 hi, lo;
                 split4(o, hi, lo);

@@ -33,6 +33,15 @@ __device__ __forceinline__ float div_by(float a, float b, float rb)
     return fmaf(fmaf(-q, b, a), rb, q);
 }
 
+// div_by on four quotients a / b with one reciprocal rb, two per packed
+// instruction: fmaf(-q, b, a) is the same exact value as fmaf(q, -b, a)
+// before its one rounding, so the result is div_by's bit for bit.
+__device__ __forceinline__ float4 div4_by(float4 a, float b, float rb)
+{
+    const float4 q = mul4s(a, rb);
+    return fma4s(fma4s(q, -b, a), rb, q);
+}
+
 // Score epilogue of the attention variant: the query of row p (p = row % S)
 // sees key columns 0 .. p + q_off; later columns hold -1e9f
 // (transformer.cu:220-221), earlier ones raw / scale (:228).
@@ -127,10 +136,8 @@ softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int
             if (ATTN && 4 * c > last) {
                 v[k] = make_float4(e_mask, e_mask, e_mask, e_mask);
             } else {
-                v[k].x = expf(v[k].x - m);
-                v[k].y = expf(v[k].y - m);
-                v[k].z = expf(v[k].z - m);
-                v[k].w = expf(v[k].w - m);
+                const float4 dv = sub4s(v[k], m);
+                v[k] = make_float4(expf(dv.x), expf(dv.y), expf(dv.z), expf(dv.w));
             }
             s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
         }
@@ -145,8 +152,7 @@ softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int
         for (int k = 0; k < V4; ++k) {
             const int c = k * TPR + lane;
             if (c < n4 && (!PAIR_OUT || 4 * c < wend)) {
-                const float4 q = make_float4(div_by(v[k].x, s, r), div_by(v[k].y, s, r), div_by(v[k].z, s, r),
-                                             div_by(v[k].w, s, r));
+                const float4 q = div4_by(v[k], s, r);
                 if constexpr (PAIR_OUT) {
                     float4 hi, lo;
                     split4(q, hi, lo);

@@ -16,14 +16,10 @@ namespace gbx {
 
 constexpr int kGeluU = 4;
 
-// Two elements per packed instruction (gelu_tanh2, add4): bit-identical to
-// the scalar form, and on B200 12% fewer instructions per launch (96.3 M
+// Two elements per packed instruction (gelu4, add4): bit-identical to the
+// scalar form, and on B200 12% fewer instructions per launch (96.3 M
 // against 109.2 M on 16,384 rows of 6400), so that under the power cap the
 // XL prefill's launch takes 249-250 us in the chain against 276 us.
-__device__ __forceinline__ float4 gelu4(float4 u)
-{
-    return cat2(gelu_tanh2(lo2(u)), gelu_tanh2(hi2(u)));
-}
 
 // blockIdx.x = slab * bands + band.  At most 32 registers (4 CTAs of the
 // widest band per SM): the kernel issues a long tanhf per element, and on

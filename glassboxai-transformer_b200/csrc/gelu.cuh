@@ -6,6 +6,8 @@
 //   out = u * (0.5f * (1.0f + tanhf(0.7978845608f * (u + 0.044715f*u*u*u))))
 #pragma once
 
+#include "gbx_common.cuh"
+
 namespace gbx {
 
 __device__ __forceinline__ float gelu_tanh(float u)
@@ -25,6 +27,11 @@ __device__ __forceinline__ float2 gelu_tanh2(float2 u)
     const float2 k = __fmul2_rn(make_float2(0.7978845608f, 0.7978845608f), __ffma2_rn(t, u, u));
     const float2 th = make_float2(tanhf(k.x), tanhf(k.y));
     return __fmul2_rn(u, __fmul2_rn(make_float2(0.5f, 0.5f), __fadd2_rn(make_float2(1.0f, 1.0f), th)));
+}
+
+__device__ __forceinline__ float4 gelu4(float4 u)
+{
+    return cat2(gelu_tanh2(lo2(u)), gelu_tanh2(hi2(u)));
 }
 
 }  // namespace gbx

@@ -186,12 +186,9 @@ __device__ __forceinline__ void epi_store16(const float (&v)[16], int64_t row, i
             if (a.bias || a.resid || a.act) {
                 float4 b = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + n + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
                 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                if (a.bias) o = make_float4(o.x + b.x, o.y + b.y, o.z + b.z, o.w + b.w);
-                if (a.act == GBX_ACT_GELU) o = make_float4(gelu_tanh(o.x), gelu_tanh(o.y), gelu_tanh(o.z), gelu_tanh(o.w));
-                if (a.resid) {
-                    const float4 r = *reinterpret_cast<const float4*>(a.resid + off + n + j);
-                    o = make_float4(r.x + o.x, r.y + o.y, r.z + o.z, r.w + o.w);
-                }
+                if (a.bias) o = add4(o, b);
+                if (a.act == GBX_ACT_GELU) o = gelu4(o);
+                if (a.resid) o = add4(*reinterpret_cast<const float4*>(a.resid + off + n + j), o);
             } else {
                 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
             }
@@ -1134,19 +1131,13 @@ splitk_reduce_kernel(const float* __restrict__ ws, int ksplit, const LinearArgs 
             float4 v = *reinterpret_cast<const float4*>(ws + 4 * i);
             for (int s = 1; s < ksplit; ++s) {
                 const float4 w = *reinterpret_cast<const float4*>(ws + s * MN + 4 * i);
-                v = make_float4(v.x + w.x, v.y + w.y, v.z + w.z, v.w + w.w);
+                v = add4(v, w);
             }
             // the epilogue of epi_store16, on 4 columns (N % 4 == 0: all in one row)
             const int n = (int)((4 * i) % a.N);
-            if (a.bias) {
-                const float4 b = __ldg(reinterpret_cast<const float4*>(a.bias + n));
-                v = make_float4(v.x + b.x, v.y + b.y, v.z + b.z, v.w + b.w);
-            }
-            if (a.act == GBX_ACT_GELU) v = make_float4(gelu_tanh(v.x), gelu_tanh(v.y), gelu_tanh(v.z), gelu_tanh(v.w));
-            if (a.resid) {
-                const float4 r = *reinterpret_cast<const float4*>(a.resid + 4 * i);
-                v = make_float4(r.x + v.x, r.y + v.y, r.z + v.z, r.w + v.w);
-            }
+            if (a.bias) v = add4(v, __ldg(reinterpret_cast<const float4*>(a.bias + n)));
+            if (a.act == GBX_ACT_GELU) v = gelu4(v);
+            if (a.resid) v = add4(*reinterpret_cast<const float4*>(a.resid + 4 * i), v);
             if (a.y_lo) {
                 float4 h, l;
                 split4(v, h, l);

@@ -31,8 +31,15 @@ namespace gbx {
 #define GBX_EMBED_LN_WARP_MIN_CTAS 4
 #endif
 
+// CTAs of 128 threads (rows.cuh): the same time as 256 for the XL prefill's
+// 32,768 tokens (88.4 us), and twice the CTAs for a decode batch.
+constexpr int kElnCTA = 128;
+template <int TPR>
+using ElnCTA = RowCTA<TPR, kElnCTA>;
+
 template <int T, int TPR, int V4>
-__global__ void __launch_bounds__(RowCTA<TPR>::threads, TPR == 32 && V4 > 4 ? GBX_EMBED_LN_WARP_MIN_CTAS : 1)
+__global__ void __launch_bounds__(ElnCTA<TPR>::threads,
+                                  TPR == 32 && V4 > 4 ? ElnCTA<TPR>::per256(GBX_EMBED_LN_WARP_MIN_CTAS) : 1)
 embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, const void* __restrict__ wpe,
                 const int32_t* __restrict__ pos_ids, float* __restrict__ h_out, float* __restrict__ y,
                 float* __restrict__ y_lo, const float* __restrict__ gamma, const float* __restrict__ beta,
@@ -41,10 +48,10 @@ embed_ln_kernel(const int32_t* __restrict__ ids, const void* __restrict__ wte, c
 {
     grid_dependency_wait();   // see launch_row_kernel
     allow_dependents();
-    __shared__ float red[2][RowCTA<TPR>::warps];
+    __shared__ float red[2][ElnCTA<TPR>::warps];
     const int n4 = d >> 2;
     const int lane = threadIdx.x & (TPR - 1);
-    const int64_t t = (int64_t)blockIdx.x * RowCTA<TPR>::rows + threadIdx.x / TPR;
+    const int64_t t = (int64_t)blockIdx.x * ElnCTA<TPR>::rows + threadIdx.x / TPR;
     const bool valid = t < n_tok;
     const int64_t tt = valid ? t : 0;
     const int32_t id = __ldg(ids + tt);
@@ -151,9 +158,9 @@ static int launch_embed_ln_v(const int32_t* ids, const void* wte, const void* wp
                              int seq, int pos_off, int d, int vocab, int n_ctx, float eps, int32_t* err,
                              cudaStream_t s)
 {
-    const int64_t grid = row_grid<TPR>(n_tok);
+    const int64_t grid = row_grid<TPR, kElnCTA>(n_tok);
     if (grid < 0) return GBX_ERANGE;
-    launch_row_kernel(embed_ln_kernel<T, TPR, V4>, dim3((unsigned)grid), dim3(RowCTA<TPR>::threads), 0, s, ids, wte,
+    launch_row_kernel(embed_ln_kernel<T, TPR, V4>, dim3((unsigned)grid), dim3(ElnCTA<TPR>::threads), 0, s, ids, wte,
                       wpe, pos_ids, h_out, y, y_lo, g, b, n_tok, seq, pos_off, d, vocab, n_ctx, eps, err);
     return GBX_OK;
 }

@@ -27,12 +27,16 @@ namespace gbx {
 constexpr int kRowMaxV4 = 4;
 constexpr int kRowMaxTPR = 1024;
 
-// Threads per CTA for a group width: 256, or the group itself when wider.
-template <int TPR>
+// Threads per CTA for a group width: CT (128 or 256, chosen per kernel), or
+// the group itself when wider.
+template <int TPR, int CT = 256>
 struct RowCTA {
-    static constexpr int threads = TPR > 256 ? TPR : 256;
+    static constexpr int threads = TPR > CT ? TPR : CT;
     static constexpr int rows = threads / TPR;
     static constexpr int warps = threads / 32;
+    // a resident-CTA count stated for CTAs of 256 threads, in CTAs of this
+    // size (the same register budget per thread)
+    static constexpr int per256(int ctas) { return ctas * 256 / threads > 0 ? ctas * 256 / threads : 1; }
 };
 
 struct RowShape {
@@ -129,10 +133,22 @@ __device__ __forceinline__ float block_max(float v, float* red)
 
 // Number of CTAs of the full-grid launch for `rows` rows at group width TPR,
 // or -1 when it exceeds the grid limit.
-template <int TPR>
+// CTA size of a row launch.  Measured on B200: a grid of many 256-thread
+// CTAs streams a little better (the XL prefill softmax, 204,800 CTAs: 962
+// against 967 us with 128 threads), while a launch of few CTAs is latency-
+// bound and gains from twice as many half-size ones (the GPT-2 XL decode
+// step 1.224 -> 1.144 ms, the GPT-2 small chain 96.5 -> 93.4 us, graph
+// replay).  Row kernels that take 128 either way (the attention softmax,
+// the plain LayerNorm, the fused embedding) fix it; the others ask here:
+// 128 threads when the 256-thread grid would hold fewer than
+// kSmallGridCTAsPerSM CTAs per SM.
+constexpr int kSmallGridCTAsPerSM = 32;
+bool small_row_grid(int64_t ctas_at_256);   // status.cu
+
+template <int TPR, int CT = 256>
 inline int64_t row_grid(int64_t rows)
 {
-    const int64_t g = (rows + RowCTA<TPR>::rows - 1) / RowCTA<TPR>::rows;
+    const int64_t g = (rows + RowCTA<TPR, CT>::rows - 1) / RowCTA<TPR, CT>::rows;
     return g > 0x7fffffffLL ? -1 : g;
 }
 

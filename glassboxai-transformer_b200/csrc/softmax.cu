@@ -22,6 +22,8 @@
 //
 // Because max is exact and expf is the same CUDA function, every e is
 // bit-identical to the reference's; only the order of the sum differs.
+#include <type_traits>
+
 #include "rows.cuh"
 #include "tf32.cuh"
 
@@ -61,10 +63,10 @@ struct ScoreEpilogue {
 // contraction, whose row tiles are 128 or 256 rows high, never reads them.
 // (PAIR_OUT held to 8 resident CTAs of 256 threads, 32 registers: 6%
 // faster on B200 than its unbounded 48 registers, a few bytes spilled.
-// The attention form without the pair, in CTAs of 256 threads, compiled for
-// GBX_ATTN_SM_MIN_CTAS resident CTAs:
-// at 6 (40 registers, no spill) 1032 us for 819,200 causal rows of 1024,
-// against 1137 us unbounded (47 registers, 5 CTAs) and 1033 us at 8.  The
+// The attention form without the pair is compiled for GBX_ATTN_SM_MIN_CTAS
+// resident CTAs of 256 threads' worth of registers (rows.cuh, per256): at 6
+// (40 registers, no spill) 1032 us for 819,200 causal rows of 1024 in CTAs
+// of 256, against 1137 us unbounded (47 registers) and 1033 us at 8.  The
 // plain softmax is best left free, GBX_SM_MIN_CTAS 1 (40 registers, 6 CTAs):
 // 962 us against 968 us at 8 CTAs (32 registers) on the same rows.)
 #ifndef GBX_ATTN_SM_MIN_CTAS
@@ -73,18 +75,26 @@ struct ScoreEpilogue {
 #ifndef GBX_SM_MIN_CTAS
 #define GBX_SM_MIN_CTAS 1
 #endif
-template <int TPR, int V4, bool ATTN, bool POW2, bool PAIR_OUT>
-__global__ void __launch_bounds__(RowCTA<TPR>::threads,
-                                  PAIR_OUT ? (2048 / RowCTA<TPR>::threads < 8 ? 2048 / RowCTA<TPR>::threads : 8)
-                                  : RowCTA<TPR>::threads > 256 ? 1 : ATTN ? GBX_ATTN_SM_MIN_CTAS : GBX_SM_MIN_CTAS)
+// CT: threads per CTA (rows.cuh).  The attention form runs CTAs of 128:
+// 947-948 against 1042 us for 819,200 causal rows of 1024 in CTAs of 256
+// (its early causal rows finish fast, and smaller CTAs refill the SMs
+// sooner).  The plain form takes 256 for large grids, 128 for small ones.
+template <int TPR, int V4, bool ATTN, bool POW2, bool PAIR_OUT, int CT>
+__global__ void __launch_bounds__(RowCTA<TPR, CT>::threads,
+                                  RowCTA<TPR, CT>::threads > 256
+                                      ? (PAIR_OUT ? 2048 / RowCTA<TPR, CT>::threads : 1)
+                                      : RowCTA<TPR, CT>::per256(PAIR_OUT ? 8
+                                                                : ATTN   ? GBX_ATTN_SM_MIN_CTAS
+                                                                         : GBX_SM_MIN_CTAS))
 softmax_vec_kernel(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep)
 {
     grid_dependency_wait();   // see launch_row_kernel
     allow_dependents();
-    __shared__ float red[2][RowCTA<TPR>::warps];
+    using C = RowCTA<TPR, CT>;
+    __shared__ float red[2][C::warps];
     const int n4 = L >> 2;
     const int lane = threadIdx.x & (TPR - 1);
-    const int64_t row = (int64_t)blockIdx.x * RowCTA<TPR>::rows + threadIdx.x / TPR;
+    const int64_t row = (int64_t)blockIdx.x * C::rows + threadIdx.x / TPR;
     const bool valid = row < rows;
     const int64_t off = row * L;
 
@@ -219,14 +229,25 @@ template <int TPR, int V4, bool ATTN, bool PAIR_OUT>
 static int launch_softmax_vec(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep,
                               cudaStream_t stream)
 {
-    const int64_t grid = row_grid<TPR>(rows);
-    if (grid < 0) return GBX_ERANGE;
-    if (ATTN && is_pow2(ep.scale))
-        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, true, PAIR_OUT>, dim3((unsigned)grid),
-                          dim3(RowCTA<TPR>::threads), 0, stream, in, out, out_lo, rows, L, ep);
-    else
-        launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, false, PAIR_OUT>, dim3((unsigned)grid),
-                          dim3(RowCTA<TPR>::threads), 0, stream, in, out, out_lo, rows, L, ep);
+    const int64_t grid256 = row_grid<TPR, 256>(rows), grid128 = row_grid<TPR, 128>(rows);
+    if (grid256 < 0 || grid128 < 0) return GBX_ERANGE;
+    auto go = [&](auto ct) {
+        constexpr int CT = decltype(ct)::value;
+        const dim3 grid((unsigned)(CT == 128 ? grid128 : grid256)), block(RowCTA<TPR, CT>::threads);
+        if (ATTN && is_pow2(ep.scale))
+            launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, true, PAIR_OUT, CT>, grid, block, 0, stream, in, out,
+                              out_lo, rows, L, ep);
+        else
+            launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, false, PAIR_OUT, CT>, grid, block, 0, stream, in, out,
+                              out_lo, rows, L, ep);
+    };
+    if constexpr (ATTN) {
+        go(std::integral_constant<int, 128>());
+    } else if (small_row_grid(grid256)) {
+        go(std::integral_constant<int, 128>());
+    } else {
+        go(std::integral_constant<int, 256>());
+    }
     return GBX_OK;
 }
 

@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "gbx_common.cuh"
+#include "rows.cuh"
 
 namespace gbx {
 
@@ -50,6 +51,12 @@ int device_info(DeviceInfo* out)
     if (g_info[dev].sm_count <= 0) return set_error(GBX_ECUDA, "could not query device %d", dev);
     *out = g_info[dev];
     return GBX_OK;
+}
+
+bool small_row_grid(int64_t ctas_at_256)
+{
+    DeviceInfo di;
+    return device_info(&di) == GBX_OK && ctas_at_256 < (int64_t)kSmallGridCTAsPerSM * di.sm_count;
 }
 
 static std::atomic<int> g_pdl{0};

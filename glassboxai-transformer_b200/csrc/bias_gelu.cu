@@ -10,11 +10,19 @@
 // reference's nvcc build fuses it, and CUDA's tanhf (no fast-math):
 //   u = in + bias; out = u * (0.5f * (1.0f + tanhf(0.7978845608f * (u + 0.044715f*u*u*u))))
 #include "gbx_common.cuh"
+#include "rows.cuh"
 #include "gelu.cuh"
 
 namespace gbx {
 
+// Rows per thread: kGeluU in large launches, kGeluSmallU in launches of few
+// CTAs (rows.cuh's small-grid rule, counted in 256-thread CTAs), where more
+// CTAs with less work each finish sooner.  Measured on B200 (graph replay):
+// the GPT-2 XL decode step 1.146 ms with 4 rows, 1.135 with 1, 1.113 with 2;
+// the GPT-2 small chain 94-98 us with 4, 88 with 1 or 2; GPT-2 medium
+// (large launches) unchanged.
 constexpr int kGeluU = 4;
+constexpr int kGeluSmallU = 2;
 
 // Two elements per packed instruction (gelu4, add4): bit-identical to the
 // scalar form, and on B200 12% fewer instructions per launch (96.3 M
@@ -25,24 +33,24 @@ constexpr int kGeluU = 4;
 // widest band per SM): the kernel issues a long tanhf per element, and on
 // B200 it streamed 13% faster with 6 resident 320-thread CTAs per SM than
 // with 3 (56 registers) or 5 (40); no spills at this bound.
-template <bool BIAS>
+template <bool BIAS, int U>
 __global__ void __launch_bounds__(512, 4)
 bias_gelu_vec_kernel(const float* in, float* out, const float* __restrict__ bias, int64_t rows, int n4, int bands)
 {
     grid_dependency_wait();   // see launch_row_kernel
     allow_dependents();
     const int band = (int)(blockIdx.x % (unsigned)bands);
-    const int64_t r0 = (int64_t)(blockIdx.x / (unsigned)bands) * kGeluU;
+    const int64_t r0 = (int64_t)(blockIdx.x / (unsigned)bands) * U;
     const int c = band * blockDim.x + threadIdx.x;
     if (c >= n4) return;
     const int64_t F = 4LL * n4;
     const float4 b = BIAS ? ld_param4(bias + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 v[kGeluU];
+    float4 v[U];
 #pragma unroll
-    for (int u = 0; u < kGeluU; ++u)
+    for (int u = 0; u < U; ++u)
         v[u] = (r0 + u < rows) ? ld_stream(in + (r0 + u) * F + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < kGeluU; ++u) {
+    for (int u = 0; u < U; ++u) {
         if (r0 + u < rows) {
             float4 x = v[u];
             if (BIAS) x = add4(x, b);
@@ -80,10 +88,16 @@ static int launch_gelu_vec(const float* in, float* out, const float* bias, int64
     const int T = gelu_band(n4);
     const int bands = (n4 + T - 1) / T;
     const int64_t grid = (int64_t)bands * ((rows + kGeluU - 1) / kGeluU);
-    if (grid > 0x7fffffffLL)
+    const int64_t grid_small = (int64_t)bands * ((rows + kGeluSmallU - 1) / kGeluSmallU);
+    if (grid_small > 0x7fffffffLL)
         return set_error(GBX_ERANGE, "gbx_bias_gelu: rows=%lld F=%d needs too many CTAs", (long long)rows, 4 * n4);
-    launch_row_kernel(bias_gelu_vec_kernel<BIAS>, dim3((unsigned)grid), dim3(T), 0, stream, in, out, bias, rows, n4,
-                      bands);
+    // a launch of few CTAs (counted in 256-thread equivalents) takes fewer rows per thread
+    if (small_row_grid(grid * T / 256))
+        launch_row_kernel(bias_gelu_vec_kernel<BIAS, kGeluSmallU>, dim3((unsigned)grid_small), dim3(T), 0, stream, in,
+                          out, bias, rows, n4, bands);
+    else
+        launch_row_kernel(bias_gelu_vec_kernel<BIAS, kGeluU>, dim3((unsigned)grid), dim3(T), 0, stream, in, out, bias,
+                          rows, n4, bands);
     return check_launch("gbx_bias_gelu");
 }
 

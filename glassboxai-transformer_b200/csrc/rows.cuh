@@ -7,7 +7,8 @@
 // HBM exactly once.
 //
 // Launch shape: one full grid, each CTA owning RPC = CTA/TPR consecutive rows
-// (no grid-stride loop).  Measured on B200, a full grid of short-lived CTAs
+// (no grid-stride loop; CTAs of 128 or 256 threads, RowCTA and
+// small_row_grid below).  Measured on B200, a full grid of short-lived CTAs
 // streams these rows at 95-106% of the measured copy bandwidth, where a
 // persistent grid of the same kernels reached 87-97%: resident CTAs then
 // work on neighbouring rows, and each SM keeps starting fresh loads while

@@ -78,7 +78,9 @@ struct ScoreEpilogue {
 // CT: threads per CTA (rows.cuh).  The attention form runs CTAs of 128:
 // 947-948 against 1042 us for 819,200 causal rows of 1024 in CTAs of 256
 // (its early causal rows finish fast, and smaller CTAs refill the SMs
-// sooner).  The plain form takes 256 for large grids, 128 for small ones.
+// sooner).  The plain form takes 256 for large grids, 128 for small ones
+// (CTAs of 512 on the XL prefill rows: 961 against 962 us alone, but the XL
+// prefill step then took 73.6-74.0 against 69.9 ms).
 template <int TPR, int V4, bool ATTN, bool POW2, bool PAIR_OUT, int CT>
 __global__ void __launch_bounds__(RowCTA<TPR, CT>::threads,
                                   RowCTA<TPR, CT>::threads > 256
@@ -233,7 +235,7 @@ static int launch_softmax_vec(const float* in, float* out, float* out_lo, int64_
     if (grid256 < 0 || grid128 < 0) return GBX_ERANGE;
     auto go = [&](auto ct) {
         constexpr int CT = decltype(ct)::value;
-        const dim3 grid((unsigned)(CT == 128 ? grid128 : grid256)), block(RowCTA<TPR, CT>::threads);
+        const dim3 grid((unsigned)row_grid<TPR, CT>(rows)), block(RowCTA<TPR, CT>::threads);
         if (ATTN && is_pow2(ep.scale))
             launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, true, PAIR_OUT, CT>, grid, block, 0, stream, in, out,
                               out_lo, rows, L, ep);

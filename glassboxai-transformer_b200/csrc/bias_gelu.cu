@@ -21,6 +21,8 @@ namespace gbx {
 // the GPT-2 XL decode step 1.146 ms with 4 rows, 1.135 with 1, 1.113 with 2;
 // the GPT-2 small chain 94-98 us with 4, 88 with 1 or 2; GPT-2 medium
 // (large launches) unchanged.
+// (large launches, XL prefill 32,768 x 6400: 248-250 us with 4 rows, 256 with
+// 2, 291 with 8 (spills at the 32-register budget).)
 constexpr int kGeluU = 4;
 constexpr int kGeluSmallU = 2;
 

@@ -90,15 +90,16 @@ static int launch_gelu_vec(const float* in, float* out, const float* bias, int64
     const int T = gelu_band(n4);
     const int bands = (n4 + T - 1) / T;
     const int64_t grid = (int64_t)bands * ((rows + kGeluU - 1) / kGeluU);
-    const int64_t grid_small = (int64_t)bands * ((rows + kGeluSmallU - 1) / kGeluSmallU);
-    if (grid_small > 0x7fffffffLL)
-        return set_error(GBX_ERANGE, "gbx_bias_gelu: rows=%lld F=%d needs too many CTAs", (long long)rows, 4 * n4);
     // a launch of few CTAs (counted in 256-thread equivalents) takes fewer rows per thread
-    if (small_row_grid(grid * T / 256))
-        launch_row_kernel(bias_gelu_vec_kernel<BIAS, kGeluSmallU>, dim3((unsigned)grid_small), dim3(T), 0, stream, in,
-                          out, bias, rows, n4, bands);
+    const bool small = small_row_grid(grid * T / 256);
+    const int64_t g = small ? (int64_t)bands * ((rows + kGeluSmallU - 1) / kGeluSmallU) : grid;
+    if (g > 0x7fffffffLL)
+        return set_error(GBX_ERANGE, "gbx_bias_gelu: rows=%lld F=%d needs too many CTAs", (long long)rows, 4 * n4);
+    if (small)
+        launch_row_kernel(bias_gelu_vec_kernel<BIAS, kGeluSmallU>, dim3((unsigned)g), dim3(T), 0, stream, in, out,
+                          bias, rows, n4, bands);
     else
-        launch_row_kernel(bias_gelu_vec_kernel<BIAS, kGeluU>, dim3((unsigned)grid), dim3(T), 0, stream, in, out, bias,
+        launch_row_kernel(bias_gelu_vec_kernel<BIAS, kGeluU>, dim3((unsigned)g), dim3(T), 0, stream, in, out, bias,
                           rows, n4, bands);
     return check_launch("gbx_bias_gelu");
 }

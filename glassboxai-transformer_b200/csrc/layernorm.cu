@@ -198,17 +198,19 @@ static int launch_ln_vec(const float* x, const float* r, const float* xbias, flo
                          const float* g, const float* b, int64_t rows, int d, int64_t ld, float eps,
                          cudaStream_t stream)
 {
-    const int64_t grid256 = row_grid<TPR, 256>(rows), grid128 = row_grid<TPR, 128>(rows);
-    if (grid256 < 0 || grid128 < 0) return GBX_ERANGE;
-    auto small = [&] {
+    const int64_t grid256 = row_grid<TPR, 256>(rows);
+    auto small = [&]() -> int {
+        const int64_t grid128 = row_grid<TPR, 128>(rows);
+        if (grid128 < 0) return GBX_ERANGE;
         launch_row_kernel(ln_vec_kernel<TPR, V4, RESID, 128>, dim3((unsigned)grid128), dim3(RowCTA<TPR, 128>::threads),
                           0, stream, x, r, xbias, h_out, y, y_lo, g, b, rows, d, ld, eps);
+        return GBX_OK;
     };
     if constexpr (!RESID) {
-        small();
-    } else if (small_row_grid(grid256)) {
-        small();
+        return small();
     } else {
+        if (grid256 >= 0 && small_row_grid(grid256)) return small();
+        if (grid256 < 0) return GBX_ERANGE;
         launch_row_kernel(ln_vec_kernel<TPR, V4, RESID, 256>, dim3((unsigned)grid256), dim3(RowCTA<TPR, 256>::threads),
                           0, stream, x, r, xbias, h_out, y, y_lo, g, b, rows, d, ld, eps);
     }

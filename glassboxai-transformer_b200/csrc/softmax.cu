@@ -231,26 +231,26 @@ template <int TPR, int V4, bool ATTN, bool PAIR_OUT>
 static int launch_softmax_vec(const float* in, float* out, float* out_lo, int64_t rows, int L, ScoreEpilogue ep,
                               cudaStream_t stream)
 {
-    const int64_t grid256 = row_grid<TPR, 256>(rows), grid128 = row_grid<TPR, 128>(rows);
-    if (grid256 < 0 || grid128 < 0) return GBX_ERANGE;
-    auto go = [&](auto ct) {
+    const int64_t grid256 = row_grid<TPR, 256>(rows);
+    auto go = [&](auto ct) -> int {
         constexpr int CT = decltype(ct)::value;
-        const dim3 grid((unsigned)row_grid<TPR, CT>(rows)), block(RowCTA<TPR, CT>::threads);
+        const int64_t g = row_grid<TPR, CT>(rows);
+        if (g < 0) return GBX_ERANGE;
+        const dim3 grid((unsigned)g), block(RowCTA<TPR, CT>::threads);
         if (ATTN && is_pow2(ep.scale))
             launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, true, PAIR_OUT, CT>, grid, block, 0, stream, in, out,
                               out_lo, rows, L, ep);
         else
             launch_row_kernel(softmax_vec_kernel<TPR, V4, ATTN, false, PAIR_OUT, CT>, grid, block, 0, stream, in, out,
                               out_lo, rows, L, ep);
+        return GBX_OK;
     };
-    if constexpr (ATTN) {
-        go(std::integral_constant<int, 128>());
-    } else if (small_row_grid(grid256)) {
-        go(std::integral_constant<int, 128>());
-    } else {
-        go(std::integral_constant<int, 256>());
-    }
-    return GBX_OK;
+    if constexpr (ATTN)
+        return go(std::integral_constant<int, 128>());
+    else if (grid256 >= 0 && small_row_grid(grid256))
+        return go(std::integral_constant<int, 128>());
+    else
+        return go(std::integral_constant<int, 256>());
 }
 
 template <bool ATTN, bool PAIR_OUT>
